@@ -1,0 +1,613 @@
+// C ABI of the operator layer (include/dav2cuda.h). Each entry validates its
+// sizes the way src/operators.cpp does before dispatching (there:
+// require_bytes / std::invalid_argument; here: DAV2CUDA_INVALID_ARGUMENT),
+// then launches the sm_100a kernels asynchronously on the caller's stream.
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "kernels.cuh"
+
+namespace dav2cuda {
+
+namespace {
+thread_local std::string t_last_error;
+std::atomic<uint64_t> g_launches{0};
+__device__ int g_device_error = 0;
+int* g_error_word[64] = {};
+}  // namespace
+
+int* device_error_word() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!g_error_word[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+        g_error_word[dev] = static_cast<int*>(p);
+    }
+    return g_error_word[dev];
+}
+
+int set_error(int status, const char* message) {
+    t_last_error = message ? message : "";
+    return status;
+}
+
+int check_launch(const char* what) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        char msg[256];
+        snprintf(msg, sizeof msg, "%s: %s", what, cudaGetErrorString(e));
+        return set_error(DAV2CUDA_LAUNCH_FAILED, msg);
+    }
+    return DAV2CUDA_OK;
+}
+
+namespace {
+
+__global__ void pad_byte_rows_kernel(uint8_t* __restrict__ out, const uint8_t* __restrict__ in, uint64_t rows,
+                                     uint32_t in_bytes, uint32_t out_bytes) {
+    const uint64_t n = rows * out_bytes;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint64_t r = i / out_bytes;
+        const uint32_t c = (uint32_t)(i % out_bytes);
+        out[i] = c < in_bytes ? in[r * in_bytes + c] : 0;
+    }
+}
+
+__global__ void f16_to_f32_kernel(float* __restrict__ out, const __half* __restrict__ in, uint64_t n) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        out[i] = __half2float(in[i]);
+}
+
+int pad_byte_rows(uint8_t* out, const void* in, uint64_t rows, uint32_t in_bytes, uint32_t out_bytes,
+                  cudaStream_t st) {
+    const uint64_t n = rows * out_bytes;
+    const unsigned grid = (unsigned)std::min<uint64_t>((n + 255) / 256 + 1, 148 * 16);
+    pad_byte_rows_kernel<<<grid, 256, 0, st>>>(out, static_cast<const uint8_t*>(in), rows, in_bytes, out_bytes);
+    return check_launch("pad_byte_rows");
+}
+
+constexpr uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+constexpr uint32_t round_up(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
+
+// Bump allocator over a caller workspace.
+struct Carve {
+    uint8_t* base;
+    uint64_t size, used = 0;
+    Carve(void* b, uint64_t s) : base(static_cast<uint8_t*>(b)), size(s) {}
+    template <typename T>
+    T* take(uint64_t bytes) {
+        const uint64_t at = align256(used);
+        used = at + bytes;
+        return reinterpret_cast<T*>(base + at);
+    }
+    bool ok() const { return used <= size; }
+};
+
+bool null_any() { return false; }
+template <typename P, typename... R>
+bool null_any(P p, R... rest) {
+    return p == nullptr || null_any(rest...);
+}
+
+}  // namespace
+}  // namespace dav2cuda
+
+using namespace dav2cuda;
+
+#define REQUIRE(cond, msg) \
+    do {                   \
+        if (!(cond)) return set_error(DAV2CUDA_INVALID_ARGUMENT, msg); \
+    } while (0)
+
+extern "C" {
+
+const char* dav2cuda_last_error(void) { return t_last_error.c_str(); }
+
+const char* dav2cuda_build_info(void) {
+    return "dav2cuda sm_100a: tcgen05 GEMM (TMA, TMEM, kind::f16 / kind::i8), flash attention, "
+           "bandwidth-bound row/elementwise/resample kernels";
+}
+
+int dav2cuda_device_error(void) {
+    cudaDeviceSynchronize();
+    int value = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&value, g_device_error, sizeof(int)) != cudaSuccess) return -1;
+    cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    return value;
+}
+
+uint64_t dav2cuda_launch_count(int reset) {
+    return reset ? g_launches.exchange(0) : g_launches.load();
+}
+
+int dav2cuda_layer_norm(float* output, const float* input, const float* weight, const float* bias, uint32_t rows,
+                        uint32_t columns, float epsilon, void* stream) {
+    REQUIRE(rows != 0 && columns != 0 && epsilon > 0.0f, "invalid layer norm parameters");
+    REQUIRE(!null_any(output, input, weight, bias), "layer norm: null buffer");
+    return launch_layer_norm(output, nullptr, input, weight, bias, rows, columns, epsilon, kLnOutF32, 1, 1, 0,
+                             as_stream(stream));
+}
+
+int dav2cuda_gelu(float* output, const float* input, uint64_t count, void* stream) {
+    REQUIRE(count != 0 && !null_any(output, input), "invalid GELU parameters");
+    return launch_gelu(output, input, count, as_stream(stream));
+}
+
+int dav2cuda_softmax_rows(float* output, const float* input, uint64_t rows, uint32_t columns, float scale,
+                          void* stream) {
+    REQUIRE(rows != 0 && columns != 0 && !null_any(output, input), "invalid softmax parameters");
+    return launch_softmax(output, input, rows, columns, scale, as_stream(stream));
+}
+
+int dav2cuda_add_scaled(float* output, const float* residual, const float* addend, const float* scale,
+                        uint64_t count, uint32_t columns, void* stream) {
+    REQUIRE(count != 0 && columns != 0 && count % columns == 0, "invalid add-scaled dimensions");
+    REQUIRE(!null_any(output, residual, addend, scale), "add-scaled: null buffer");
+    return launch_add_scaled(output, residual, addend, scale, count, columns, as_stream(stream));
+}
+
+int dav2cuda_relu(float* output, const float* input, uint64_t count, void* stream) {
+    REQUIRE(!null_any(output, input), "ReLU: null buffer");
+    if (count == 0) return DAV2CUDA_OK;
+    return launch_relu(output, input, count, as_stream(stream));
+}
+
+int dav2cuda_add(float* output, const float* left, const float* right, uint64_t count, void* stream) {
+    REQUIRE(!null_any(output, left, right), "add: null buffer");
+    if (count == 0) return DAV2CUDA_OK;
+    return launch_add(output, left, right, count, as_stream(stream));
+}
+
+int dav2cuda_sigmoid_scale(float* output, const float* input, uint64_t count, float scale, void* stream) {
+    REQUIRE(!null_any(output, input), "sigmoid_scale: null buffer");
+    if (count == 0) return DAV2CUDA_OK;
+    return launch_sigmoid_scale(output, input, count, scale, as_stream(stream));
+}
+
+int dav2cuda_bilinear_align_true(float* output, const float* input, uint32_t iw, uint32_t ih, uint32_t ow,
+                                 uint32_t oh, uint32_t channels, void* stream) {
+    REQUIRE(iw && ih && ow && oh && channels, "invalid bilinear dimensions");
+    REQUIRE(!null_any(output, input), "bilinear: null buffer");
+    return launch_bilinear_align<float, float>(output, input, iw, ih, ow, oh, channels, as_stream(stream));
+}
+
+int dav2cuda_reduce_minmax(const float* input, float* range, uint64_t count, void* stream) {
+    REQUIRE(count != 0, "empty depth reduction");
+    REQUIRE(!null_any(input, range), "reduce_minmax: null buffer");
+    return launch_minmax(input, range, count, as_stream(stream));
+}
+
+int dav2cuda_normalize_relative(float* depth, const float* range, uint64_t count, void* stream) {
+    REQUIRE(count != 0, "empty relative depth");
+    REQUIRE(!null_any(depth, range), "normalize: null buffer");
+    return launch_normalize(depth, range, count, 0.0f, as_stream(stream));
+}
+
+int dav2cuda_normalize_metric(float* depth, const float* range, uint64_t count, float maximum_depth,
+                              void* stream) {
+    REQUIRE(count != 0 && maximum_depth > 0.0f, "invalid metric depth normalization");
+    REQUIRE(!null_any(depth, range), "normalize: null buffer");
+    return launch_normalize(depth, range, count, maximum_depth, as_stream(stream));
+}
+
+int dav2cuda_preprocess_u32(float* output_chw, const uint32_t* pixels, uint32_t sw, uint32_t sh,
+                            uint32_t row_stride_pixels, uint32_t rgba_order, uint32_t dw, uint32_t dh,
+                            void* stream) {
+    REQUIRE(sw && sh && dw && dh && row_stride_pixels >= sw, "invalid preprocessing dimensions");
+    REQUIRE(!null_any(output_chw, pixels), "preprocess: null buffer");
+    return launch_preprocess_u32(output_chw, pixels, sw, sh, row_stride_pixels, rgba_order, dw, dh,
+                                 as_stream(stream));
+}
+
+int dav2cuda_preprocess_bgr8(float* output_chw, const uint8_t* bgr, uint32_t batch, uint32_t sw, uint32_t sh,
+                             uint64_t row_stride, uint64_t image_stride, uint32_t dw, uint32_t dh, void* stream) {
+    REQUIRE(batch && sw && sh && dw && dh && row_stride >= 3ull * sw, "invalid source image");
+    REQUIRE(batch == 1 || image_stride >= row_stride * sh, "invalid image stride");
+    REQUIRE(!null_any(output_chw, bgr), "preprocess: null buffer");
+    return launch_preprocess_bgr8(output_chw, bgr, batch, sw, sh, row_stride, image_stride, dw, dh, 0,
+                                  as_stream(stream));
+}
+
+int dav2cuda_preprocess_bgr8_bilinear(float* output_chw, const uint8_t* bgr, uint32_t batch, uint32_t sw,
+                                      uint32_t sh, uint64_t row_stride, uint64_t image_stride, uint32_t dw,
+                                      uint32_t dh, void* stream) {
+    REQUIRE(batch && sw && sh && dw && dh && row_stride >= 3ull * sw, "invalid source image");
+    REQUIRE(batch == 1 || image_stride >= row_stride * sh, "invalid image stride");
+    REQUIRE(!null_any(output_chw, bgr), "preprocess: null buffer");
+    return launch_preprocess_bgr8(output_chw, bgr, batch, sw, sh, row_stride, image_stride, dw, dh, 1,
+                                  as_stream(stream));
+}
+
+int dav2cuda_quantize_rows_s8(uint32_t* packed, float* scales, const float* input, uint32_t rows,
+                              uint32_t columns, uint64_t input_offset, void* stream) {
+    REQUIRE(rows && columns && columns % 4 == 0, "invalid INT8 row quantization dimensions");
+    REQUIRE(!null_any(packed, scales, input), "quantize: null buffer");
+    return launch_quantize_rows<float>(packed, scales, input, rows, columns, input_offset, rows,
+                                       (uint64_t)rows * columns, columns / 4, as_stream(stream));
+}
+
+int dav2cuda_im2col_quantize_s8(uint32_t* packed, float* scales, const float* input, uint32_t iw, uint32_t ih,
+                                uint32_t ic, uint32_t ow, uint32_t oh, uint32_t kernel, uint32_t stride,
+                                int32_t padding, void* stream) {
+    REQUIRE(iw && ih && ic && ow && oh && kernel && stride && padding >= 0, "invalid im2col dimensions");
+    REQUIRE(!null_any(packed, scales, input), "im2col: null buffer");
+    return launch_im2col_quantize(packed, scales, input, 1, iw, ih, ic, ow, oh, kernel, stride, padding,
+                                  (ic * kernel * kernel + 3) / 4, as_stream(stream));
+}
+
+int dav2cuda_linear_s8_packed(float* output, const uint32_t* packed_input, const uint32_t* packed_weight,
+                              const float* input_scales, const float* weight_scales, const float* bias,
+                              uint32_t rows, uint32_t input_columns, uint32_t output_columns,
+                              uint32_t output_row_offset, uint32_t output_row_stride, uint32_t output_transposed,
+                              uint32_t has_bias, void* stream) {
+    REQUIRE(rows && input_columns && output_columns, "invalid INT8 linear dimensions");
+    REQUIRE(input_columns % 16 == 0, "INT8 linear: input_columns must be a multiple of 16");
+    REQUIRE(!null_any(output, packed_input, packed_weight, input_scales, weight_scales), "INT8 linear: null buffer");
+    REQUIRE(!has_bias || bias, "INT8 linear: null bias");
+    GemmArgs g;
+    g.elem = kElemS8;
+    g.a = packed_input;
+    g.lda = input_columns;
+    g.b = packed_weight;
+    g.ldb = input_columns;
+    g.m = rows;
+    g.n = output_columns;
+    g.k = input_columns;
+    g.flags = kEpiDequant | (has_bias ? kEpiBias : 0u);
+    g.s_in = input_scales;
+    g.s_w = weight_scales;
+    g.bias = bias;
+    g.out = output;
+    if (output_transposed) {
+        g.out_kind = kOutF32Planar;
+        g.img_stride = 0;
+        g.col_stride = output_row_stride;
+        g.row_offset = output_row_offset;
+    } else {
+        g.out_kind = kOutF32Rows;
+        g.ldo = output_columns;
+        g.rows_per_img = rows;
+        g.out_rows_per_img = rows + output_row_offset;
+        g.row_offset = output_row_offset;
+    }
+    return launch_gemm(g, as_stream(stream));
+}
+
+uint64_t dav2cuda_linear_int8_workspace_size(uint32_t rows, uint32_t input_columns, uint32_t output_columns) {
+    const uint32_t kp = round_up(input_columns, 16);
+    return align256((uint64_t)rows * kp) + align256((uint64_t)rows * 4) +
+           (kp != input_columns ? align256((uint64_t)output_columns * kp) : 0) + 256;
+}
+
+int dav2cuda_linear_int8(float* output, const float* input, const uint32_t* int8_weight, const float* weight_scales,
+                         const float* bias, uint32_t rows, uint32_t input_columns, uint32_t output_columns,
+                         uint32_t gelu, void* workspace, uint64_t workspace_bytes, void* stream) {
+    REQUIRE(rows && input_columns && output_columns && input_columns % 4 == 0, "invalid INT8 linear dimensions");
+    REQUIRE(!null_any(output, input, int8_weight, weight_scales, bias, workspace), "INT8 linear: null buffer");
+    REQUIRE(workspace_bytes >= dav2cuda_linear_int8_workspace_size(rows, input_columns, output_columns),
+            "INT8 linear: workspace is too small");
+    cudaStream_t st = as_stream(stream);
+    const uint32_t kp = round_up(input_columns, 16);
+    Carve ws(workspace, workspace_bytes);
+    uint32_t* codes = ws.take<uint32_t>((uint64_t)rows * kp);
+    float* scales = ws.take<float>((uint64_t)rows * 4);
+    const uint32_t* w = int8_weight;
+    if (kp != input_columns) {
+        uint8_t* wp = ws.take<uint8_t>((uint64_t)output_columns * kp);
+        if (int rc = pad_byte_rows(wp, int8_weight, output_columns, input_columns, kp, st)) return rc;
+        w = reinterpret_cast<const uint32_t*>(wp);
+    }
+    if (int rc = launch_quantize_rows<float>(codes, scales, input, rows, input_columns, 0, rows,
+                                             (uint64_t)rows * input_columns, kp / 4, st))
+        return rc;
+    GemmArgs g;
+    g.elem = kElemS8;
+    g.a = codes;
+    g.lda = kp;
+    g.b = w;
+    g.ldb = kp;
+    g.m = rows;
+    g.n = output_columns;
+    g.k = kp;
+    g.flags = kEpiDequant | kEpiBias | (gelu ? kEpiGelu : 0u);
+    g.s_in = scales;
+    g.s_w = weight_scales;
+    g.bias = bias;
+    g.out = output;
+    g.out_kind = kOutF32Rows;
+    g.ldo = output_columns;
+    return launch_gemm(g, st);
+}
+
+uint64_t dav2cuda_conv2d_int8_workspace_size(uint32_t iw, uint32_t ih, uint32_t ic, uint32_t oc, uint32_t k,
+                                             uint32_t s, uint32_t p) {
+    if (!iw || !ih || !k || !s || iw + 2 * p < k || ih + 2 * p < k) return 0;
+    const uint64_t ow = (iw + 2 * p - k) / s + 1, oh = (ih + 2 * p - k) / s + 1;
+    const uint32_t kp = round_up(ic * k * k, 16);
+    return align256(ow * oh * kp) + align256(ow * oh * 4) + align256((uint64_t)oc * kp) + 256;
+}
+
+int dav2cuda_conv2d_int8(float* output, const float* input, const uint32_t* int8_weight, const float* weight_scales,
+                         const float* bias, uint32_t iw, uint32_t ih, uint32_t ic, uint32_t oc, uint32_t k,
+                         uint32_t s, uint32_t p, uint32_t has_bias, void* workspace, uint64_t workspace_bytes,
+                         void* stream) {
+    REQUIRE(iw && ih && ic && oc && k && s && iw + 2 * p >= k && ih + 2 * p >= k,
+            "invalid INT8 convolution dimensions");
+    REQUIRE((ic * k * k) % 4 == 0, "INT8 convolution inner size is not packed");
+    REQUIRE(!null_any(output, input, int8_weight, weight_scales, workspace), "INT8 convolution: null buffer");
+    REQUIRE(!has_bias || bias, "INT8 convolution: null bias");
+    REQUIRE(workspace_bytes >= dav2cuda_conv2d_int8_workspace_size(iw, ih, ic, oc, k, s, p),
+            "INT8 convolution: workspace is too small");
+    cudaStream_t st = as_stream(stream);
+    const uint32_t ow = (iw + 2 * p - k) / s + 1, oh = (ih + 2 * p - k) / s + 1;
+    const uint32_t K = ic * k * k, kp = round_up(K, 16);
+    const uint64_t rows = (uint64_t)ow * oh;
+    Carve ws(workspace, workspace_bytes);
+    uint32_t* codes = ws.take<uint32_t>(rows * kp);
+    float* scales = ws.take<float>(rows * 4);
+    const void* w = int8_weight;
+    if (kp != K) {
+        uint8_t* wp = ws.take<uint8_t>((uint64_t)oc * kp);
+        if (int rc = pad_byte_rows(wp, int8_weight, oc, K, kp, st)) return rc;
+        w = wp;
+    }
+    if (int rc = launch_im2col_quantize(codes, scales, input, 1, iw, ih, ic, ow, oh, k, s, (int)p, kp / 4, st))
+        return rc;
+    GemmArgs g;
+    g.elem = kElemS8;
+    g.a = codes;
+    g.lda = kp;
+    g.b = w;
+    g.ldb = kp;
+    g.m = (uint32_t)rows;
+    g.n = oc;
+    g.k = kp;
+    g.flags = kEpiDequant | (has_bias ? kEpiBias : 0u);
+    g.s_in = scales;
+    g.s_w = weight_scales;
+    g.bias = bias;
+    g.out = output;
+    g.out_kind = kOutF32Planar;
+    g.col_stride = rows;
+    return launch_gemm(g, st);
+}
+
+uint64_t dav2cuda_conv_transpose_int8_workspace_size(uint32_t iw, uint32_t ih, uint32_t ic, uint32_t oc, uint32_t k) {
+    const uint32_t kp = round_up(ic, 16);
+    const uint64_t rows = (uint64_t)iw * ih;
+    return align256(rows * kp) + align256(rows * 4) + align256((uint64_t)k * k * oc * kp) +
+           align256((uint64_t)k * k * oc * 4) + 256;
+}
+
+int dav2cuda_conv_transpose_int8(float* output, const float* input, const uint32_t* int8_weight,
+                                 const float* weight_scales, const float* bias, uint32_t iw, uint32_t ih, uint32_t ic,
+                                 uint32_t oc, uint32_t k, void* workspace, uint64_t workspace_bytes, void* stream) {
+    REQUIRE(iw && ih && ic && oc && k && ic % 4 == 0, "invalid INT8 transposed convolution");
+    REQUIRE(!null_any(output, input, int8_weight, weight_scales, bias, workspace), "INT8 transposed conv: null buffer");
+    REQUIRE(workspace_bytes >= dav2cuda_conv_transpose_int8_workspace_size(iw, ih, ic, oc, k),
+            "INT8 transposed convolution: workspace is too small");
+    cudaStream_t st = as_stream(stream);
+    const uint32_t kp = round_up(ic, 16);
+    const uint64_t rows = (uint64_t)iw * ih;
+    const uint32_t wrows = k * k * oc;
+    Carve ws(workspace, workspace_bytes);
+    uint32_t* codes = ws.take<uint32_t>(rows * kp);
+    float* scales = ws.take<float>(rows * 4);
+    const void* w = int8_weight;
+    if (kp != ic) {
+        uint8_t* wp = ws.take<uint8_t>((uint64_t)wrows * kp);
+        if (int rc = pad_byte_rows(wp, int8_weight, wrows, ic, kp, st)) return rc;
+        w = wp;
+    }
+    // per-pixel channel quantization: im2col with k=1 (src/operators.cpp:1951-1957)
+    if (int rc = launch_im2col_quantize(codes, scales, input, 1, iw, ih, ic, iw, ih, 1, 1, 0, kp / 4, st)) return rc;
+    GemmArgs g;
+    g.elem = kElemS8;
+    g.a = codes;
+    g.lda = kp;
+    g.b = w;
+    g.ldb = kp;
+    g.m = (uint32_t)rows;
+    g.n = wrows;
+    g.k = kp;
+    g.flags = kEpiDequant;
+    g.s_in = scales;
+    g.s_w = weight_scales;
+    g.out = output;
+    g.out_kind = kOutConvTF32;
+    g.convt_k = k;
+    g.convt_cout = oc;
+    g.convt_w = iw;
+    g.convt_h = ih;
+    // bias is per output channel, not per GEMM column: added by the scatter
+    // through a column-expanded bias below.
+    float* bias_cols = ws.take<float>((uint64_t)wrows * 4);
+    if (!ws.ok()) return set_error(DAV2CUDA_INVALID_ARGUMENT, "INT8 transposed convolution: workspace is too small");
+    for (uint32_t t = 0; t < k * k; ++t)
+        if (cudaMemcpyAsync(bias_cols + (uint64_t)t * oc, bias, oc * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+            return set_error(DAV2CUDA_LAUNCH_FAILED, "INT8 transposed convolution: bias copy failed");
+    g.flags |= kEpiBias;
+    g.bias = bias_cols;
+    return launch_gemm(g, st);
+}
+
+uint64_t dav2cuda_conv3x3_int8_up2_workspace_size(uint32_t batch, uint32_t w, uint32_t h, uint32_t ic, uint32_t oc) {
+    const uint32_t kp = round_up(ic * 9, 16);
+    const uint64_t rows = (uint64_t)batch * w * h;
+    return align256(rows * kp) + align256(rows * 4) + align256((uint64_t)oc * kp) +
+           align256((uint64_t)batch * oc * w * h * 4) + 256;
+}
+
+int dav2cuda_conv3x3_int8_up2(float* output, const float* input, const uint32_t* int8_weight,
+                              const float* weight_scales, const float* bias, uint32_t batch, uint32_t w, uint32_t h,
+                              uint32_t ic, uint32_t oc, void* workspace, uint64_t workspace_bytes, void* stream) {
+    REQUIRE(batch && w && h && ic && oc && (ic * 9) % 4 == 0, "invalid INT8 convolution dimensions");
+    REQUIRE(!null_any(output, input, int8_weight, weight_scales, bias, workspace), "conv3x3_int8_up2: null buffer");
+    REQUIRE(workspace_bytes >= dav2cuda_conv3x3_int8_up2_workspace_size(batch, w, h, ic, oc),
+            "conv3x3_int8_up2: workspace is too small");
+    cudaStream_t st = as_stream(stream);
+    const uint32_t K = ic * 9, kp = round_up(K, 16);
+    const uint64_t hw = (uint64_t)w * h, rows = batch * hw;
+    Carve ws(workspace, workspace_bytes);
+    uint32_t* codes = ws.take<uint32_t>(rows * kp);
+    float* scales = ws.take<float>(rows * 4);
+    const void* wt = int8_weight;
+    if (kp != K) {
+        uint8_t* wp = ws.take<uint8_t>((uint64_t)oc * kp);
+        if (int rc = pad_byte_rows(wp, int8_weight, oc, K, kp, st)) return rc;
+        wt = wp;
+    }
+    float* conv = ws.take<float>((uint64_t)batch * oc * hw * 4);
+    if (int rc = launch_im2col_quantize(codes, scales, input, batch, w, h, ic, w, h, 3, 1, 1, kp / 4, st)) return rc;
+    GemmArgs g;
+    g.elem = kElemS8;
+    g.a = codes;
+    g.lda = kp;
+    g.b = wt;
+    g.ldb = kp;
+    g.m = (uint32_t)rows;
+    g.n = oc;
+    g.k = kp;
+    g.flags = kEpiDequant | kEpiBias;
+    g.s_in = scales;
+    g.s_w = weight_scales;
+    g.bias = bias;
+    g.out = conv;
+    g.out_kind = kOutF32Planar;
+    g.rows_per_img = (uint32_t)hw;
+    g.img_stride = (uint64_t)oc * hw;
+    g.col_stride = hw;
+    if (int rc = launch_gemm(g, st)) return rc;
+    return launch_bilinear_align<float, float>(output, conv, w, h, 2 * w, 2 * h, batch * oc, st);
+}
+
+uint64_t dav2cuda_attention_head64_workspace_size(uint32_t batch, uint32_t tokens, uint32_t heads) {
+    const uint64_t e = (uint64_t)heads * 64;
+    return align256((uint64_t)batch * tokens * 3 * e * 2) + align256((uint64_t)batch * tokens * e * 2) + 256;
+}
+
+int dav2cuda_attention_head64(float* output, const float* qkv, uint32_t batch, uint32_t tokens, uint32_t heads,
+                              void* workspace, uint64_t workspace_bytes, void* stream) {
+    REQUIRE(batch && tokens && heads, "invalid attention dimensions");
+    REQUIRE(!null_any(output, qkv, workspace), "attention: null buffer");
+    REQUIRE(workspace_bytes >= dav2cuda_attention_head64_workspace_size(batch, tokens, heads),
+            "attention: workspace is too small");
+    cudaStream_t st = as_stream(stream);
+    const uint64_t e = (uint64_t)heads * 64;
+    Carve ws(workspace, workspace_bytes);
+    __half* q = ws.take<__half>((uint64_t)batch * tokens * 3 * e * 2);
+    __half* o = ws.take<__half>((uint64_t)batch * tokens * e * 2);
+    if (int rc = launch_to_half<__half>(q, qkv, (uint64_t)batch * tokens * 3 * e, st)) return rc;
+    if (int rc = launch_attention<__half>(o, q, batch, tokens, heads, 3 * e, e, st)) return rc;
+    const uint64_t n = (uint64_t)batch * tokens * e;
+    f16_to_f32_kernel<<<(unsigned)std::min<uint64_t>((n + 255) / 256, 148 * 16), 256, 0, st>>>(output, o, n);
+    return check_launch("attention_out");
+}
+
+uint64_t dav2cuda_linear_half_workspace_size(uint32_t rows, uint32_t in_cols, uint32_t out_cols) {
+    const uint32_t kp = round_up(in_cols, 8);
+    return align256((uint64_t)rows * kp * 2) + align256((uint64_t)out_cols * kp * 2) + 256;
+}
+
+int dav2cuda_linear_half(float* output, const float* input, const float* weight, const float* bias, uint32_t rows,
+                         uint32_t in_cols, uint32_t out_cols, uint32_t gelu, uint32_t precision, void* workspace,
+                         uint64_t workspace_bytes, void* stream) {
+    REQUIRE(rows && in_cols && out_cols && (precision == 1 || precision == 2), "invalid linear parameters");
+    REQUIRE(!null_any(output, input, weight, workspace), "linear: null buffer");
+    REQUIRE(workspace_bytes >= dav2cuda_linear_half_workspace_size(rows, in_cols, out_cols),
+            "linear: workspace is too small");
+    cudaStream_t st = as_stream(stream);
+    const uint32_t kp = round_up(in_cols, 8);
+    Carve ws(workspace, workspace_bytes);
+    void* a = ws.take<uint8_t>((uint64_t)rows * kp * 2);
+    void* b = ws.take<uint8_t>((uint64_t)out_cols * kp * 2);
+    const bool bf = precision == 1;
+    int rc = bf ? launch_pad_rows_half<__nv_bfloat16>((__nv_bfloat16*)a, input, rows, in_cols, kp, st)
+                : launch_pad_rows_half<__half>((__half*)a, input, rows, in_cols, kp, st);
+    if (rc) return rc;
+    rc = bf ? launch_pad_rows_half<__nv_bfloat16>((__nv_bfloat16*)b, weight, out_cols, in_cols, kp, st)
+            : launch_pad_rows_half<__half>((__half*)b, weight, out_cols, in_cols, kp, st);
+    if (rc) return rc;
+    GemmArgs g;
+    g.elem = bf ? kElemBF16 : kElemF16;
+    g.a = a;
+    g.lda = kp;
+    g.b = b;
+    g.ldb = kp;
+    g.m = rows;
+    g.n = out_cols;
+    g.k = kp;
+    g.flags = (bias ? kEpiBias : 0u) | (gelu ? kEpiGelu : 0u);
+    g.bias = bias;
+    g.out = output;
+    g.out_kind = kOutF32Rows;
+    g.ldo = out_cols;
+    return launch_gemm(g, st);
+}
+
+uint64_t dav2cuda_conv2d_half_workspace_size(uint32_t iw, uint32_t ih, uint32_t ic, uint32_t oc, uint32_t k,
+                                             uint32_t s, uint32_t p) {
+    if (!iw || !ih || !k || !s || iw + 2 * p < k || ih + 2 * p < k) return 0;
+    const uint64_t ow = (iw + 2 * p - k) / s + 1, oh = (ih + 2 * p - k) / s + 1;
+    const bool implicit = k == 3 && s == 1 && p == 1;
+    const uint32_t cp = implicit ? round_up(ic, 64) : round_up(ic, 8);
+    uint64_t bytes = align256((uint64_t)iw * ih * cp * 2) + align256((uint64_t)oc * k * k * cp * 2) + 256;
+    if (!implicit && k != 1) bytes += align256(ow * oh * (uint64_t)k * k * cp * 2);
+    if (k == 1 && (s != 1 || p != 0)) bytes += align256(ow * oh * (uint64_t)cp * 2);
+    return bytes;
+}
+
+int dav2cuda_conv2d_half(float* output, const float* input, const float* weight, const float* bias, uint32_t iw,
+                         uint32_t ih, uint32_t ic, uint32_t oc, uint32_t k, uint32_t s, uint32_t p, void* workspace,
+                         uint64_t workspace_bytes, void* stream) {
+    REQUIRE(iw && ih && ic && oc && k && s && iw + 2 * p >= k && ih + 2 * p >= k, "invalid convolution dimensions");
+    REQUIRE(!null_any(output, input, weight, workspace), "convolution: null buffer");
+    REQUIRE(workspace_bytes >= dav2cuda_conv2d_half_workspace_size(iw, ih, ic, oc, k, s, p),
+            "convolution: workspace is too small");
+    cudaStream_t st = as_stream(stream);
+    const uint32_t ow = (iw + 2 * p - k) / s + 1, oh = (ih + 2 * p - k) / s + 1;
+    const bool implicit = k == 3 && s == 1 && p == 1;
+    const uint32_t cp = implicit ? round_up(ic, 64) : round_up(ic, 8);
+    Carve ws(workspace, workspace_bytes);
+    __half* x = ws.take<__half>((uint64_t)iw * ih * cp * 2);
+    __half* wt = ws.take<__half>((uint64_t)oc * k * k * cp * 2);
+    if (int rc = launch_nchw_to_nhwc<__half>(x, input, 1, ic, ih, iw, cp, st)) return rc;
+    if (int rc = launch_conv_weight_to_half<__half>(wt, weight, oc, ic, k, cp, st)) return rc;
+    GemmArgs g;
+    g.elem = kElemF16;
+    g.b = wt;
+    g.ldb = (uint64_t)k * k * cp;
+    g.n = oc;
+    g.k = k * k * cp;
+    g.m = ow * oh;
+    g.flags = bias ? kEpiBias : 0u;
+    g.bias = bias;
+    g.out = output;
+    g.out_kind = kOutF32Planar;
+    g.col_stride = (uint64_t)ow * oh;
+    if (implicit) {
+        g.a_mode = kAModeConv3x3;
+        g.a = x;
+        g.conv_batch = 1;
+        g.conv_h = ih;
+        g.conv_w = iw;
+        g.conv_c = cp;
+    } else if (k == 1 && s == 1 && p == 0) {
+        g.a = x;
+        g.lda = cp;
+    } else {
+        __half* col = ws.take<__half>((uint64_t)ow * oh * k * k * cp * 2);
+        if (int rc = launch_im2col_nhwc<__half>(col, x, 1, ih, iw, cp, k, s, p, oh, ow, k * k * cp, st)) return rc;
+        g.a = col;
+        g.lda = (uint64_t)k * k * cp;
+    }
+    return launch_gemm(g, st);
+}
+
+}  // extern "C"

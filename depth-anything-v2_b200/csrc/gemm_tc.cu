@@ -1,0 +1,598 @@
+// Persistent, warp-specialized tcgen05 GEMM for sm_100a.
+//
+//   C[M, N] = A[M, K] . B[N, K]^T   (both operands K-major)
+//
+// A is either a plain row-major matrix (linear layers, 1x1 convolutions,
+// explicit im2col) or a channels-last feature map read as an implicit 3x3
+// (stride 1, pad 1) convolution: for tap (ky, kx) and channel block c0 the
+// A tile of a 16x8-pixel output block is one 4-D TMA box loaded at pixel
+// offset (kx-1, ky-1) — the tensor-memory-access unit zero-fills the halo.
+// B is a K-major weight matrix ([Cout][ky][kx][Cin] for convolutions).
+//
+// Roles per CTA (192 threads, one CTA per SM):
+//   warp 0        TMA producer: fills a STAGES-deep ring of 128-byte-swizzled
+//                 A/B tiles (128 x 128 B and BN x 128 B);
+//   warp 1        TMEM allocator + MMA issuer: 4 tcgen05.mma (K=32 bytes) per
+//                 ring slot into one of two TMEM accumulators (128 lanes x
+//                 BN columns each), tcgen05.commit frees slots / publishes
+//                 accumulators;
+//   warps 2..5    epilogue: tcgen05.ld 32x32b rows out of TMEM, fused
+//                 dequant / bias / GELU / LayerScale-residual / ReLU /
+//                 residual adds / output-head dot, then global stores.
+// The two accumulators let the epilogue of tile i overlap the MMAs of
+// tile i+1. Every wait is bounded (common.cuh: mbar_wait); a timeout sets
+// the device error word and the CTA drains and returns instead of hanging.
+#include "kernels.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <mutex>
+
+namespace dav2cuda {
+namespace {
+
+struct GemmParamsDev {
+    uint32_t m, n, num_kb, num_m_tiles, num_n_tiles;
+    uint32_t a_mode;
+    uint32_t conv_h, conv_w, tiles_x, tiles_y, kb_per_tap;
+    uint32_t flags;
+    int out_kind;
+    int out_bf16;
+    void* out;
+    void* out2;
+    uint64_t ldo;
+    const float* bias;
+    const float* s_in;
+    const float* s_w;
+    const float* gamma;
+    const void* res1;
+    const void* res2;
+    const float* head_w;
+    float head_b, head_max;
+    uint32_t rows_per_img, out_rows_per_img, row_offset;
+    uint64_t img_stride, col_stride;
+    uint32_t ct_k, ct_cout, ct_w, ct_h;
+    int* err;
+};
+
+__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b, bool bf16) {
+    if (bf16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float half_at(const void* p, uint64_t i, bool bf16) {
+    if (bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+    return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+
+template <bool kInt8>
+__device__ __forceinline__ void epilogue_chunk(const GemmParamsDev& p, const uint32_t (&acc)[32], bool valid,
+                                               uint64_t r, uint32_t col0) {
+    if (!valid) return;
+    const uint32_t f = p.flags;
+    const bool full = col0 + 32 <= p.n;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = kInt8 ? (float)(int32_t)acc[j] : __uint_as_float(acc[j]);
+    if (f & kEpiDequant) {
+        const float si = __ldg(p.s_in + r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const float sw = (full || col0 + j < p.n) ? __ldg(p.s_w + col0 + j) : 0.f;
+            v[j] = __fmul_rn(__fmul_rn(v[j], si), sw);
+        }
+    }
+    if (f & kEpiBias) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (full || col0 + j < p.n) v[j] = __fadd_rn(v[j], __ldg(p.bias + col0 + j));
+    }
+    if (f & kEpiGelu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+    }
+
+    // --- output-head dot product (one value per row)
+    if (f & kEpiHeadDot) {
+        float d = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const float a = fmaxf(v[j], 0.0f);
+            if (full || col0 + j < p.n) d = fmaf(a, __ldg(p.head_w + col0 + j), d);
+        }
+        d += p.head_b;
+        d = (f & kEpiMetricHead) ? p.head_max / (1.0f + expf(-d)) : fmaxf(d, 0.0f);
+        uint64_t orow = r;
+        if (p.rows_per_img) orow = (r / p.rows_per_img) * p.out_rows_per_img + p.row_offset + r % p.rows_per_img;
+        reinterpret_cast<float*>(p.out)[orow] = d;
+        return;
+    }
+
+    // --- element addresses
+    if (p.out_kind == kOutF32Rows || p.out_kind == kOutHalfRows) {
+        uint64_t orow = r;
+        if (p.rows_per_img) orow = (r / p.rows_per_img) * p.out_rows_per_img + p.row_offset + r % p.rows_per_img;
+        const uint64_t base = orow * p.ldo + col0;
+        const bool hb = p.out_bf16 != 0;
+        if (p.out_kind == kOutF32Rows) {
+            if (f & (kEpiLayerScale | kEpiResidual1 | kEpiResidual2)) {
+                const float* r1 = reinterpret_cast<const float*>(p.res1);
+                const float* r2 = reinterpret_cast<const float*>(p.res2);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (!(full || col0 + j < p.n)) continue;
+                    if (f & kEpiLayerScale) v[j] = __fadd_rn(r1[base + j], __fmul_rn(v[j], __ldg(p.gamma + col0 + j)));
+                    else if (f & kEpiResidual1) v[j] = v[j] + r1[base + j];
+                    if (f & kEpiResidual2) v[j] = r2[base + j] + v[j];
+                }
+            }
+            if (f & kEpiRelu) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+            }
+            float* o = reinterpret_cast<float*>(p.out) + base;
+            if (full && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+                for (int j = 0; j < 32; ++j)
+                    if (col0 + j < p.n) o[j] = v[j];
+            }
+            if (f & kEpiReluCopy) {
+                float* o2 = reinterpret_cast<float*>(p.out2) + base;
+                for (int j = 0; j < 32; ++j)
+                    if (col0 + j < p.n) o2[j] = fmaxf(v[j], 0.f);
+            }
+        } else {
+            if (f & (kEpiResidual1 | kEpiResidual2)) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (!(full || col0 + j < p.n)) continue;
+                    if (f & kEpiResidual1) v[j] = v[j] + half_at(p.res1, base + j, hb);
+                    if (f & kEpiResidual2) v[j] = half_at(p.res2, base + j, hb) + v[j];
+                }
+            }
+            if (f & kEpiRelu) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+            }
+            uint16_t* o = reinterpret_cast<uint16_t*>(p.out) + base;
+            uint16_t* o2 = (f & kEpiReluCopy) ? reinterpret_cast<uint16_t*>(p.out2) + base : nullptr;
+            if (full && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) {
+                    uint4 w;
+                    w.x = pack_half2(v[j], v[j + 1], hb);
+                    w.y = pack_half2(v[j + 2], v[j + 3], hb);
+                    w.z = pack_half2(v[j + 4], v[j + 5], hb);
+                    w.w = pack_half2(v[j + 6], v[j + 7], hb);
+                    *reinterpret_cast<uint4*>(o + j) = w;
+                    if (o2) {
+                        uint4 z;
+                        z.x = pack_half2(fmaxf(v[j], 0.f), fmaxf(v[j + 1], 0.f), hb);
+                        z.y = pack_half2(fmaxf(v[j + 2], 0.f), fmaxf(v[j + 3], 0.f), hb);
+                        z.z = pack_half2(fmaxf(v[j + 4], 0.f), fmaxf(v[j + 5], 0.f), hb);
+                        z.w = pack_half2(fmaxf(v[j + 6], 0.f), fmaxf(v[j + 7], 0.f), hb);
+                        *reinterpret_cast<uint4*>(o2 + j) = z;
+                    }
+                }
+            } else {
+                for (int j = 0; j < 32; j += 2) {
+                    if (col0 + j >= p.n) break;
+                    const uint32_t w = pack_half2(v[j], v[j + 1], hb);
+                    o[j] = (uint16_t)(w & 0xffff);
+                    if (col0 + j + 1 < p.n) o[j + 1] = (uint16_t)(w >> 16);
+                    if (o2) {
+                        const uint32_t z = pack_half2(fmaxf(v[j], 0.f), fmaxf(v[j + 1], 0.f), hb);
+                        o2[j] = (uint16_t)(z & 0xffff);
+                        if (col0 + j + 1 < p.n) o2[j + 1] = (uint16_t)(z >> 16);
+                    }
+                }
+            }
+        }
+        return;
+    }
+    if (f & kEpiRelu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+    }
+    if (p.out_kind == kOutF32Planar) {
+        uint64_t img = 0, px = r;
+        if (p.rows_per_img) {
+            img = r / p.rows_per_img;
+            px = r % p.rows_per_img;
+        }
+        float* o = reinterpret_cast<float*>(p.out) + img * p.img_stride + p.row_offset + px;
+        for (int j = 0; j < 32; ++j)
+            if (col0 + j < p.n) o[(uint64_t)(col0 + j) * p.col_stride] = v[j];
+        return;
+    }
+    // conv-transpose scatter (kernel == stride)
+    const uint32_t hw = p.ct_w * p.ct_h;
+    const uint64_t img = r / hw;
+    const uint32_t pp = (uint32_t)(r % hw);
+    const uint32_t y = pp / p.ct_w, x = pp % p.ct_w;
+    const uint32_t ow = p.ct_w * p.ct_k, oh = p.ct_h * p.ct_k;
+    for (int j = 0; j < 32; ++j) {
+        const uint32_t col = col0 + j;
+        if (col >= p.n) break;
+        const uint32_t kk = col / p.ct_cout, co = col % p.ct_cout;
+        const uint32_t oy = y * p.ct_k + kk / p.ct_k, ox = x * p.ct_k + kk % p.ct_k;
+        if (p.out_kind == kOutConvTF32) {
+            reinterpret_cast<float*>(p.out)[((img * p.ct_cout + co) * oh + oy) * ow + ox] = v[j];
+        } else {
+            const uint64_t idx = ((img * oh + oy) * ow + ox) * p.ct_cout + co;
+            if (p.out_bf16)
+                reinterpret_cast<__nv_bfloat16*>(p.out)[idx] = __float2bfloat16_rn(v[j]);
+            else
+                reinterpret_cast<__half*>(p.out)[idx] = __float2half_rn(v[j]);
+        }
+    }
+}
+
+template <int BN, int STAGES, int ELEM, int AMODE>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                   const GemmParamsDev p) {
+    constexpr bool kInt8 = ELEM == kElemS8;
+    constexpr uint32_t kABytes = 128u * 128u;
+    constexpr uint32_t kBBytes = (uint32_t)BN * 128u;
+    constexpr uint32_t kTmemCols = 2u * BN < 32u ? 32u : 2u * BN;
+    // f16: A/B format 0; bf16: 1; s8 (signed): 1. D: f32 = 1, s32 = 2.
+    constexpr uint32_t kIdesc = make_idesc(kInt8 ? 2u : 1u, ELEM == kElemF16 ? 0u : 1u, 128u, (uint32_t)BN);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * kABytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * kBBytes);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        tma_prefetch_desc(&tm_a);
+        tma_prefetch_desc(&tm_b);
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&tfull[0], 1);
+        mbar_init(&tfull[1], 1);
+        mbar_init(&tempty[0], 4);
+        mbar_init(&tempty[1], 4);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const uint32_t num_tiles = p.num_m_tiles * p.num_n_tiles;
+    bool mma_issued = false;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0;
+            for (uint32_t tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+                const uint32_t n_blk = tile % p.num_n_tiles;
+                const uint32_t m_blk = tile / p.num_n_tiles;
+                int img = 0, y0 = 0, x0 = 0;
+                if constexpr (AMODE == kAModeConv3x3) {
+                    const uint32_t per_img = p.tiles_x * p.tiles_y;
+                    img = (int)(m_blk / per_img);
+                    const uint32_t rem = m_blk % per_img;
+                    y0 = (int)(rem / p.tiles_x) * 8;
+                    x0 = (int)(rem % p.tiles_x) * 16;
+                }
+                for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) break;
+                    mbar_arrive_expect_tx(&full[stage], kABytes + kBBytes);
+                    const int kcol = (int)(kb * (kInt8 ? 128u : 64u));
+                    if constexpr (AMODE == kAModeRows) {
+                        tma_load_2d(sA + stage * kABytes, &tm_a, &full[stage], kcol, (int)(m_blk * 128u));
+                    } else {
+                        const uint32_t tap = kb / p.kb_per_tap;
+                        const int c0 = (int)((kb % p.kb_per_tap) * (kInt8 ? 128u : 64u));
+                        const int ky = (int)(tap / 3), kx = (int)(tap % 3);
+                        tma_load_4d(sA + stage * kABytes, &tm_a, &full[stage], c0, x0 + kx - 1, y0 + ky - 1, img);
+                    }
+                    tma_load_2d(sB + stage * kBBytes, &tm_b, &full[stage], kcol, (int)(n_blk * (uint32_t)BN));
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, local = 0;
+            for (uint32_t tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++local) {
+                const uint32_t buf = local & 1u;
+                if (!mbar_wait(&tempty[buf], ((local >> 1) & 1u) ^ 1u, abort_flag, p.err)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + buf * (uint32_t)BN;
+                bool ok = true;
+                for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_addr(sA + stage * kABytes);
+                    const uint32_t b_addr = smem_addr(sB + stage * kBBytes);
+#pragma unroll
+                    for (uint32_t j = 0; j < 4; ++j) {
+                        umma<kInt8>(d, smem_desc_sw128(a_addr + 32u * j), smem_desc_sw128(b_addr + 32u * j), kIdesc,
+                                    (kb | j) != 0u ? 1u : 0u);
+                    }
+                    mma_issued = true;
+                    umma_commit(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&tfull[buf]);
+            }
+        }
+    } else {
+        const uint32_t quarter = warp & 3u;
+        const uint32_t row_in_tile = quarter * 32u + lane;
+        uint32_t local = 0;
+        for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+            const uint32_t buf = local & 1u;
+            if (!mbar_wait(&tfull[buf], (local >> 1) & 1u, abort_flag, p.err)) break;
+            tc_fence_after();
+            const uint32_t n_blk = tile % p.num_n_tiles;
+            const uint32_t m_blk = tile / p.num_n_tiles;
+            uint64_t r;
+            bool valid;
+            if constexpr (AMODE == kAModeRows) {
+                r = (uint64_t)m_blk * 128u + row_in_tile;
+                valid = r < p.m;
+            } else {
+                const uint32_t per_img = p.tiles_x * p.tiles_y;
+                const uint32_t img = m_blk / per_img;
+                const uint32_t rem = m_blk % per_img;
+                const uint32_t y = (rem / p.tiles_x) * 8u + row_in_tile / 16u;
+                const uint32_t x = (rem % p.tiles_x) * 16u + row_in_tile % 16u;
+                valid = y < p.conv_h && x < p.conv_w;
+                r = ((uint64_t)img * p.conv_h + y) * p.conv_w + x;
+            }
+            const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + buf * (uint32_t)BN;
+#pragma unroll 1
+            for (uint32_t c = 0; c < (uint32_t)BN; c += 32) {
+                uint32_t acc[32];
+                tmem_ld_32x32b_x32(taddr + c, acc);
+                tmem_ld_wait();
+                const uint32_t col0 = n_blk * (uint32_t)BN + c;
+                if (col0 < p.n) epilogue_chunk<kInt8>(p, acc, valid, r, col0);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+        }
+    }
+
+    __syncthreads();
+    if (*abort_flag) {
+        // Drain: let issued MMAs and in-flight tensor copies finish (bounded)
+        // before the accumulator memory is released.
+        if (warp == 1 && lane == 0 && mma_issued) {
+            umma_commit(drain);
+            const unsigned long long t0 = globaltimer();
+            while (!mbar_try_wait(smem_addr(drain), 0) && globaltimer() - t0 < 100000000ull) {
+            }
+        }
+        if (threadIdx.x == 0) {
+            const unsigned long long t0 = globaltimer();
+            while (globaltimer() - t0 < 2000000ull) {
+            }
+        }
+        __syncthreads();
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool get_encoder() {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    return g_encode != nullptr;
+}
+
+CUtensorMapDataType tm_type(int elem) {
+    switch (elem) {
+        case kElemS8: return CU_TENSOR_MAP_DATA_TYPE_UINT8;
+        case kElemF16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        default: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    }
+}
+
+int make_map(CUtensorMap* map, int elem, int rank, const void* base, const cuuint64_t* dims,
+             const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+    if (!get_encoder()) return set_error(DAV2CUDA_INTERNAL_ERROR, "cuTensorMapEncodeTiled unavailable");
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    const CUresult rc = g_encode(map, tm_type(elem), rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (rc != CUDA_SUCCESS) {
+        char msg[160];
+        snprintf(msg, sizeof msg, "cuTensorMapEncodeTiled failed (%d)", (int)rc);
+        return set_error(DAV2CUDA_INVALID_ARGUMENT, msg);
+    }
+    return DAV2CUDA_OK;
+}
+
+template <int BN>
+constexpr int stages_for() {
+    return BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
+}
+
+template <int BN>
+constexpr size_t smem_for() {
+    return (size_t)stages_for<BN>() * (128 * 128 + BN * 128) + 256 + 1024;
+}
+
+int g_num_sms = 0;
+
+template <int BN, int ELEM, int AMODE>
+int run(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParamsDev& p, int max_ctas, cudaStream_t st) {
+    constexpr int S = stages_for<BN>();
+    constexpr size_t smem = smem_for<BN>();
+    auto kernel = gemm_tc_kernel<BN, S, ELEM, AMODE>;
+    static uint64_t configured = 0;  // one bit per device ordinal
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(configured >> (dev & 63) & 1ull)) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return set_error(DAV2CUDA_LAUNCH_FAILED, "gemm: cannot set shared memory size");
+        configured |= 1ull << (dev & 63);
+    }
+    if (g_num_sms == 0) {
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    const uint32_t tiles = p.num_m_tiles * p.num_n_tiles;
+    uint32_t grid = (uint32_t)(max_ctas > 0 ? max_ctas : g_num_sms);
+    if (grid > tiles) grid = tiles;
+    kernel<<<grid, 192, smem, st>>>(ma, mb, p);
+    return check_launch("gemm_tc");
+}
+
+template <int ELEM, int AMODE>
+int dispatch_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmParamsDev& p, int max_ctas,
+                cudaStream_t st) {
+    switch (bn) {
+        case 256: return run<256, ELEM, AMODE>(ma, mb, p, max_ctas, st);
+        case 128: return run<128, ELEM, AMODE>(ma, mb, p, max_ctas, st);
+        case 64: return run<64, ELEM, AMODE>(ma, mb, p, max_ctas, st);
+        default: return run<32, ELEM, AMODE>(ma, mb, p, max_ctas, st);
+    }
+}
+
+}  // namespace
+
+int launch_gemm(const GemmArgs& g, cudaStream_t st) {
+    if (g.m == 0 || g.n == 0 || g.k == 0) return set_error(DAV2CUDA_INVALID_ARGUMENT, "gemm: empty extent");
+    const uint32_t es = g.elem == kElemS8 ? 1u : 2u;
+    const uint32_t bk = 128u / es;
+    const int bn = g.block_n ? g.block_n : (g.n >= 256 && g.n % 256 == 0 ? 256 : (g.n > 64 ? 128 : (g.n > 32 ? 64 : 32)));
+    if ((g.flags & kEpiHeadDot) && (bn != 32 || g.n > 32))
+        return set_error(DAV2CUDA_INVALID_ARGUMENT, "gemm: head dot needs N <= 32");
+    if (reinterpret_cast<uintptr_t>(g.a) % 16 || reinterpret_cast<uintptr_t>(g.b) % 16)
+        return set_error(DAV2CUDA_INVALID_ARGUMENT, "gemm: operands must be 16-byte aligned");
+    if ((g.ldb * es) % 16) return set_error(DAV2CUDA_INVALID_ARGUMENT, "gemm: weight rows must be 16-byte multiples");
+
+    GemmParamsDev p{};
+    p.m = g.m;
+    p.n = g.n;
+    p.a_mode = (uint32_t)g.a_mode;
+    p.flags = g.flags;
+    p.out_kind = g.out_kind;
+    p.out_bf16 = g.out_half_bf16 ? 1 : 0;
+    p.out = g.out;
+    p.out2 = g.out2;
+    p.ldo = g.ldo;
+    p.bias = g.bias;
+    p.s_in = g.s_in;
+    p.s_w = g.s_w;
+    p.gamma = g.gamma;
+    p.res1 = g.res1;
+    p.res2 = g.res2;
+    p.head_w = g.head_w;
+    p.head_b = g.head_b;
+    p.head_max = g.head_max_depth;
+    p.rows_per_img = g.rows_per_img;
+    p.out_rows_per_img = g.out_rows_per_img;
+    p.row_offset = g.row_offset;
+    p.img_stride = g.img_stride;
+    p.col_stride = g.col_stride;
+    p.ct_k = g.convt_k;
+    p.ct_cout = g.convt_cout;
+    p.ct_w = g.convt_w;
+    p.ct_h = g.convt_h;
+    p.num_n_tiles = (g.n + bn - 1) / bn;
+    p.err = device_error_word();
+    if (!p.err) return set_error(DAV2CUDA_INTERNAL_ERROR, "gemm: no device error word");
+
+    CUtensorMap ma, mb;
+    {
+        const cuuint64_t dims[2] = {g.k, g.n};
+        const cuuint64_t strides[1] = {g.ldb * es};
+        const cuuint32_t box[2] = {bk, (cuuint32_t)bn};
+        if (int rc = make_map(&mb, g.elem, 2, g.b, dims, strides, box)) return rc;
+    }
+    if (g.a_mode == kAModeRows) {
+        if ((g.lda * es) % 16) return set_error(DAV2CUDA_INVALID_ARGUMENT, "gemm: A rows must be 16-byte multiples");
+        const cuuint64_t dims[2] = {g.k, g.m};
+        const cuuint64_t strides[1] = {g.lda * es};
+        const cuuint32_t box[2] = {bk, 128};
+        if (int rc = make_map(&ma, g.elem, 2, g.a, dims, strides, box)) return rc;
+        p.num_m_tiles = (g.m + 127) / 128;
+        p.num_kb = (g.k + bk - 1) / bk;
+    } else {
+        if (g.conv_c % bk) return set_error(DAV2CUDA_INVALID_ARGUMENT, "gemm: conv channels must be a multiple of 128 bytes");
+        if (g.k != 9 * g.conv_c) return set_error(DAV2CUDA_INVALID_ARGUMENT, "gemm: conv K must be 9*C");
+        const cuuint64_t dims[4] = {g.conv_c, g.conv_w, g.conv_h, g.conv_batch};
+        const cuuint64_t strides[3] = {(cuuint64_t)g.conv_c * es, (cuuint64_t)g.conv_c * g.conv_w * es,
+                                       (cuuint64_t)g.conv_c * g.conv_w * g.conv_h * es};
+        const cuuint32_t box[4] = {bk, 16, 8, 1};
+        if (int rc = make_map(&ma, g.elem, 4, g.a, dims, strides, box)) return rc;
+        p.conv_h = g.conv_h;
+        p.conv_w = g.conv_w;
+        p.tiles_x = (g.conv_w + 15) / 16;
+        p.tiles_y = (g.conv_h + 7) / 8;
+        p.kb_per_tap = g.conv_c / bk;
+        p.num_m_tiles = p.tiles_x * p.tiles_y * g.conv_batch;
+        p.num_kb = 9 * p.kb_per_tap;
+        if (g.m != g.conv_batch * g.conv_h * g.conv_w)
+            return set_error(DAV2CUDA_INVALID_ARGUMENT, "gemm: conv M must be batch*H*W");
+    }
+    const int mc = g.max_ctas;
+    if (g.a_mode == kAModeRows) {
+        switch (g.elem) {
+            case kElemS8: return dispatch_bn<kElemS8, kAModeRows>(bn, ma, mb, p, mc, st);
+            case kElemF16: return dispatch_bn<kElemF16, kAModeRows>(bn, ma, mb, p, mc, st);
+            default: return dispatch_bn<kElemBF16, kAModeRows>(bn, ma, mb, p, mc, st);
+        }
+    }
+    switch (g.elem) {
+        case kElemS8: return dispatch_bn<kElemS8, kAModeConv3x3>(bn, ma, mb, p, mc, st);
+        case kElemF16: return dispatch_bn<kElemF16, kAModeConv3x3>(bn, ma, mb, p, mc, st);
+        default: return dispatch_bn<kElemBF16, kAModeConv3x3>(bn, ma, mb, p, mc, st);
+    }
+}
+
+}  // namespace dav2cuda

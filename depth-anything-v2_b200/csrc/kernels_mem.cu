@@ -1,0 +1,756 @@
+// Bandwidth-bound kernels of the operator layer: LayerNorm (plain and fused
+// with row quantization), exact GELU, row softmax, LayerScale/residual adds,
+// align-corners bilinear, min-max normalization, image preprocessing and the
+// int8 row / im2col quantizers. Layouts follow the reference operators
+// (src/operators.cpp); each kernel names the shader whose arithmetic it
+// reproduces.
+#include "kernels.cuh"
+
+#include <cfloat>
+
+namespace dav2cuda {
+
+namespace {
+
+constexpr int kBlock = 256;
+
+__device__ __forceinline__ float gelu_erf(float v) {
+    // torch.nn.GELU (exact erf), which gelu.glsl approximates to ~1.2e-7.
+    return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// ------------------------------------------------------------- LayerNorm
+// layer_norm.glsl:27-67: mean = sum/n; var = max(sumsq/n - mean^2, 0);
+// y = (x - mean) * rsqrt(var + eps) * w + b. One warp per row; the row is
+// held in registers (VPL float4 per lane) so the input is read once.
+// Output row o reads input row (o / out_group) * in_group + in_offset +
+// o % out_group, which lets the encoder taps drop the class-token row.
+// Output kinds: f32, f16 or bf16 values, or int8 codes + per-row scale
+// (the fused form of layer_norm followed by quantize_rows_int8_fused.glsl).
+enum LnOut { kLnF32 = 0, kLnF16 = 1, kLnBF16 = 2, kLnS8 = 3 };
+
+template <int VPL, int OUT>
+__global__ void __launch_bounds__(256) layer_norm_warp_kernel(
+    void* __restrict__ out, float* __restrict__ out_scales, const float* __restrict__ in,
+    const float* __restrict__ w, const float* __restrict__ b, uint32_t rows, uint32_t cols, float eps,
+    uint32_t out_group, uint32_t in_group, uint32_t in_offset) {
+    const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const uint64_t in_row = (uint64_t)(warp / out_group) * in_group + in_offset + warp % out_group;
+    const float4* x4 = reinterpret_cast<const float4*>(in + in_row * cols);
+    const uint32_t n4 = cols >> 2;
+    float4 v[VPL];
+    float s = 0.f, q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const uint32_t c = lane + 32u * i;
+        if (c < n4) {
+            v[i] = __ldg(x4 + c);
+            s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+            q += (v[i].x * v[i].x + v[i].y * v[i].y) + (v[i].z * v[i].z + v[i].w * v[i].w);
+        } else {
+            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    s = warp_sum(s);
+    q = warp_sum(q);
+    const float n = fmaxf((float)cols, 1.0f);
+    const float mean = s / n;
+    const float var = fmaxf(q / n - mean * mean, 0.0f);
+    const float inv = 1.0f / sqrtf(var + eps);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const uint32_t c = lane + 32u * i;
+        if (c < n4) {
+            const float4 ww = __ldg(w4 + c), bb = __ldg(b4 + c);
+            v[i].x = (v[i].x - mean) * inv * ww.x + bb.x;
+            v[i].y = (v[i].y - mean) * inv * ww.y + bb.y;
+            v[i].z = (v[i].z - mean) * inv * ww.z + bb.z;
+            v[i].w = (v[i].w - mean) * inv * ww.w + bb.w;
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+        }
+    }
+    const uint64_t orow = warp;
+    if constexpr (OUT == kLnS8) {
+        amax = warp_max(amax);
+        const float scale = fmaxf(amax / 127.0f, 1.0e-8f);
+        if (lane == 0) out_scales[orow] = scale;
+        uint32_t* o = reinterpret_cast<uint32_t*>(out) + orow * n4;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const uint32_t c = lane + 32u * i;
+            if (c < n4)
+                o[c] = q8(v[i].x / scale) | (q8(v[i].y / scale) << 8) | (q8(v[i].z / scale) << 16) |
+                       (q8(v[i].w / scale) << 24);
+        }
+    } else if constexpr (OUT == kLnF32) {
+        float4* o = reinterpret_cast<float4*>(out) + orow * n4;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const uint32_t c = lane + 32u * i;
+            if (c < n4) o[c] = v[i];
+        }
+    } else {
+        using H = typename std::conditional<OUT == kLnF16, __half, __nv_bfloat16>::type;
+        uint2* o = reinterpret_cast<uint2*>(out) + orow * n4;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const uint32_t c = lane + 32u * i;
+            if (c < n4) {
+                H h[4] = {from_f<H>(v[i].x), from_f<H>(v[i].y), from_f<H>(v[i].z), from_f<H>(v[i].w)};
+                o[c] = *reinterpret_cast<uint2*>(h);
+            }
+        }
+    }
+}
+
+// Generic LayerNorm for column counts the register path does not cover:
+// one 64-thread block per row, lane-strided partial sums exactly as the
+// shader, two reads of the row.
+__global__ void layer_norm_generic_kernel(float* __restrict__ out, const float* __restrict__ in,
+                                          const float* __restrict__ w, const float* __restrict__ b,
+                                          uint32_t cols, float eps) {
+    __shared__ float ps[64], pq[64];
+    const uint64_t row = blockIdx.x;
+    const float* x = in + row * cols;
+    float s = 0.f, q = 0.f;
+    for (uint32_t c = threadIdx.x; c < cols; c += 64) {
+        const float v = x[c];
+        s += v;
+        q += v * v;
+    }
+    ps[threadIdx.x] = s;
+    pq[threadIdx.x] = q;
+    __syncthreads();
+    for (int width = 32; width > 0; width >>= 1) {
+        if ((int)threadIdx.x < width) {
+            ps[threadIdx.x] += ps[threadIdx.x + width];
+            pq[threadIdx.x] += pq[threadIdx.x + width];
+        }
+        __syncthreads();
+    }
+    const float n = fmaxf((float)cols, 1.0f);
+    const float mean = ps[0] / n;
+    const float var = fmaxf(pq[0] / n - mean * mean, 0.0f);
+    const float inv = 1.0f / sqrtf(var + eps);
+    for (uint32_t c = threadIdx.x; c < cols; c += 64) out[row * cols + c] = (x[c] - mean) * inv * w[c] + b[c];
+}
+
+// ------------------------------------------------------------ elementwise
+__global__ void gelu_kernel(float* __restrict__ out, const float* __restrict__ in, uint64_t n) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t n4 = n >> 2;
+    const float4* i4 = reinterpret_cast<const float4*>(in);
+    float4* o4 = reinterpret_cast<float4*>(out);
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        float4 v = __ldcs(i4 + i);
+        v.x = gelu_erf(v.x);
+        v.y = gelu_erf(v.y);
+        v.z = gelu_erf(v.z);
+        v.w = gelu_erf(v.w);
+        __stcs(o4 + i, v);
+    }
+    for (uint64_t i = (n4 << 2) + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        out[i] = gelu_erf(in[i]);
+}
+
+// add_scaled.glsl is declared `precise`: product and sum are rounded
+// separately (no FMA contraction).
+__global__ void add_scaled_kernel(float* __restrict__ out, const float* __restrict__ res,
+                                  const float* __restrict__ add, const float* __restrict__ scale, uint64_t n,
+                                  uint32_t cols) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        out[i] = __fadd_rn(res[i], __fmul_rn(add[i], __ldg(scale + i % cols)));
+}
+
+__global__ void relu_kernel(float* __restrict__ out, const float* __restrict__ in, uint64_t n) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        out[i] = fmaxf(in[i], 0.0f);
+}
+
+__global__ void add_kernel(float* __restrict__ out, const float* __restrict__ a, const float* __restrict__ b,
+                           uint64_t n) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        out[i] = a[i] + b[i];
+}
+
+__global__ void sigmoid_scale_kernel(float* __restrict__ out, const float* __restrict__ in, uint64_t n,
+                                     float s) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        out[i] = s / (1.0f + expf(-in[i]));
+}
+
+// ---------------------------------------------------------------- softmax
+// softmax_lastdim.glsl:19-69 on input*scale: max, exp(v - max), sum,
+// multiply by 1/max(sum, 1e-20). One warp per row, the row kept in
+// registers (MAXV float2 per lane), so each element is read and written
+// exactly once.
+template <int MAXV>
+__global__ void __launch_bounds__(256) softmax_warp_kernel(float* __restrict__ out, const float* __restrict__ in,
+                                                           uint64_t rows, uint32_t cols, float scale) {
+    const uint64_t warp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const float2* x2 = reinterpret_cast<const float2*>(in + warp * cols);
+    float2* y2 = reinterpret_cast<float2*>(out + warp * cols);
+    const uint32_t n2 = cols >> 1;
+    float2 v[MAXV];
+    float m = -FLT_MAX;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const uint32_t c = lane + 32u * i;
+        if (c < n2) {
+            v[i] = __ldcs(x2 + c);
+            v[i].x *= scale;
+            v[i].y *= scale;
+            m = fmaxf(m, fmaxf(v[i].x, v[i].y));
+        }
+    }
+    float tail = 0.f;
+    const bool odd = (cols & 1u) && lane == 0;
+    if (odd) {
+        tail = in[warp * cols + cols - 1] * scale;
+        m = fmaxf(m, tail);
+    }
+    m = warp_max(m);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const uint32_t c = lane + 32u * i;
+        if (c < n2) {
+            v[i].x = expf(v[i].x - m);
+            v[i].y = expf(v[i].y - m);
+            s += v[i].x + v[i].y;
+        }
+    }
+    if (odd) {
+        tail = expf(tail - m);
+        s += tail;
+    }
+    s = warp_sum(s);
+    const float inv = 1.0f / fmaxf(s, 1.0e-20f);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const uint32_t c = lane + 32u * i;
+        if (c < n2) __stcs(y2 + c, make_float2(v[i].x * inv, v[i].y * inv));
+    }
+    if (odd) out[warp * cols + cols - 1] = tail * inv;
+}
+
+// Generic row softmax (any width): one block per row, three passes.
+__global__ void softmax_generic_kernel(float* __restrict__ out, const float* __restrict__ in, uint32_t cols,
+                                       float scale) {
+    __shared__ float red[32];
+    const uint64_t row = blockIdx.x;
+    const float* x = in + row * cols;
+    float* y = out + row * cols;
+    float m = -FLT_MAX;
+    for (uint32_t c = threadIdx.x; c < cols; c += blockDim.x) m = fmaxf(m, x[c] * scale);
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : -FLT_MAX;
+        t = warp_max(t);
+        if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    m = red[0];
+    __syncthreads();
+    float s = 0.f;
+    for (uint32_t c = threadIdx.x; c < cols; c += blockDim.x) {
+        const float e = expf(x[c] * scale - m);
+        y[c] = e;
+        s += e;
+    }
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float inv = 1.0f / fmaxf(red[0], 1.0e-20f);
+    for (uint32_t c = threadIdx.x; c < cols; c += blockDim.x) y[c] *= inv;
+}
+
+// --------------------------------------------------------------- bilinear
+// bilinear_align_true.glsl:27-63: src = (x*(in-1))/(out-1) in f32,
+// x1 = min(x0+1, in-1), top/bottom lerps. Products and sums are rounded
+// separately so the result equals the shader's written order.
+__device__ __forceinline__ void align_coord(uint32_t o, uint32_t in, uint32_t out, uint32_t& i0, uint32_t& i1,
+                                            float& f) {
+    const float s = out > 1 ? __fdiv_rn(__fmul_rn((float)o, (float)(in - 1)), (float)(out - 1)) : 0.0f;
+    i0 = (uint32_t)floorf(s);
+    i1 = min(i0 + 1, in - 1);
+    f = __fsub_rn(s, (float)i0);
+}
+
+__device__ __forceinline__ float lerp_rn(float a, float b, float f) {
+    return __fadd_rn(__fmul_rn(a, __fsub_rn(1.0f, f)), __fmul_rn(b, f));
+}
+
+template <typename TI, typename TO>
+__global__ void bilinear_align_kernel(TO* __restrict__ out, const TI* __restrict__ in, uint32_t iw, uint32_t ih,
+                                      uint32_t ow, uint32_t oh, uint32_t planes) {
+    const uint32_t x = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t y = blockIdx.y;
+    if (x >= ow) return;
+    uint32_t x0, x1, y0, y1;
+    float fx, fy;
+    align_coord(x, iw, ow, x0, x1, fx);
+    align_coord(y, ih, oh, y0, y1, fy);
+    for (uint32_t c = blockIdx.z; c < planes; c += gridDim.z) {
+        const TI* src = in + (uint64_t)c * iw * ih;
+        const float top = lerp_rn(to_f(src[(uint64_t)y0 * iw + x0]), to_f(src[(uint64_t)y0 * iw + x1]), fx);
+        const float bot = lerp_rn(to_f(src[(uint64_t)y1 * iw + x0]), to_f(src[(uint64_t)y1 * iw + x1]), fx);
+        out[((uint64_t)c * oh + y) * ow + x] = from_f<TO>(lerp_rn(top, bot, fy));
+    }
+}
+
+// ---------------------------------------------------------------- min/max
+__device__ __forceinline__ uint32_t order_key(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float order_value(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+__global__ void minmax_init_kernel(uint32_t* keys) {
+    keys[0] = 0xffffffffu;  // +max key
+    keys[1] = 0u;           // -max key
+}
+
+// reduce_minmax.glsl:10-33 as a grid-wide reduction: per-block warp
+// reductions, then order-preserving integer atomics on the two range slots.
+__global__ void minmax_reduce_kernel(uint32_t* keys, const float* __restrict__ in, uint64_t n) {
+    float lo = INFINITY, hi = -INFINITY;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const float v = __ldg(in + i);
+        lo = fminf(lo, v);
+        hi = fmaxf(hi, v);
+    }
+    lo = warp_min(lo);
+    hi = warp_max(hi);
+    if ((threadIdx.x & 31) == 0) {
+        atomicMin(keys, order_key(lo));
+        atomicMax(keys + 1, order_key(hi));
+    }
+}
+
+__global__ void minmax_finish_kernel(uint32_t* keys) {
+    const float lo = order_value(keys[0]);
+    const float hi = order_value(keys[1]);
+    reinterpret_cast<float*>(keys)[0] = lo;
+    reinterpret_cast<float*>(keys)[1] = hi;
+}
+
+// normalize_relative.glsl / normalize_metric.glsl (metric: maximum > 0).
+__global__ void normalize_kernel(float* __restrict__ d, const float* __restrict__ range, uint64_t n,
+                                 float maximum) {
+    const float lo = range[0];
+    const float span = (maximum > 0.0f ? maximum : range[1]) - lo;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        d[i] = span > 1.0e-12f ? fminf(fmaxf((d[i] - lo) / span, 0.0f), 1.0f) : 0.0f;
+}
+
+// -------------------------------------------------------------- preprocess
+__device__ __forceinline__ float cubic_w(int tap, float t) {
+    const float a = -0.75f;
+    float x;
+    switch (tap) {
+        case 0: x = t + 1.0f; return ((a * x - 5.0f * a) * x + 8.0f * a) * x - 4.0f * a;
+        case 1: x = t; return ((a + 2.0f) * x - (a + 3.0f)) * x * x + 1.0f;
+        case 2: x = 1.0f - t; return ((a + 2.0f) * x - (a + 3.0f)) * x * x + 1.0f;
+        default: x = 2.0f - t; return ((a * x - 5.0f * a) * x + 8.0f * a) * x - 4.0f * a;
+    }
+}
+
+__constant__ float c_mean[3] = {0.485f, 0.456f, 0.406f};
+__constant__ float c_dev[3] = {0.229f, 0.224f, 0.225f};
+
+// preprocess_rgba.glsl:53-108 (per output pixel, 16 taps per channel).
+__global__ void preprocess_u32_kernel(float* __restrict__ out, const uint32_t* __restrict__ px, uint32_t sw,
+                                      uint32_t sh, uint32_t stride, uint32_t rgba, uint32_t dw, uint32_t dh) {
+    const uint32_t x = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t y = blockIdx.y;
+    if (x >= dw) return;
+    const float sx = ((float)x + 0.5f) * (float)sw / (float)dw - 0.5f;
+    const float sy = ((float)y + 0.5f) * (float)sh / (float)dh - 0.5f;
+    const int bx = (int)floorf(sx), by = (int)floorf(sy);
+    const float fx = sx - (float)bx, fy = sy - (float)by;
+    const uint64_t plane = (uint64_t)dw * dh;
+    for (int ch = 0; ch < 3; ++ch) {
+        const uint32_t shift = ch == 1 ? 8u : (rgba ? (ch == 0 ? 0u : 16u) : (ch == 0 ? 16u : 0u));
+        float r = 0.0f;
+        for (int ty = 0; ty < 4; ++ty) {
+            const int iy = min(max(by - 1 + ty, 0), (int)sh - 1);
+            float row = 0.0f;
+            for (int tx = 0; tx < 4; ++tx) {
+                const int ix = min(max(bx - 1 + tx, 0), (int)sw - 1);
+                const uint32_t p = __ldg(px + (uint64_t)iy * stride + ix);
+                row += (float)((p >> shift) & 255u) / 255.0f * cubic_w(tx, fx);
+            }
+            r += row * cubic_w(ty, fy);
+        }
+        out[ch * plane + (uint64_t)y * dw + x] = (r - c_mean[ch]) / c_dev[ch];
+    }
+}
+
+// OpenCV-style bicubic of src/image.cpp:163-269 for BGR8 (float
+// coefficients; the reference accumulates in double, here in float: the
+// difference is far below the fp32 operator tolerance).
+__device__ __forceinline__ void cv_coeffs(float x, float c[4]) {
+    const float a = -0.75f;
+    c[0] = ((a * (x + 1.0f) - 5.0f * a) * (x + 1.0f) + 8.0f * a) * (x + 1.0f) - 4.0f * a;
+    c[1] = ((a + 2.0f) * x - (a + 3.0f)) * x * x + 1.0f;
+    const float o = 1.0f - x;
+    c[2] = ((a + 2.0f) * o - (a + 3.0f)) * o * o + 1.0f;
+    c[3] = 1.0f - c[0] - c[1] - c[2];
+}
+
+__global__ void preprocess_bgr8_kernel(float* __restrict__ out, const uint8_t* __restrict__ bgr, uint32_t sw,
+                                       uint32_t sh, uint64_t row_stride, uint64_t img_stride, uint32_t dw,
+                                       uint32_t dh) {
+    const uint32_t x = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t y = blockIdx.y;
+    const uint32_t img = blockIdx.z;
+    if (x >= dw) return;
+    const double scale_x = (double)sw / dw, scale_y = (double)sh / dh;
+    const float cx = (float)((x + 0.5) * scale_x - 0.5);
+    const float cy = (float)((y + 0.5) * scale_y - 0.5);
+    const int bx = (int)floorf(cx), by = (int)floorf(cy);
+    float ax[4], ay[4];
+    cv_coeffs(cx - (float)bx, ax);
+    cv_coeffs(cy - (float)by, ay);
+    const uint8_t* src = bgr + img * img_stride;
+    float acc[3] = {0.f, 0.f, 0.f};
+    for (int ty = 0; ty < 4; ++ty) {
+        const int iy = min(max(by - 1 + ty, 0), (int)sh - 1);
+        const uint8_t* row = src + (uint64_t)iy * row_stride;
+        float h[3] = {0.f, 0.f, 0.f};
+        for (int tx = 0; tx < 4; ++tx) {
+            const int ix = min(max(bx - 1 + tx, 0), (int)sw - 1);
+            const uint8_t* p = row + 3 * ix;
+            h[0] += ((float)__ldg(p + 2) / 255.0f) * ax[tx];
+            h[1] += ((float)__ldg(p + 1) / 255.0f) * ax[tx];
+            h[2] += ((float)__ldg(p + 0) / 255.0f) * ax[tx];
+        }
+        acc[0] += h[0] * ay[ty];
+        acc[1] += h[1] * ay[ty];
+        acc[2] += h[2] * ay[ty];
+    }
+    const uint64_t plane = (uint64_t)dw * dh;
+    float* o = out + (uint64_t)img * 3 * plane + (uint64_t)y * dw + x;
+    for (int ch = 0; ch < 3; ++ch) o[ch * plane] = (acc[ch] - c_mean[ch]) / c_dev[ch];
+}
+
+// Bilinear (align_corners=False) square resize of BGR8 frames.
+__device__ __forceinline__ void hp_coord(uint32_t d, uint32_t in, uint32_t out, uint32_t& i0, uint32_t& i1,
+                                         float& l) {
+    const float scale = (float)in / (float)out;
+    float src = scale * ((float)d + 0.5f) - 0.5f;
+    src = fmaxf(src, 0.0f);
+    uint32_t a = (uint32_t)src;
+    a = min(a, in - 1);
+    i0 = a;
+    i1 = a + (a < in - 1 ? 1u : 0u);
+    l = src - (float)a;
+}
+
+__global__ void preprocess_bgr8_bilinear_kernel(float* __restrict__ out, const uint8_t* __restrict__ bgr,
+                                                uint32_t sw, uint32_t sh, uint64_t row_stride,
+                                                uint64_t img_stride, uint32_t dw, uint32_t dh) {
+    const uint32_t x = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t y = blockIdx.y;
+    const uint32_t img = blockIdx.z;
+    if (x >= dw) return;
+    uint32_t x0, x1, y0, y1;
+    float lx, ly;
+    hp_coord(x, sw, dw, x0, x1, lx);
+    hp_coord(y, sh, dh, y0, y1, ly);
+    const uint8_t* src = bgr + img * img_stride;
+    const uint8_t* r0 = src + (uint64_t)y0 * row_stride;
+    const uint8_t* r1 = src + (uint64_t)y1 * row_stride;
+    const uint64_t plane = (uint64_t)dw * dh;
+    float* o = out + (uint64_t)img * 3 * plane + (uint64_t)y * dw + x;
+    for (int ch = 0; ch < 3; ++ch) {
+        const int b = 2 - ch;
+        const float v00 = __ldg(r0 + 3 * x0 + b) / 255.0f, v01 = __ldg(r0 + 3 * x1 + b) / 255.0f;
+        const float v10 = __ldg(r1 + 3 * x0 + b) / 255.0f, v11 = __ldg(r1 + 3 * x1 + b) / 255.0f;
+        const float top = v00 * (1.0f - lx) + v01 * lx;
+        const float bot = v10 * (1.0f - lx) + v11 * lx;
+        o[ch * plane] = ((top * (1.0f - ly) + bot * ly) - c_mean[ch]) / c_dev[ch];
+    }
+}
+
+// ------------------------------------------------------------ quantizers
+__device__ __forceinline__ float block_max_128(float v, float* red) {
+    v = warp_max(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    const float r = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    return r;
+}
+
+// quantize_rows_int8_fused.glsl:20-55: scale = max(absmax/127, 1e-8);
+// code = rint(clamp(x/scale, -127, 127)). One 128-thread block per row.
+// The input row o starts at input_offset + (o / group) * group_stride +
+// (o % group) * columns, so token matrices can skip their class row.
+template <typename T>
+__global__ void __launch_bounds__(128) quantize_rows_kernel(uint32_t* __restrict__ packed,
+                                                            float* __restrict__ scales,
+                                                            const T* __restrict__ in, uint32_t cols,
+                                                            uint64_t offset, uint32_t group,
+                                                            uint64_t group_stride, uint32_t out_words) {
+    __shared__ float red[4];
+    const uint64_t row = blockIdx.x;
+    const T* x = in + offset + (row / group) * group_stride + (row % group) * (uint64_t)cols;
+    float m = 0.f;
+    for (uint32_t c = threadIdx.x; c < cols; c += 128) m = fmaxf(m, fabsf(to_f(x[c])));
+    m = block_max_128(m, red);
+    const float scale = fmaxf(m / 127.0f, 1.0e-8f);
+    if (threadIdx.x == 0) scales[row] = scale;
+    const uint32_t words = cols >> 2;
+    uint32_t* o = packed + row * out_words;
+    for (uint32_t w = threadIdx.x; w < out_words; w += 128) {
+        uint32_t word = 0;
+        if (w < words) {
+            word = q8(to_f(x[4 * w]) / scale) | (q8(to_f(x[4 * w + 1]) / scale) << 8) |
+                   (q8(to_f(x[4 * w + 2]) / scale) << 16) | (q8(to_f(x[4 * w + 3]) / scale) << 24);
+        }
+        o[w] = word;
+    }
+}
+
+// im2col_quantize_int8.glsl:26-84 on planar [C,H,W] input: row = output
+// pixel, column = c*k*k + ky*k + kx, zero padding; code = rint(clamp(x *
+// (1/scale))). Rows are written out_words words apart (>= ceil(K/4));
+// words past the im2col width are zero.
+__global__ void __launch_bounds__(128) im2col_quantize_kernel(
+    uint32_t* __restrict__ packed, float* __restrict__ scales, const float* __restrict__ in, uint32_t iw,
+    uint32_t ih, uint32_t ic, uint32_t ow, uint32_t oh, uint32_t k, uint32_t s, int pad, uint32_t out_words,
+    uint64_t image_stride, uint64_t rows_per_image) {
+    __shared__ float red[4];
+    const uint64_t row_global = blockIdx.x;
+    const uint64_t img = row_global / rows_per_image;
+    const uint32_t row = (uint32_t)(row_global % rows_per_image);
+    const float* src = in + img * image_stride;
+    const uint32_t ox = row % ow, oy = row / ow;
+    const uint32_t area = k * k;
+    const uint32_t cols = ic * area;
+    auto value = [&](uint32_t c) -> float {
+        const uint32_t ci = c / area, ki = c % area;
+        const int ix = (int)(ox * s + ki % k) - pad;
+        const int iy = (int)(oy * s + ki / k) - pad;
+        if (ix < 0 || iy < 0 || ix >= (int)iw || iy >= (int)ih) return 0.0f;
+        return __ldg(src + ((uint64_t)ci * ih + iy) * iw + ix);
+    };
+    float m = 0.f;
+    for (uint32_t c = threadIdx.x; c < cols; c += 128) m = fmaxf(m, fabsf(value(c)));
+    m = block_max_128(m, red);
+    const float scale = fmaxf(m / 127.0f, 1.0e-8f);
+    if (threadIdx.x == 0) scales[row_global] = scale;
+    const float inv = 1.0f / scale;
+    uint32_t* o = packed + row_global * out_words;
+    for (uint32_t w = threadIdx.x; w < out_words; w += 128) {
+        uint32_t word = 0;
+        for (uint32_t j = 0; j < 4; ++j) {
+            const uint32_t c = 4 * w + j;
+            if (c < cols) word |= q8(__fmul_rn(value(c), inv)) << (8 * j);
+        }
+        o[w] = word;
+    }
+}
+
+}  // namespace
+
+// ============================================================ launchers
+static unsigned grid_for(uint64_t n, unsigned block = kBlock) {
+    const uint64_t g = (n + block - 1) / block;
+    const uint64_t cap = 148ull * 16;
+    return (unsigned)(g < cap ? (g == 0 ? 1 : g) : cap);
+}
+
+int launch_layer_norm(void* out, float* out_scales, const float* in, const float* w, const float* b,
+                      uint32_t rows, uint32_t cols, float eps, int out_kind, uint32_t out_group,
+                      uint32_t in_group, uint32_t in_offset, cudaStream_t st) {
+    const bool vec = (cols % 4 == 0) && cols <= 32 * 4 * 8 && (reinterpret_cast<uintptr_t>(in) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (reinterpret_cast<uintptr_t>(b) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(out) % 16 == 0);
+    if (!vec) {
+        if (out_kind != kLnF32 || out_group != in_group || in_offset != 0)
+            return set_error(DAV2CUDA_INVALID_ARGUMENT, "layer_norm: this output form needs columns % 4 == 0 and <= 1024");
+        layer_norm_generic_kernel<<<rows, 64, 0, st>>>(static_cast<float*>(out), in, w, b, cols, eps);
+        return check_launch("layer_norm_generic");
+    }
+    const unsigned grid = (unsigned)(((uint64_t)rows * 32 + 255) / 256);
+    const int vpl = (int)((cols / 4 + 31) / 32);
+#define LN_CASE(V)                                                                                         \
+    case V:                                                                                                \
+        switch (out_kind) {                                                                                \
+            case kLnF32: layer_norm_warp_kernel<V, kLnF32><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break; \
+            case kLnF16: layer_norm_warp_kernel<V, kLnF16><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break; \
+            case kLnBF16: layer_norm_warp_kernel<V, kLnBF16><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break; \
+            default: layer_norm_warp_kernel<V, kLnS8><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break; \
+        }                                                                                                  \
+        break;
+    switch (vpl) {
+        LN_CASE(1)
+        LN_CASE(2)
+        LN_CASE(3)
+        LN_CASE(4)
+        LN_CASE(6)
+        LN_CASE(8)
+        case 5:
+        case 7:
+            switch (out_kind) {
+                case kLnF32: layer_norm_warp_kernel<8, kLnF32><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break;
+                case kLnF16: layer_norm_warp_kernel<8, kLnF16><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break;
+                case kLnBF16: layer_norm_warp_kernel<8, kLnBF16><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break;
+                default: layer_norm_warp_kernel<8, kLnS8><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break;
+            }
+            break;
+        default: return set_error(DAV2CUDA_INVALID_ARGUMENT, "layer_norm: unsupported width");
+    }
+#undef LN_CASE
+    return check_launch("layer_norm");
+}
+
+int launch_gelu(float* out, const float* in, uint64_t n, cudaStream_t st) {
+    gelu_kernel<<<grid_for((n + 3) / 4), kBlock, 0, st>>>(out, in, n);
+    return check_launch("gelu");
+}
+
+int launch_softmax(float* out, const float* in, uint64_t rows, uint32_t cols, float scale, cudaStream_t st) {
+    const bool aligned = (reinterpret_cast<uintptr_t>(in) % 8 == 0) && (reinterpret_cast<uintptr_t>(out) % 8 == 0) &&
+                         (cols % 2 == 0);
+    const unsigned grid = (unsigned)((rows * 32 + 255) / 256);
+    if (aligned && cols <= 2 * 32 * 24) {
+        softmax_warp_kernel<24><<<grid, 256, 0, st>>>(out, in, rows, cols, scale);
+    } else if (aligned && cols <= 2 * 32 * 48) {
+        softmax_warp_kernel<48><<<grid, 256, 0, st>>>(out, in, rows, cols, scale);
+    } else {
+        softmax_generic_kernel<<<(unsigned)rows, 256, 0, st>>>(out, in, cols, scale);
+    }
+    return check_launch("softmax");
+}
+
+int launch_add_scaled(float* out, const float* res, const float* add, const float* scale, uint64_t n,
+                      uint32_t cols, cudaStream_t st) {
+    add_scaled_kernel<<<grid_for(n), kBlock, 0, st>>>(out, res, add, scale, n, cols);
+    return check_launch("add_scaled");
+}
+
+int launch_relu(float* out, const float* in, uint64_t n, cudaStream_t st) {
+    relu_kernel<<<grid_for(n), kBlock, 0, st>>>(out, in, n);
+    return check_launch("relu");
+}
+
+int launch_add(float* out, const float* a, const float* b, uint64_t n, cudaStream_t st) {
+    add_kernel<<<grid_for(n), kBlock, 0, st>>>(out, a, b, n);
+    return check_launch("add");
+}
+
+int launch_sigmoid_scale(float* out, const float* in, uint64_t n, float s, cudaStream_t st) {
+    sigmoid_scale_kernel<<<grid_for(n), kBlock, 0, st>>>(out, in, n, s);
+    return check_launch("sigmoid_scale");
+}
+
+template <typename TI, typename TO>
+int launch_bilinear_align(TO* out, const TI* in, uint32_t iw, uint32_t ih, uint32_t ow, uint32_t oh,
+                          uint32_t planes, cudaStream_t st) {
+    dim3 grid((ow + 127) / 128, oh, planes < 65535 ? planes : 65535);
+    bilinear_align_kernel<TI, TO><<<grid, 128, 0, st>>>(out, in, iw, ih, ow, oh, planes);
+    return check_launch("bilinear_align_true");
+}
+template int launch_bilinear_align<float, float>(float*, const float*, uint32_t, uint32_t, uint32_t, uint32_t,
+                                                 uint32_t, cudaStream_t);
+
+int launch_minmax(const float* in, float* range, uint64_t n, cudaStream_t st) {
+    uint32_t* keys = reinterpret_cast<uint32_t*>(range);
+    minmax_init_kernel<<<1, 1, 0, st>>>(keys);
+    minmax_reduce_kernel<<<grid_for(n), kBlock, 0, st>>>(keys, in, n);
+    minmax_finish_kernel<<<1, 1, 0, st>>>(keys);
+    return check_launch("reduce_minmax");
+}
+
+int launch_normalize(float* d, const float* range, uint64_t n, float maximum, cudaStream_t st) {
+    normalize_kernel<<<grid_for(n), kBlock, 0, st>>>(d, range, n, maximum);
+    return check_launch("normalize");
+}
+
+int launch_preprocess_u32(float* out, const uint32_t* px, uint32_t sw, uint32_t sh, uint32_t stride,
+                          uint32_t rgba, uint32_t dw, uint32_t dh, cudaStream_t st) {
+    dim3 grid((dw + 127) / 128, dh);
+    preprocess_u32_kernel<<<grid, 128, 0, st>>>(out, px, sw, sh, stride, rgba, dw, dh);
+    return check_launch("preprocess_u32");
+}
+
+int launch_preprocess_bgr8(float* out, const uint8_t* bgr, uint32_t batch, uint32_t sw, uint32_t sh,
+                           uint64_t row_stride, uint64_t img_stride, uint32_t dw, uint32_t dh, int bilinear,
+                           cudaStream_t st) {
+    dim3 grid((dw + 127) / 128, dh, batch);
+    if (bilinear)
+        preprocess_bgr8_bilinear_kernel<<<grid, 128, 0, st>>>(out, bgr, sw, sh, row_stride, img_stride, dw, dh);
+    else
+        preprocess_bgr8_kernel<<<grid, 128, 0, st>>>(out, bgr, sw, sh, row_stride, img_stride, dw, dh);
+    return check_launch("preprocess_bgr8");
+}
+
+template <typename T>
+int launch_quantize_rows(uint32_t* packed, float* scales, const T* in, uint64_t rows, uint32_t cols,
+                         uint64_t offset, uint32_t group, uint64_t group_stride, uint32_t out_words,
+                         cudaStream_t st) {
+    if (rows == 0) return DAV2CUDA_OK;
+    quantize_rows_kernel<T><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, offset, group, group_stride,
+                                                            out_words);
+    return check_launch("quantize_rows");
+}
+template int launch_quantize_rows<float>(uint32_t*, float*, const float*, uint64_t, uint32_t, uint64_t,
+                                         uint32_t, uint64_t, uint32_t, cudaStream_t);
+template int launch_quantize_rows<__half>(uint32_t*, float*, const __half*, uint64_t, uint32_t, uint64_t,
+                                          uint32_t, uint64_t, uint32_t, cudaStream_t);
+
+int launch_im2col_quantize(uint32_t* packed, float* scales, const float* in, uint32_t batch, uint32_t iw,
+                           uint32_t ih, uint32_t ic, uint32_t ow, uint32_t oh, uint32_t k, uint32_t s, int pad,
+                           uint32_t out_words, cudaStream_t st) {
+    const uint64_t rows = (uint64_t)ow * oh;
+    im2col_quantize_kernel<<<(unsigned)(rows * batch), 128, 0, st>>>(packed, scales, in, iw, ih, ic, ow, oh, k, s,
+                                                                      pad, out_words, (uint64_t)ic * iw * ih, rows);
+    return check_launch("im2col_quantize");
+}
+
+}  // namespace dav2cuda

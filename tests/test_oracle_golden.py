@@ -1,0 +1,219 @@
+"""Pins the CPU oracle (oracle/dav2_oracle.c) before it is trusted:
+  * against the reference's own known-answer tests (tests/vulkan_smoke.cpp,
+    tests/image_tests.cpp, tests/c_abi_smoke.c), with their tolerances;
+  * against fixtures produced by the reference's Python model
+    (tests/golden/make_golden.py: torch CPU, the reference's declared
+    accuracy authority).
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import max_rel
+
+G = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture(scope="module")
+def ops():
+    return np.load(G / "ops.npz")
+
+
+def test_crc32_kat():
+    assert oracle.crc32(b"123456789") == 0xCBF43926  # tests/vulkan_smoke.cpp:68-69
+
+
+def test_network_shape_kat():
+    # tests/image_tests.cpp:10-17, tests/c_abi_smoke.c:16-22
+    assert oracle.network_shape(640, 480, 518) == (686, 518)
+    assert oracle.network_shape(480, 640, 518) == (518, 686)
+    assert oracle.network_shape(518, 518, 518) == (518, 518)
+    assert oracle.network_shape(1920, 1080, 280) == (504, 280)
+    with pytest.raises(ValueError):
+        oracle.network_shape(0, 480, 518)
+
+
+def test_one_pixel_bgr_kat():
+    # tests/image_tests.cpp:19-25
+    chw = oracle.preprocess_bgr8(np.array([[[0, 0, 255]]], np.uint8), 1, 1).reshape(3)
+    assert abs(chw[0] - np.float32((1.0 - 0.485) / 0.229)) < 1e-6
+    assert abs(chw[1] - np.float32((0.0 - 0.456) / 0.224)) < 1e-6
+    assert abs(chw[2] - np.float32((0.0 - 0.406) / 0.225)) < 1e-6
+
+
+def test_minmax_normalize_kat():
+    # tests/vulkan_smoke.cpp:121-142
+    d = np.array([2, 3, 5, 10], np.float32)
+    out = oracle.normalize_relative(d, oracle.reduce_minmax(d))
+    assert np.abs(out - [0, 0.125, 0.375, 1]).max() <= 1e-6
+
+
+def _kat_conv():
+    W, H, C, O, K = 5, 4, 4, 5, 3
+    x = (((np.arange(W * H * C) % 23) - 11) * 0.03125).astype(np.float32).reshape(C, H, W)
+    w = (((np.arange(O * C * K * K) % 19) - 9) * 0.015625).astype(np.float32).reshape(O, C, K, K)
+    b = (np.arange(O) * 0.01).astype(np.float32)
+    return x, w, b
+
+
+def test_conv2d_int8_vs_fp32_kat():
+    # tests/vulkan_smoke.cpp:143-186: int8 conv within 0.006 of fp32 conv
+    x, w, b = _kat_conv()
+    pw, sw = oracle.pack_weight_s8(w)
+    pk, sc = oracle.im2col_quantize_s8(x, 3, 1, 1)
+    int8 = oracle.linear_s8(pk, pw, sc, sw, b, 20, 36, 5, transposed=True).reshape(5, 4, 5)
+    assert np.abs(int8 - oracle.conv2d_f32(x, w, b, 1, 1)).max() <= 0.006
+
+
+def test_conv_transpose_int8_vs_fp32_kat():
+    # tests/vulkan_smoke.cpp:187-240
+    W, H, I, O, K = 3, 2, 4, 3, 2
+    x = (((np.arange(W * H * I) % 17) - 8) * 0.03125).astype(np.float32).reshape(I, H, W)
+    w = (((np.arange(I * O * K * K) % 13) - 6) * 0.02).astype(np.float32).reshape(I, O, K, K)
+    b = (np.arange(O) * 0.01).astype(np.float32)
+    pw, sw = oracle.pack_weight_s8(w, transposed_conv=True)
+    pk, sc = oracle.im2col_quantize_s8(x, 1, 1, 0)
+    int8 = oracle.conv_transpose_s8(pk, pw, sc, sw, b, W, H, I, O, K)
+    assert np.abs(int8 - oracle.conv_transpose_f32(x, w, b)).max() <= 0.004
+
+
+def test_conv_stride2_kat():
+    # tests/vulkan_smoke.cpp:241-337 (expected loop restated in numpy), +-2e-6
+    x = (((np.arange(5 * 9 * 11) % 17) - 8) * 0.03125).astype(np.float32).reshape(5, 9, 11)
+    w = (((np.arange(9 * 5 * 9) % 13) - 6) * 0.015625).astype(np.float32).reshape(9, 5, 3, 3)
+    b = ((np.arange(9) - 4) * 0.0078125).astype(np.float32)
+    got = oracle.conv2d_f32(x, w, b, 2, 1)
+    xp = np.pad(x, ((0, 0), (1, 1), (1, 1)))
+    want = np.zeros((9, 5, 6), np.float64)
+    for oy in range(5):
+        for ox in range(6):
+            patch = xp[:, oy * 2:oy * 2 + 3, ox * 2:ox * 2 + 3]
+            want[:, oy, ox] = (w * patch[None]).reshape(9, -1).sum(1) + b
+    assert np.abs(got - want).max() <= 2e-6
+
+
+def test_linear_kat():
+    # tests/vulkan_smoke.cpp:338-402, +-1e-6
+    x = (((np.arange(3 * 19) % 13) - 6) * 0.03125).astype(np.float32).reshape(3, 19)
+    w = (((np.arange(7 * 19) % 11) - 5) * 0.015625).astype(np.float32).reshape(7, 19)
+    b = (np.arange(7) * 0.0625).astype(np.float32)
+    assert np.abs(oracle.linear_f32(x, w, b) - (x.astype(np.float64) @ w.T + b)).max() <= 1e-6
+
+
+def test_layer_norm_kat():
+    # tests/vulkan_smoke.cpp:436-494, +-1e-5
+    x = ((np.arange(4 * 17) % 23) - 10).astype(np.float32).reshape(4, 17) * 0.125
+    out = oracle.layer_norm(x, np.ones(17, np.float32), np.zeros(17, np.float32))
+    m = x.mean(1, keepdims=True)
+    v = np.maximum((x * x).mean(1, keepdims=True) - m * m, 0)
+    assert np.abs(out - (x - m) / np.sqrt(v + 1e-6)).max() <= 1e-5
+
+
+def test_add_scaled_exact_kat():
+    # tests/vulkan_smoke.cpp:496-538: exact
+    res = np.arange(15, dtype=np.float32) * 0.125
+    add = (np.arange(15, dtype=np.float32) + 2) * -0.0625
+    sc = (np.arange(5, dtype=np.float32) + 1) * 0.25
+    assert np.array_equal(oracle.add_scaled(res, add, sc), res + add * np.tile(sc, 3))
+
+
+def test_attention_kat():
+    # tests/vulkan_smoke.cpp:540-628, +-2e-6
+    T, H = 5, 2
+    qkv = (((np.arange(T * H * 64 * 3) % 29) - 14) * 0.0078125).astype(np.float32).reshape(T, 3 * H * 64)
+    got = oracle.attention_head64(qkv, T, H)
+    E = H * 64
+    for h in range(H):
+        q = qkv[:, h * 64:(h + 1) * 64].astype(np.float64) * 0.125
+        k = qkv[:, E + h * 64:E + (h + 1) * 64].astype(np.float64)
+        v = qkv[:, 2 * E + h * 64:2 * E + (h + 1) * 64].astype(np.float64)
+        s = q @ k.T
+        p = np.exp(s - s.max(1, keepdims=True))
+        p /= p.sum(1, keepdims=True)
+        assert np.abs(got[:, h * 64:(h + 1) * 64] - p @ v).max() <= 2e-6
+
+
+def test_prepare_tokens_kat():
+    # tests/vulkan_smoke.cpp:630-754: 42x28 zero image, D=3, pos (i%31-15)/64
+    D, pw, ph = 3, 3, 2
+    pos = (((np.arange(1370 * D) % 31) - 15) * 0.015625).astype(np.float32).reshape(1370, D)
+    bias = np.array([0.25, -0.5, 0.75], np.float32)
+    cls = np.array([1, 2, 3], np.float32)
+    tokens = oracle.patch_embed_f32(np.zeros((3, 28, 42), np.float32), np.zeros((D, 3, 14, 14), np.float32), bias, cls)
+    tokens = oracle.add_position(tokens, oracle.position_bicubic(pos, pw, ph), pos, pw, ph)
+    assert np.array_equal(tokens[0], cls + pos[0])
+
+    def c1(x):
+        a = -0.75
+        return ((a + 2) * x - (a + 3)) * x * x + 1
+
+    def c2(x):
+        a = -0.75
+        return ((a * x - 5 * a) * x + 8 * a) * x - 4 * a
+
+    for py in range(ph):
+        for px in range(pw):
+            sx = (px + 0.5) * (37.0 / (pw + 0.1)) - 0.5
+            sy = (py + 0.5) * (37.0 / (ph + 0.1)) - 0.5
+            bx, by = int(np.floor(sx)), int(np.floor(sy))
+            fx, fy = sx - bx, sy - by
+            cx = [c2(fx + 1), c1(fx), c1(1 - fx), c2(2 - fx)]
+            cy = [c2(fy + 1), c1(fy), c1(1 - fy), c2(2 - fy)]
+            for f in range(D):
+                e = bias[f]
+                for r in range(4):
+                    yy = min(max(by - 1 + r, 0), 36)
+                    row = sum(pos[1 + yy * 37 + min(max(bx - 1 + c, 0), 36), f] * cx[c] for c in range(4))
+                    e += row * cy[r]
+                assert abs(tokens[1 + py * pw + px, f] - e) <= 2e-6
+
+
+# ------------------------------------------ fixtures from the Python reference
+def test_ops_vs_reference_python(ops):
+    assert max_rel(oracle.layer_norm(ops["ln_x"], ops["ln_w"], ops["ln_b"]), ops["ln_y"]) < 1e-5
+    assert np.abs(oracle.gelu(ops["gelu_x"]) - ops["gelu_y"]).max() < 1e-6 * 16
+    assert max_rel(oracle.softmax_rows(ops["sm_x"], 0.125), ops["sm_y"]) < 1e-5
+    assert max_rel(oracle.bilinear_align_true(ops["bl_x"], 45, 37), ops["bl_y"]) < 1e-5
+    assert max_rel(oracle.conv2d_f32(ops["cv_x"], ops["cv_w"], ops["cv_b"], 1, 1), ops["cv_y1"]) < 1e-5
+    assert max_rel(oracle.conv2d_f32(ops["cv_x"], ops["cv_w"], ops["cv_b"], 2, 1), ops["cv_y2"]) < 1e-5
+    assert max_rel(oracle.conv_transpose_f32(ops["ct_x"], ops["ct_w"], ops["ct_b"]), ops["ct_y"]) < 1e-5
+    assert max_rel(oracle.attention_head64(ops["att_qkv"], 9, 2), ops["att_out"]) < 1e-5
+
+
+def test_position_interpolation_vs_reference_python(ops):
+    pos = (np.random.default_rng(5).standard_normal((1, 1370, 384)) * 0.02).astype(np.float32)
+    # the fixture called interpolate_pos_encoding(x, 98, 70): DINOv2 names
+    # the image dims (w, h) = (H, W), so the grid is 7 rows x 5 columns
+    pw, ph = 5, 7
+    planar = oracle.position_bicubic(pos, pw, ph)
+    want = ops["pos_out"][0]  # [1 + 35, 384]
+    assert np.abs(planar.reshape(384, -1).T - want[1:]).max() < 1e-6
+    assert np.array_equal(want[0], pos[0, 0])
+
+
+@pytest.mark.parametrize("tag", ["base", "strong"])
+@pytest.mark.parametrize("shape", ["70x98", "126x126"])
+def test_full_graph_vs_reference_python(tag, shape):
+    from dav2_b200 import dav2file
+
+    fx = np.load(G / "model_vits.npz")
+    sd = dav2file.random_state_dict("vits", seed=0) if tag == "base" else \
+        dav2file.random_state_dict("vits", seed=1, std=0.05, bias_std=0.02)
+    ref = fx[f"{tag}_{shape}_out"]
+    got = oracle.infer_tensor(sd, fx[f"{tag}_{shape}_in"], "vits")
+    assert max_rel(got, ref) < 1e-5
+    assert np.abs(got - ref).max() / (ref.max() - ref.min()) < 1e-3
+
+
+def test_infer_image_vs_reference_python():
+    from dav2_b200 import dav2file
+
+    fx = np.load(G / "image_vits.npz")
+    sd = dav2file.random_state_dict("vits", seed=1, std=0.05, bias_std=0.02)
+    nw, nh = oracle.network_shape(53, 37, 70)
+    tensor = oracle.preprocess_bgr8(fx["bgr"], nw, nh)
+    assert np.abs(tensor - fx["tensor"]).max() < 1e-5
+    depth = oracle.infer_bgr8(sd, fx["bgr"], "vits", 70)
+    assert max_rel(depth, fx["depth"]) < 1e-5

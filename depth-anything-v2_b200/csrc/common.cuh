@@ -213,11 +213,4 @@ __device__ __forceinline__ uint32_t q8(float v) {
 
 }  // namespace dav2cuda
 
-// Host-side helpers shared by the .cu translation units.
-namespace dav2cuda {
-int set_error(int status, const char* message);
-int check_launch(const char* what);
-// Device address of the error word of the current device.
-int* device_error_word();
-inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
-}  // namespace dav2cuda
+#include "launch.h"

@@ -1,132 +1,5 @@
-// Internal launcher declarations shared by the C ABI (dav2cuda_abi.cu) and
-// the executor runtime.
+// Device-side helpers plus the launcher declarations.
 #pragma once
 
 #include "common.cuh"
-
-namespace dav2cuda {
-
-// ------------------------------------------------------------ memory-bound
-enum LnOutKind { kLnOutF32 = 0, kLnOutF16 = 1, kLnOutBF16 = 2, kLnOutS8 = 3 };
-int launch_layer_norm(void* out, float* out_scales, const float* in, const float* w, const float* b,
-                      uint32_t rows, uint32_t cols, float eps, int out_kind, uint32_t out_group,
-                      uint32_t in_group, uint32_t in_offset, cudaStream_t st);
-int launch_gelu(float* out, const float* in, uint64_t n, cudaStream_t st);
-int launch_softmax(float* out, const float* in, uint64_t rows, uint32_t cols, float scale, cudaStream_t st);
-int launch_add_scaled(float* out, const float* res, const float* add, const float* scale, uint64_t n,
-                      uint32_t cols, cudaStream_t st);
-int launch_relu(float* out, const float* in, uint64_t n, cudaStream_t st);
-int launch_add(float* out, const float* a, const float* b, uint64_t n, cudaStream_t st);
-int launch_sigmoid_scale(float* out, const float* in, uint64_t n, float s, cudaStream_t st);
-template <typename TI, typename TO>
-int launch_bilinear_align(TO* out, const TI* in, uint32_t iw, uint32_t ih, uint32_t ow, uint32_t oh,
-                          uint32_t planes, cudaStream_t st);
-int launch_minmax(const float* in, float* range, uint64_t n, cudaStream_t st);
-int launch_normalize(float* d, const float* range, uint64_t n, float maximum, cudaStream_t st);
-int launch_preprocess_u32(float* out, const uint32_t* px, uint32_t sw, uint32_t sh, uint32_t stride,
-                          uint32_t rgba, uint32_t dw, uint32_t dh, cudaStream_t st);
-int launch_preprocess_bgr8(float* out, const uint8_t* bgr, uint32_t batch, uint32_t sw, uint32_t sh,
-                           uint64_t row_stride, uint64_t img_stride, uint32_t dw, uint32_t dh, int bilinear,
-                           cudaStream_t st);
-template <typename T>
-int launch_quantize_rows(uint32_t* packed, float* scales, const T* in, uint64_t rows, uint32_t cols,
-                         uint64_t offset, uint32_t group, uint64_t group_stride, uint32_t out_words,
-                         cudaStream_t st);
-int launch_im2col_quantize(uint32_t* packed, float* scales, const float* in, uint32_t batch, uint32_t iw,
-                           uint32_t ih, uint32_t ic, uint32_t ow, uint32_t oh, uint32_t k, uint32_t s, int pad,
-                           uint32_t out_words, cudaStream_t st);
-
-// --------------------------------------------------------- layout helpers
-// planar f32 [B][C][H][W] -> channels-last half [B][H][W][Cp] (channels
-// beyond C are zero).
-template <typename H>
-int launch_nchw_to_nhwc(H* out, const float* in, uint32_t batch, uint32_t c, uint32_t h, uint32_t w,
-                        uint32_t cp, cudaStream_t st);
-// f32 -> half (elementwise, any count).
-template <typename H>
-int launch_to_half(H* out, const float* in, uint64_t n, cudaStream_t st);
-// f32 matrix [rows, cols] -> half [rows, cols_p] with zero padding.
-template <typename H>
-int launch_pad_rows_half(H* out, const float* in, uint64_t rows, uint32_t cols, uint32_t cols_p,
-                         cudaStream_t st);
-// Explicit im2col of a channels-last half map (any stride/padding); column
-// order (ky, kx, c) and rows padded to kp columns.
-template <typename H>
-int launch_im2col_nhwc(H* out, const H* in, uint32_t batch, uint32_t h, uint32_t w, uint32_t c, uint32_t k,
-                       uint32_t s, uint32_t pad, uint32_t oh, uint32_t ow, uint32_t kp, cudaStream_t st);
-// Weight reorders: [Co][Ci][k][k] f32 -> [Co][k][k][Cip] half.
-template <typename H>
-int launch_conv_weight_to_half(H* out, const float* w, uint32_t co, uint32_t ci, uint32_t k, uint32_t cip,
-                               cudaStream_t st);
-
-// ------------------------------------------------------------- attention
-template <typename H>
-int launch_attention(H* out, const H* qkv, uint32_t batch, uint32_t tokens, uint32_t heads, uint64_t qkv_ld,
-                     uint64_t out_ld, cudaStream_t st);
-
-// ------------------------------------------------------------------ GEMM
-enum GemmElem { kElemS8 = 0, kElemF16 = 1, kElemBF16 = 2 };
-enum GemmAMode { kAModeRows = 0, kAModeConv3x3 = 1 };
-enum EpiFlags : uint32_t {
-    kEpiBias = 1u << 0,
-    kEpiDequant = 1u << 1,      // int8: acc * s_in[row] * s_w[col]
-    kEpiGelu = 1u << 2,
-    kEpiLayerScale = 1u << 3,   // res + v * gamma[col] (f32 residual, rounded separately)
-    kEpiResidual1 = 1u << 4,    // v + res1
-    kEpiResidual2 = 1u << 5,    // res2 + (...)
-    kEpiRelu = 1u << 6,
-    kEpiReluCopy = 1u << 7,     // also store relu(v) to out2
-    kEpiHeadDot = 1u << 8,      // relu(v) . w2 + b2 -> one value per row (output head)
-    kEpiMetricHead = 1u << 9,   // head output: sigmoid * max_depth instead of relu
-};
-enum OutKind {
-    kOutF32Rows = 0,    // row-major, ldo elements per row
-    kOutHalfRows = 1,   // row-major half (f16 / bf16 per out_half_bf16)
-    kOutF32Planar = 2,  // per image planar: [img][col][plane]
-    kOutConvTF32 = 3,   // conv-transpose scatter into planar f32 [img][co][H*k][W*k]
-    kOutConvTHalf = 4,  // conv-transpose scatter into channels-last half [img][H*k][W*k][co]
-    kOutHeadF32 = 5,    // kEpiHeadDot result, one f32 per row at out[row_remap]
-};
-
-struct GemmArgs {
-    int elem = kElemBF16;
-    int a_mode = kAModeRows;
-    // operands
-    const void* a = nullptr;        // rows mode: [M][lda] ; conv mode: NHWC [img][H][W][C]
-    uint64_t lda = 0;               // elements per A row (rows mode)
-    const void* b = nullptr;        // [N][ldb] (K-major weights)
-    uint64_t ldb = 0;
-    uint32_t m = 0, n = 0, k = 0;   // GEMM extents (k = reduction length in elements)
-    // conv mode geometry (3x3, stride 1, pad 1, channels-last input)
-    uint32_t conv_batch = 0, conv_h = 0, conv_w = 0, conv_c = 0;
-    // epilogue
-    uint32_t flags = 0;
-    int out_kind = kOutF32Rows;
-    bool out_half_bf16 = false;     // half outputs: bf16 (true) or f16 (false)
-    void* out = nullptr;
-    void* out2 = nullptr;           // relu copy (same layout as out)
-    uint64_t ldo = 0;
-    const float* bias = nullptr;
-    const float* s_in = nullptr;
-    const float* s_w = nullptr;
-    const float* gamma = nullptr;
-    const void* res1 = nullptr;     // residual tensors: same layout and type as out
-    const void* res2 = nullptr;
-    const float* head_w = nullptr;  // kEpiHeadDot
-    float head_b = 0.f;
-    float head_max_depth = 0.f;
-    // row remap: out_row = (r / rows_per_img) * out_rows_per_img + row_offset + r % rows_per_img
-    uint32_t rows_per_img = 0;      // 0 = no remap (identity)
-    uint32_t out_rows_per_img = 0;
-    uint32_t row_offset = 0;
-    // planar outputs: image stride and channel stride in elements
-    uint64_t img_stride = 0, col_stride = 0;
-    // conv-transpose scatter
-    uint32_t convt_k = 0, convt_cout = 0, convt_w = 0, convt_h = 0;
-    int block_n = 0;                // 0 = choose
-    int max_ctas = 0;               // 0 = all SMs
-};
-
-int launch_gemm(const GemmArgs& args, cudaStream_t st);
-
-}  // namespace dav2cuda
+#include "launch.h"

@@ -1,0 +1,327 @@
+// Kernels the executor graph needs around the GEMMs: patch im2col, the
+// bicubic positional-embedding resize, token initialisation, channels-last
+// bilinear resize and im2col-quantize, and on-device weight preparation
+// (per-output-row int8 codes, half conversion, reorders).
+#include "kernels.cuh"
+
+namespace dav2cuda {
+namespace {
+
+template <typename H>
+__device__ __forceinline__ H cvt(float v);
+template <>
+__device__ __forceinline__ __half cvt<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 cvt<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <typename H>
+__device__ __forceinline__ float tof(H v);
+template <>
+__device__ __forceinline__ float tof<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float tof<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+unsigned gcap(uint64_t n) {
+    const uint64_t g = (n + 255) / 256;
+    return (unsigned)(g == 0 ? 1 : (g < 148 * 32 ? g : 148 * 32));
+}
+
+// Non-overlapping 14x14 patches of planar [B][3][H][W] images -> rows
+// (img, py, px) with columns c*196 + ky*14 + kx (the Conv2d weight order),
+// zero-padded to kp columns.
+template <typename H>
+__global__ void patch_im2col_kernel(H* __restrict__ out, const float* __restrict__ img, uint32_t h, uint32_t w,
+                                    uint32_t kp, uint64_t rows) {
+    const uint32_t pw = w / 14, ph = h / 14;
+    const uint64_t n = rows * kp;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint64_t r = i / kp;
+        const uint32_t col = (uint32_t)(i % kp);
+        float v = 0.f;
+        if (col < 588) {
+            const uint64_t b = r / ((uint64_t)pw * ph);
+            const uint32_t p = (uint32_t)(r % ((uint64_t)pw * ph));
+            const uint32_t py = p / pw, px = p % pw;
+            const uint32_t c = col / 196, rem = col % 196;
+            v = __ldg(img + ((b * 3 + c) * h + py * 14 + rem / 14) * w + px * 14 + rem % 14);
+        }
+        out[i] = cvt<H>(v);
+    }
+}
+
+// position_bicubic.glsl:76-105 (a = -0.75, clamp to the 37x37 grid) with
+// the scale rule of src/operators.cpp:1346-1364, written token-major:
+// out[(py*pw + px)*D + f].
+__device__ __forceinline__ float cc1(float x) {
+    const float a = -0.75f;
+    return ((a + 2.0f) * x - (a + 3.0f)) * x * x + 1.0f;
+}
+__device__ __forceinline__ float cc2(float x) {
+    const float a = -0.75f;
+    return ((a * x - 5.0f * a) * x + 8.0f * a) * x - 4.0f * a;
+}
+__device__ __forceinline__ float cubic_interp(float x0, float x1, float x2, float x3, float t) {
+    return x0 * cc2(t + 1.0f) + x1 * cc1(t) + x2 * cc1(1.0f - t) + x3 * cc2((1.0f - t) + 1.0f);
+}
+
+__global__ void position_bicubic_kernel(float* __restrict__ out, const float* __restrict__ pos, uint32_t d,
+                                        uint32_t pw, uint32_t ph, float sx, float sy) {
+    const uint64_t n = (uint64_t)pw * ph * d;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint32_t f = (uint32_t)(i % d);
+        const uint32_t p = (uint32_t)(i / d);
+        const uint32_t x = p % pw, y = p / pw;
+        const float srcx = ((float)x + 0.5f) * sx - 0.5f;
+        const float srcy = ((float)y + 0.5f) * sy - 0.5f;
+        const int bx = (int)floorf(srcx), by = (int)floorf(srcy);
+        const float tx = srcx - (float)bx, ty = srcy - (float)by;
+        float rows[4];
+        for (int k = 0; k < 4; ++k) {
+            const int yy = min(max(by - 1 + k, 0), 36);
+            float v[4];
+            for (int j = 0; j < 4; ++j) {
+                const int xx = min(max(bx - 1 + j, 0), 36);
+                v[j] = __ldg(pos + (uint64_t)(1 + yy * 37 + xx) * d + f);
+            }
+            rows[k] = cubic_interp(v[0], v[1], v[2], v[3], tx);
+        }
+        out[i] = cubic_interp(rows[0], rows[1], rows[2], rows[3], ty);
+    }
+}
+
+// tokens[img*T + 0] = cls + pos[0]; tokens[img*T + 1 + p] = pos_interp[p]
+// (the patch GEMM then adds its result on top: add_position.glsl order).
+__global__ void fill_tokens_kernel(float* __restrict__ x, const float* __restrict__ cls,
+                                   const float* __restrict__ pos, const float* __restrict__ interp, uint32_t d,
+                                   uint32_t tokens, uint64_t rows) {
+    const uint64_t n = rows * d;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint32_t f = (uint32_t)(i % d);
+        const uint32_t t = (uint32_t)((i / d) % tokens);
+        x[i] = t == 0 ? __ldg(cls + f) + __ldg(pos + f) : __ldg(interp + (uint64_t)(t - 1) * d + f);
+    }
+}
+
+// Align-corners bilinear on channels-last half maps: 8 channels per thread.
+template <typename H>
+__global__ void bilinear_nhwc_kernel(H* __restrict__ out, const H* __restrict__ in, uint32_t ih, uint32_t iw,
+                                     uint32_t oh, uint32_t ow, uint32_t c, uint32_t batch) {
+    const uint32_t cv = c / 8;
+    const uint64_t n = (uint64_t)batch * oh * ow * cv;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint32_t cc = (uint32_t)(i % cv) * 8;
+        const uint64_t pix = i / cv;
+        const uint32_t x = (uint32_t)(pix % ow);
+        const uint32_t y = (uint32_t)((pix / ow) % oh);
+        const uint64_t b = pix / ((uint64_t)ow * oh);
+        const float sxf = ow > 1 ? __fdiv_rn(__fmul_rn((float)x, (float)(iw - 1)), (float)(ow - 1)) : 0.f;
+        const float syf = oh > 1 ? __fdiv_rn(__fmul_rn((float)y, (float)(ih - 1)), (float)(oh - 1)) : 0.f;
+        const uint32_t x0 = (uint32_t)floorf(sxf), y0 = (uint32_t)floorf(syf);
+        const uint32_t x1 = min(x0 + 1, iw - 1), y1 = min(y0 + 1, ih - 1);
+        const float fx = sxf - (float)x0, fy = syf - (float)y0;
+        const H* base = in + b * ih * iw * c;
+        const uint4 a00 = *reinterpret_cast<const uint4*>(base + ((uint64_t)y0 * iw + x0) * c + cc);
+        const uint4 a01 = *reinterpret_cast<const uint4*>(base + ((uint64_t)y0 * iw + x1) * c + cc);
+        const uint4 a10 = *reinterpret_cast<const uint4*>(base + ((uint64_t)y1 * iw + x0) * c + cc);
+        const uint4 a11 = *reinterpret_cast<const uint4*>(base + ((uint64_t)y1 * iw + x1) * c + cc);
+        const H* h00 = reinterpret_cast<const H*>(&a00);
+        const H* h01 = reinterpret_cast<const H*>(&a01);
+        const H* h10 = reinterpret_cast<const H*>(&a10);
+        const H* h11 = reinterpret_cast<const H*>(&a11);
+        uint4 res;
+        H* r = reinterpret_cast<H*>(&res);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float top = tof(h00[j]) * (1.f - fx) + tof(h01[j]) * fx;
+            const float bot = tof(h10[j]) * (1.f - fx) + tof(h11[j]) * fx;
+            r[j] = cvt<H>(top * (1.f - fy) + bot * fy);
+        }
+        *reinterpret_cast<uint4*>(out + pix * c + cc) = res;
+    }
+}
+
+// im2col-quantize of a channels-last half map (the stride-2 resize layer in
+// the int8 path): row = output pixel, columns in (ky, kx, c) order — the
+// reference's (c, ky, kx) order with the weight columns permuted alike, which
+// leaves every row scale, every code and every integer dot product
+// unchanged. Row scale = max(absmax/127, 1e-8), code = rint(x*(1/scale)).
+template <typename H>
+__global__ void __launch_bounds__(256) im2col_quantize_nhwc_kernel(uint8_t* __restrict__ out,
+                                                                   float* __restrict__ scales,
+                                                                   const H* __restrict__ in, uint32_t h,
+                                                                   uint32_t w, uint32_t c, uint32_t ldc,
+                                                                   uint32_t k, uint32_t s, uint32_t pad,
+                                                                   uint32_t oh, uint32_t ow, uint32_t kp) {
+    __shared__ float red[8];
+    const uint64_t r = blockIdx.x;
+    const uint64_t b = r / ((uint64_t)oh * ow);
+    const uint32_t pp = (uint32_t)(r % ((uint64_t)oh * ow));
+    const uint32_t oy = pp / ow, ox = pp % ow;
+    const uint32_t cols = k * k * c;
+    auto value = [&](uint32_t col) -> float {
+        const uint32_t tap = col / c, ch = col % c;
+        const int iy = (int)(oy * s + tap / k) - (int)pad, ix = (int)(ox * s + tap % k) - (int)pad;
+        if (iy < 0 || ix < 0 || iy >= (int)h || ix >= (int)w) return 0.f;
+        return tof(in[((b * h + iy) * w + ix) * ldc + ch]);
+    };
+    float m = 0.f;
+    for (uint32_t col = threadIdx.x; col < cols; col += 256) m = fmaxf(m, fabsf(value(col)));
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int i = 0; i < 8; ++i) t = fmaxf(t, red[i]);
+        red[0] = fmaxf(t / 127.0f, 1.0e-8f);
+        scales[r] = red[0];
+    }
+    __syncthreads();
+    const float inv = 1.0f / red[0];
+    for (uint32_t col = threadIdx.x; col < kp; col += 256)
+        out[r * kp + col] = col < cols ? (uint8_t)q8(__fmul_rn(value(col), inv)) : 0;
+}
+
+// Per-output-row int8 weight codes (src/gpu_model.cpp:207-284): scale =
+// max(absmax/127, 1e-8), code = nearbyint(clamp(w/scale)). Source element
+// of (row, col) per layout:
+//   kind 0: w[row*K + col]                          (linear / conv, c-major)
+//   kind 1: conv-transpose [Ci][Co][k][k]: row = (ky*k+kx)*Co + co, col = ci
+//   kind 2: conv [Co][Ci][k][k] with columns reordered to (ky, kx, ci)
+__device__ __forceinline__ float weight_at(const float* w, int kind, uint64_t row, uint32_t col, uint32_t K,
+                                           uint32_t co, uint32_t k, uint32_t ci) {
+    if (kind == 0) return w[row * K + col];
+    if (kind == 1) {
+        const uint32_t kk = (uint32_t)(row / co), o = (uint32_t)(row % co);
+        return w[(((uint64_t)col * co + o) * k + kk / k) * k + kk % k];
+    }
+    const uint32_t tap = col / ci, c = col % ci;
+    return w[((row * ci + c) * k + tap / k) * k + tap % k];
+}
+
+__global__ void __launch_bounds__(256) pack_weight_s8_kernel(uint8_t* __restrict__ out, float* __restrict__ scales,
+                                                             const float* __restrict__ w, int kind, uint32_t K,
+                                                             uint32_t kp, uint32_t co, uint32_t k, uint32_t ci) {
+    __shared__ float red[8];
+    const uint64_t row = blockIdx.x;
+    float m = 0.f;
+    for (uint32_t col = threadIdx.x; col < K; col += 256) m = fmaxf(m, fabsf(weight_at(w, kind, row, col, K, co, k, ci)));
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int i = 0; i < 8; ++i) t = fmaxf(t, red[i]);
+        red[0] = fmaxf(t / 127.0f, 1.0e-8f);
+        scales[row] = red[0];
+    }
+    __syncthreads();
+    const float scale = red[0];
+    for (uint32_t col = threadIdx.x; col < kp; col += 256)
+        out[row * kp + col] = col < K ? (uint8_t)q8(weight_at(w, kind, row, col, K, co, k, ci) / scale) : 0;
+}
+
+// Half weights in the same three layouts (kind 2 pads channels to cip).
+template <typename H>
+__global__ void half_weight_kernel(H* __restrict__ out, const float* __restrict__ w, int kind, uint64_t rows,
+                                   uint32_t K, uint32_t kp, uint32_t co, uint32_t k, uint32_t ci, uint32_t cip) {
+    const uint64_t n = rows * kp;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint64_t row = i / kp;
+        const uint32_t col = (uint32_t)(i % kp);
+        float v = 0.f;
+        if (kind == 2) {
+            const uint32_t tap = col / cip, c = col % cip;
+            if (tap < k * k && c < ci) v = w[((row * ci + c) * k + tap / k) * k + tap % k];
+        } else if (col < K) {
+            v = weight_at(w, kind, row, col, K, co, k, ci);
+        }
+        out[i] = cvt<H>(v);
+    }
+}
+
+__global__ void expand_bias_kernel(float* __restrict__ out, const float* __restrict__ bias, uint32_t co,
+                                   uint32_t reps) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < co * reps) out[i] = bias[i % co];
+}
+
+}  // namespace
+
+template <typename H>
+int launch_patch_im2col(H* out, const float* img, uint32_t batch, uint32_t h, uint32_t w, uint32_t kp,
+                        cudaStream_t st) {
+    const uint64_t rows = (uint64_t)batch * (h / 14) * (w / 14);
+    patch_im2col_kernel<H><<<gcap(rows * kp), 256, 0, st>>>(out, img, h, w, kp, rows);
+    return check_launch("patch_im2col");
+}
+
+int launch_position_bicubic(float* out, const float* pos, uint32_t d, uint32_t pw, uint32_t ph, cudaStream_t st) {
+    const bool same = pw == 37 && ph == 37;
+    const float sx = same ? 1.0f : (float)(1.0 / (((double)pw + 0.1) / 37.0));
+    const float sy = same ? 1.0f : (float)(1.0 / (((double)ph + 0.1) / 37.0));
+    position_bicubic_kernel<<<gcap((uint64_t)pw * ph * d), 256, 0, st>>>(out, pos, d, pw, ph, sx, sy);
+    return check_launch("position_bicubic");
+}
+
+int launch_fill_tokens(float* x, const float* cls, const float* pos, const float* interp, uint32_t d,
+                       uint32_t tokens, uint32_t batch, cudaStream_t st) {
+    const uint64_t rows = (uint64_t)batch * tokens;
+    fill_tokens_kernel<<<gcap(rows * d), 256, 0, st>>>(x, cls, pos, interp, d, tokens, rows);
+    return check_launch("fill_tokens");
+}
+
+template <typename H>
+int launch_bilinear_nhwc(H* out, const H* in, uint32_t batch, uint32_t ih, uint32_t iw, uint32_t oh, uint32_t ow,
+                         uint32_t c, cudaStream_t st) {
+    if (c % 8) return set_error(DAV2CUDA_INVALID_ARGUMENT, "bilinear_nhwc: channels % 8");
+    bilinear_nhwc_kernel<H><<<gcap((uint64_t)batch * oh * ow * (c / 8)), 256, 0, st>>>(out, in, ih, iw, oh, ow, c,
+                                                                                       batch);
+    return check_launch("bilinear_nhwc");
+}
+
+template <typename H>
+int launch_im2col_quantize_nhwc(uint8_t* out, float* scales, const H* in, uint32_t batch, uint32_t h, uint32_t w,
+                                uint32_t c, uint32_t ldc, uint32_t k, uint32_t s, uint32_t pad, uint32_t oh,
+                                uint32_t ow, uint32_t kp, cudaStream_t st) {
+    const uint64_t rows = (uint64_t)batch * oh * ow;
+    im2col_quantize_nhwc_kernel<H><<<(unsigned)rows, 256, 0, st>>>(out, scales, in, h, w, c, ldc, k, s, pad, oh, ow,
+                                                                    kp);
+    return check_launch("im2col_quantize_nhwc");
+}
+
+int launch_pack_weight_s8(uint8_t* out, float* scales, const float* w, int kind, uint64_t rows, uint32_t K,
+                          uint32_t kp, uint32_t co, uint32_t k, uint32_t ci, cudaStream_t st) {
+    pack_weight_s8_kernel<<<(unsigned)rows, 256, 0, st>>>(out, scales, w, kind, K, kp, co, k, ci);
+    return check_launch("pack_weight_s8");
+}
+
+template <typename H>
+int launch_half_weight(H* out, const float* w, int kind, uint64_t rows, uint32_t K, uint32_t kp, uint32_t co,
+                       uint32_t k, uint32_t ci, uint32_t cip, cudaStream_t st) {
+    half_weight_kernel<H><<<gcap(rows * kp), 256, 0, st>>>(out, w, kind, rows, K, kp, co, k, ci, cip);
+    return check_launch("half_weight");
+}
+
+int launch_expand_bias(float* out, const float* bias, uint32_t co, uint32_t reps, cudaStream_t st) {
+    expand_bias_kernel<<<(co * reps + 255) / 256, 256, 0, st>>>(out, bias, co, reps);
+    return check_launch("expand_bias");
+}
+
+#define DAV2_INST(H)                                                                                            \
+    template int launch_patch_im2col<H>(H*, const float*, uint32_t, uint32_t, uint32_t, uint32_t, cudaStream_t); \
+    template int launch_bilinear_nhwc<H>(H*, const H*, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t,       \
+                                         uint32_t, cudaStream_t);                                               \
+    template int launch_im2col_quantize_nhwc<H>(uint8_t*, float*, const H*, uint32_t, uint32_t, uint32_t,      \
+                                                uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t,     \
+                                                uint32_t, uint32_t, cudaStream_t);                              \
+    template int launch_half_weight<H>(H*, const float*, int, uint64_t, uint32_t, uint32_t, uint32_t, uint32_t, \
+                                       uint32_t, uint32_t, cudaStream_t);
+DAV2_INST(__half)
+DAV2_INST(__nv_bfloat16)
+#undef DAV2_INST
+
+}  // namespace dav2cuda

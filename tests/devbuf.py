@@ -1,17 +1,27 @@
-"""Device-buffer helpers for the GPU tests (torch is only the allocator)."""
+"""Device-buffer helpers for the GPU tests (torch is only the allocator).
+
+Buffers made here stay referenced until finish(): a tensor created inline in
+an argument list would otherwise be freed (and its block handed to the next
+allocation) before the asynchronous kernel reads it."""
 import numpy as np
+
+_live = []
 
 
 def dev(torch, array):
-    """numpy -> CUDA tensor (same dtype), contiguous."""
+    """numpy -> CUDA tensor (same dtype), contiguous, kept alive until finish()."""
     a = np.ascontiguousarray(array)
-    return torch.from_numpy(a.copy()).cuda()
+    t = torch.from_numpy(a.copy()).cuda()
+    _live.append(t)
+    return t
 
 
 def empty(torch, shape, dtype=np.float32):
     tdt = {np.float32: torch.float32, np.uint32: torch.int32, np.uint8: torch.uint8,
            np.int32: torch.int32}[np.dtype(dtype).type]
-    return torch.zeros(shape, dtype=tdt, device="cuda")
+    t = torch.zeros(shape, dtype=tdt, device="cuda")
+    _live.append(t)
+    return t
 
 
 def host(t, dtype=None):
@@ -36,4 +46,5 @@ def call(lib, name, *args):
 def finish(torch, lib):
     torch.cuda.synchronize()
     err = lib.dav2cuda_device_error()
+    _live.clear()
     assert err == 0, f"device error word = {err}"

@@ -229,7 +229,7 @@ int dav2cuda_quantize_rows_s8(uint32_t* packed, float* scales, const float* inpu
     REQUIRE(rows && columns && columns % 4 == 0, "invalid INT8 row quantization dimensions");
     REQUIRE(!null_any(packed, scales, input), "quantize: null buffer");
     return launch_quantize_rows<float>(packed, scales, input, rows, columns, input_offset, rows,
-                                       (uint64_t)rows * columns, columns / 4, as_stream(stream));
+                                       (uint64_t)rows * columns, columns, columns / 4, as_stream(stream));
 }
 
 int dav2cuda_im2col_quantize_s8(uint32_t* packed, float* scales, const float* input, uint32_t iw, uint32_t ih,
@@ -304,7 +304,7 @@ int dav2cuda_linear_int8(float* output, const float* input, const uint32_t* int8
         w = reinterpret_cast<const uint32_t*>(wp);
     }
     if (int rc = launch_quantize_rows<float>(codes, scales, input, rows, input_columns, 0, rows,
-                                             (uint64_t)rows * input_columns, kp / 4, st))
+                                             (uint64_t)rows * input_columns, input_columns, kp / 4, st))
         return rc;
     GemmArgs g;
     g.elem = kElemS8;

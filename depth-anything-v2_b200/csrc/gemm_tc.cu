@@ -229,7 +229,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParamsDev& p, const uin
         if (p.out_kind == kOutConvTF32) {
             reinterpret_cast<float*>(p.out)[((img * p.ct_cout + co) * oh + oy) * ow + ox] = v[j];
         } else {
-            const uint64_t idx = ((img * oh + oy) * ow + ox) * p.ct_cout + co;
+            const uint64_t idx = ((img * oh + oy) * ow + ox) * (p.ldo ? p.ldo : p.ct_cout) + co;
             if (p.out_bf16)
                 reinterpret_cast<__nv_bfloat16*>(p.out)[idx] = __float2bfloat16_rn(v[j]);
             else

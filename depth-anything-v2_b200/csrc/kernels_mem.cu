@@ -528,16 +528,18 @@ __device__ __forceinline__ float block_max_128(float v, float* red) {
 // quantize_rows_int8_fused.glsl:20-55: scale = max(absmax/127, 1e-8);
 // code = rint(clamp(x/scale, -127, 127)). One 128-thread block per row.
 // The input row o starts at input_offset + (o / group) * group_stride +
-// (o % group) * columns, so token matrices can skip their class row.
+// (o % group) * row_stride, so token matrices can skip their class row and
+// channel-padded maps can be read in place.
 template <typename T>
 __global__ void __launch_bounds__(128) quantize_rows_kernel(uint32_t* __restrict__ packed,
                                                             float* __restrict__ scales,
                                                             const T* __restrict__ in, uint32_t cols,
                                                             uint64_t offset, uint32_t group,
-                                                            uint64_t group_stride, uint32_t out_words) {
+                                                            uint64_t group_stride, uint32_t row_stride,
+                                                            uint32_t out_words) {
     __shared__ float red[4];
     const uint64_t row = blockIdx.x;
-    const T* x = in + offset + (row / group) * group_stride + (row % group) * (uint64_t)cols;
+    const T* x = in + offset + (row / group) * group_stride + (row % group) * (uint64_t)row_stride;
     float m = 0.f;
     for (uint32_t c = threadIdx.x; c < cols; c += 128) m = fmaxf(m, fabsf(to_f(x[c])));
     m = block_max_128(m, red);
@@ -732,17 +734,17 @@ int launch_preprocess_bgr8(float* out, const uint8_t* bgr, uint32_t batch, uint3
 
 template <typename T>
 int launch_quantize_rows(uint32_t* packed, float* scales, const T* in, uint64_t rows, uint32_t cols,
-                         uint64_t offset, uint32_t group, uint64_t group_stride, uint32_t out_words,
-                         cudaStream_t st) {
+                         uint64_t offset, uint32_t group, uint64_t group_stride, uint32_t row_stride,
+                         uint32_t out_words, cudaStream_t st) {
     if (rows == 0) return DAV2CUDA_OK;
     quantize_rows_kernel<T><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, offset, group, group_stride,
-                                                            out_words);
+                                                            row_stride, out_words);
     return check_launch("quantize_rows");
 }
 template int launch_quantize_rows<float>(uint32_t*, float*, const float*, uint64_t, uint32_t, uint64_t,
-                                         uint32_t, uint64_t, uint32_t, cudaStream_t);
+                                         uint32_t, uint64_t, uint32_t, uint32_t, cudaStream_t);
 template int launch_quantize_rows<__half>(uint32_t*, float*, const __half*, uint64_t, uint32_t, uint64_t,
-                                          uint32_t, uint64_t, uint32_t, cudaStream_t);
+                                          uint32_t, uint64_t, uint32_t, uint32_t, cudaStream_t);
 
 int launch_im2col_quantize(uint32_t* packed, float* scales, const float* in, uint32_t batch, uint32_t iw,
                            uint32_t ih, uint32_t ic, uint32_t ow, uint32_t oh, uint32_t k, uint32_t s, int pad,

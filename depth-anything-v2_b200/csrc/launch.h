@@ -41,8 +41,8 @@ int launch_preprocess_bgr8(float* out, const uint8_t* bgr, uint32_t batch, uint3
                            cudaStream_t st);
 template <typename T>
 int launch_quantize_rows(uint32_t* packed, float* scales, const T* in, uint64_t rows, uint32_t cols,
-                         uint64_t offset, uint32_t group, uint64_t group_stride, uint32_t out_words,
-                         cudaStream_t st);
+                         uint64_t offset, uint32_t group, uint64_t group_stride, uint32_t row_stride,
+                         uint32_t out_words, cudaStream_t st);
 int launch_im2col_quantize(uint32_t* packed, float* scales, const float* in, uint32_t batch, uint32_t iw,
                            uint32_t ih, uint32_t ic, uint32_t ow, uint32_t oh, uint32_t k, uint32_t s, int pad,
                            uint32_t out_words, cudaStream_t st);
@@ -70,6 +70,30 @@ template <typename H>
 int launch_conv_weight_to_half(H* out, const float* w, uint32_t co, uint32_t ci, uint32_t k, uint32_t cip,
                                cudaStream_t st);
 
+// ------------------------------------------------------------ graph pieces
+template <typename H>
+int launch_patch_im2col(H* out, const float* img, uint32_t batch, uint32_t h, uint32_t w, uint32_t kp,
+                        cudaStream_t st);
+int launch_position_bicubic(float* out, const float* pos, uint32_t d, uint32_t pw, uint32_t ph, cudaStream_t st);
+int launch_fill_tokens(float* x, const float* cls, const float* pos, const float* interp, uint32_t d,
+                       uint32_t tokens, uint32_t batch, cudaStream_t st);
+template <typename H>
+int launch_bilinear_nhwc(H* out, const H* in, uint32_t batch, uint32_t ih, uint32_t iw, uint32_t oh, uint32_t ow,
+                         uint32_t c, cudaStream_t st);
+template <typename H>
+int launch_im2col_quantize_nhwc(uint8_t* out, float* scales, const H* in, uint32_t batch, uint32_t h, uint32_t w,
+                                uint32_t c, uint32_t ldc, uint32_t k, uint32_t s, uint32_t pad, uint32_t oh,
+                                uint32_t ow, uint32_t kp, cudaStream_t st);
+// Weight layouts: 0 = [rows][K] as stored; 1 = conv-transpose [Ci][Co][k][k]
+// read as rows (ky*k+kx)*Co+co over Ci; 2 = conv [Co][Ci][k][k] read with
+// columns in (ky, kx, ci) order (half: channels padded to cip).
+int launch_pack_weight_s8(uint8_t* out, float* scales, const float* w, int kind, uint64_t rows, uint32_t K,
+                          uint32_t kp, uint32_t co, uint32_t k, uint32_t ci, cudaStream_t st);
+template <typename H>
+int launch_half_weight(H* out, const float* w, int kind, uint64_t rows, uint32_t K, uint32_t kp, uint32_t co,
+                       uint32_t k, uint32_t ci, uint32_t cip, cudaStream_t st);
+int launch_expand_bias(float* out, const float* bias, uint32_t co, uint32_t reps, cudaStream_t st);
+
 // ------------------------------------------------------------- attention
 template <typename H>
 int launch_attention(H* out, const H* qkv, uint32_t batch, uint32_t tokens, uint32_t heads, uint64_t qkv_ld,
@@ -95,7 +119,7 @@ enum OutKind {
     kOutHalfRows = 1,   // row-major half (f16 / bf16 per out_half_bf16)
     kOutF32Planar = 2,  // per image planar: [img][col][plane]
     kOutConvTF32 = 3,   // conv-transpose scatter into planar f32 [img][co][H*k][W*k]
-    kOutConvTHalf = 4,  // conv-transpose scatter into channels-last half [img][H*k][W*k][co]
+    kOutConvTHalf = 4,  // conv-transpose scatter into channels-last half [img][H*k][W*k][ldo]
     kOutHeadF32 = 5,    // kEpiHeadDot result, one f32 per row at out[row_remap]
 };
 

@@ -1,0 +1,980 @@
+// CUDA executor: the DINOv2 encoder (src/encoder.cpp:322-597) and the DPT
+// head (src/dpt.cpp:628-863) as a sequence of sm_100a kernels on one stream,
+// captured once per input shape into a CUDA graph.
+//
+// Layouts in HBM (per batch of B images, T = 1 + pw*ph tokens):
+//   residual stream  f32 [B*T, D]           (in-place LayerScale updates)
+//   GEMM activations int8 codes [rows, K] + f32 row scales   (int8 path)
+//                    f16 [rows, K]                            (fp16 path)
+//   QKV / attention  f16 [B*T, 3D] / [B*T, D]
+//   DPT feature maps channels-last f16 [B][h][w][Cp], Cp = channels rounded
+//                    up to 64 (zero pad) so the implicit-GEMM convolutions
+//                    can read 128-byte channel blocks with TMA
+//   depth            f32 [B][H][W]
+// Precision routing follows the reference (src/encoder.cpp:255-303,
+// src/dpt.cpp:479-535): in int8 mode the transformer linears, the patch
+// embedding, the DPT projections and resize layers use per-row int8
+// activations x per-output-channel int8 weights; attention and the DPT
+// refinement convolutions run with f16 operands (the reference's fp16
+// refinement precision); every accumulation is f32 / s32.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "executor.h"
+#include "image.h"
+#include "launch.h"
+#include "model_file.h"
+
+namespace dav2 {
+namespace {
+
+using namespace dav2cuda;
+
+void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) {
+        if (e == cudaErrorMemoryAllocation) throw std::bad_alloc();
+        throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+    }
+}
+
+void op(int rc, const char* what) {
+    if (rc != 0) throw std::runtime_error(std::string(what) + ": " + dav2cuda_last_error());
+}
+
+constexpr uint32_t up(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
+
+// True when `p` is page-locked host memory the copy engines can read directly.
+bool is_pinned(const void* p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+struct Arch {
+    uint32_t d, heads, blocks, taps[4], f, oc[4];
+};
+
+Arch arch_for(dav2_encoder e) {
+    switch (e) {
+        case DAV2_ENCODER_VITS: return {384, 6, 12, {2, 5, 8, 11}, 64, {48, 96, 192, 384}};
+        case DAV2_ENCODER_VITB: return {768, 12, 12, {2, 5, 8, 11}, 128, {96, 192, 384, 768}};
+        case DAV2_ENCODER_VITL: return {1024, 16, 24, {4, 11, 17, 23}, 256, {256, 512, 1024, 1024}};
+        default: throw std::invalid_argument("unsupported encoder");
+    }
+}
+
+// Device memory: one cudaMalloc per region, bump-allocated, 256-byte aligned.
+class Arena {
+public:
+    Arena() = default;
+    Arena(const Arena&) = delete;
+    Arena& operator=(const Arena&) = delete;
+    ~Arena() {
+        if (base_) cudaFree(base_);
+    }
+    void reserve(uint64_t bytes) {
+        cuda_check(cudaMalloc(&base_, bytes), "cudaMalloc");
+        cuda_check(cudaMemset(base_, 0, bytes), "cudaMemset");
+        cap_ = bytes;
+    }
+    template <typename T>
+    T* take(uint64_t bytes) {
+        const uint64_t at = (used_ + 255) & ~uint64_t(255);
+        if (base_ == nullptr) {  // sizing pass
+            used_ = at + bytes;
+            return nullptr;
+        }
+        if (at + bytes > cap_) throw std::runtime_error("arena overflow");
+        used_ = at + bytes;
+        return reinterpret_cast<T*>(static_cast<uint8_t*>(base_) + at);
+    }
+    uint64_t used() const { return used_; }
+    // Ends a sizing pass: the next reserve() makes take() hand out memory.
+    void rewind() { used_ = 0; }
+
+private:
+    void* base_ = nullptr;
+    uint64_t cap_ = 0, used_ = 0;
+};
+
+struct Linear {
+    void* w = nullptr;        // int8 codes [n][kp] or f16 [n][kp]
+    float* s = nullptr;       // int8 row scales [n]
+    const float* b = nullptr; // bias [n] (nullable)
+    uint32_t n = 0, kp = 0;
+};
+
+struct Block {
+    const float *ln1_w, *ln1_b, *ln2_w, *ln2_b, *ls1, *ls2;
+    Linear qkv, proj, fc1, fc2;
+};
+
+struct RefineNet {
+    Linear rcu[2][2];  // [unit][conv], f16 [F][9F]
+    Linear out;        // f16 [F][F]
+};
+
+class CudaExecutor final : public Executor {
+public:
+    CudaExecutor(const std::string& path, dav2_encoder encoder, int device, uint32_t flags)
+        : model_(path, encoder), encoder_(encoder), device_(device), arch_(arch_for(encoder)) {
+        int count = 0;
+        if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0)
+            throw std::runtime_error("no CUDA device is available");
+        if (device < 0 || device >= count) throw std::invalid_argument("CUDA device index out of range");
+        int8_ = (flags & DAV2_CREATE_FORCE_INT8) != 0;
+        cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+        cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+        model_.verify_crc();
+        load_weights();
+    }
+
+    ~CudaExecutor() override {
+        cudaSetDevice(device_);
+        for (auto& [k, p] : plans_)
+            if (p.graph) cudaGraphExecDestroy(p.graph);
+        plans_.clear();
+        if (staging_) cudaFree(staging_);
+        if (host_in_) cudaFreeHost(host_in_);
+        if (host_out_) cudaFreeHost(host_out_);
+        if (stream_) cudaStreamDestroy(stream_);
+    }
+
+    void prepare(int image_width, int image_height, int input_size) override {
+        const ImageShape s = network_shape(image_width, image_height, input_size);
+        std::lock_guard<std::mutex> lock(mutex_);
+        cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+        plan(1, s.width, s.height);
+    }
+
+    void infer(const float* chw, int w, int h, float* depth) override { infer_resized(chw, w, h, depth, w, h); }
+
+    void infer_resized(const float* chw, int w, int h, float* depth, int ow, int oh) override {
+        run_host_tensor(chw, 1, w, h, depth, ow, oh);
+    }
+
+    void infer_batch(const float* chw, int batch, int w, int h, float* depth) override {
+        run_host_tensor(chw, batch, w, h, depth, w, h);
+    }
+
+    void infer_bgr8(const uint8_t* bgr, int batch, int w, int h, std::ptrdiff_t row_stride,
+                    std::ptrdiff_t image_stride, int input_size, float* depth, bool device_memory,
+                    void* user_stream) override {
+        if (!bgr || !depth || batch <= 0 || w <= 0 || h <= 0 || row_stride < std::ptrdiff_t(w) * 3 ||
+            (batch > 1 && image_stride < row_stride * h))
+            throw std::invalid_argument("invalid source image");
+        const ImageShape s = network_shape(w, h, input_size);
+        std::lock_guard<std::mutex> lock(mutex_);
+        cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+        Plan& p = plan(batch, s.width, s.height);
+        cudaStream_t st = user_stream ? static_cast<cudaStream_t>(user_stream) : stream_;
+        const uint64_t img_bytes = uint64_t(image_stride > 0 ? image_stride : row_stride * h);
+        const uint64_t in_bytes = img_bytes * (batch - 1) + uint64_t(row_stride) * (h - 1) + uint64_t(w) * 3;
+        const uint8_t* dbgr = bgr;
+        const bool pinned_in = !device_memory && is_pinned(bgr);
+        const bool pinned_out = !device_memory && is_pinned(depth);
+        if (!device_memory) {
+            ensure_staging(in_bytes);
+            ensure_host(pinned_in ? 0 : in_bytes, pinned_out ? 0 : uint64_t(batch) * w * h * 4);
+            const void* src = bgr;
+            if (!pinned_in) {
+                std::memcpy(host_in_, bgr, in_bytes);
+                src = host_in_;
+            }
+            cuda_check(cudaMemcpyAsync(staging_, src, in_bytes, cudaMemcpyHostToDevice, st), "H2D");
+            upload_bytes_ += in_bytes;
+            dbgr = staging_;
+        }
+        op(launch_preprocess_bgr8(p.image, dbgr, batch, w, h, row_stride, img_bytes, s.width, s.height, 0, st),
+           "preprocess_bgr8");
+        ++launches_;
+        launch_plan(p, st);
+        float* result = p.depth;
+        if (w != s.width || h != s.height) {
+            float* resized = resized_buffer(uint64_t(batch) * w * h);
+            op(launch_bilinear_align<float, float>(resized, p.depth, s.width, s.height, w, h, batch, st),
+               "resize depth");
+            ++launches_;
+            result = resized;
+        }
+        const uint64_t out_bytes = uint64_t(batch) * w * h * 4;
+        if (device_memory) {
+            cuda_check(cudaMemcpyAsync(depth, result, out_bytes, cudaMemcpyDeviceToDevice, st), "D2D");
+            if (!user_stream) cuda_check(cudaStreamSynchronize(st), "sync");
+        } else {
+            cuda_check(cudaMemcpyAsync(pinned_out ? static_cast<void*>(depth) : host_out_, result, out_bytes,
+                                       cudaMemcpyDeviceToHost, st),
+                       "D2H");
+            cuda_check(cudaStreamSynchronize(st), "sync");
+            if (!pinned_out) std::memcpy(depth, host_out_, out_bytes);
+            download_bytes_ += out_bytes;
+        }
+        check_device_error();
+    }
+
+    uint64_t kernel_launches() const override { return launches_; }
+    std::string profile_json(int batch, int w, int h) override { return profile(batch, w, h); }
+
+    void synchronize() override {
+        cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+        cuda_check(cudaStreamSynchronize(stream_), "sync");
+        check_device_error();
+    }
+
+    GpuCapabilities gpu_capabilities() const override {
+        GpuCapabilities c;
+        c.flags = DAV2_GPU_CAP_NO_HOST_PIXEL_STAGING | DAV2_GPU_CAP_NO_HOST_DEPTH_STAGING;
+        c.maximum_in_flight_jobs = 1;
+        return c;
+    }
+
+    void transfer_counters(uint64_t& up_bytes, uint64_t& down_bytes) const override {
+        up_bytes = upload_bytes_;
+        down_bytes = download_bytes_;
+    }
+
+    dav2_encoder encoder() const override { return encoder_; }
+    float metric_max_depth() const override { return model_.metric_max_depth(); }
+
+private:
+    // ------------------------------------------------------------ weights
+    const TensorView& t(const std::string& name) const { return model_.tensor(name); }
+
+    const float* f32(const std::string& name) {
+        const TensorView& v = t(name);
+        float* d = wa_.take<float>(v.elements * 4);
+        if (d) cuda_check(cudaMemcpy(d, v.data, v.elements * 4, cudaMemcpyHostToDevice), "upload");
+        return d;
+    }
+
+    // Uploads a float tensor to the staging buffer (weights pass only).
+    const float* stage(const std::string& name) {
+        const TensorView& v = t(name);
+        if (!wa_used_pass_) return nullptr;
+        cuda_check(cudaMemcpy(wstage_, v.data, v.elements * 4, cudaMemcpyHostToDevice), "upload");
+        return wstage_;
+    }
+
+    // kind: 0 plain [n][K]; 1 conv-transpose; 2 conv (ky,kx,c) with cip
+    Linear make_linear(const std::string& wname, const std::string& bname, bool int8, int kind, uint32_t n,
+                       uint32_t K, uint32_t kp, uint32_t co = 0, uint32_t k = 0, uint32_t ci = 0, uint32_t cip = 0) {
+        Linear L;
+        L.n = n;
+        L.kp = kp;
+        if (int8) {
+            L.w = wa_.take<uint8_t>(uint64_t(n) * kp);
+            L.s = wa_.take<float>(uint64_t(n) * 4);
+        } else {
+            L.w = wa_.take<__half>(uint64_t(n) * kp * 2);
+        }
+        if (!bname.empty()) L.b = kind == 1 ? wa_.take<float>(uint64_t(n) * 4) : f32(bname);
+        const float* src = stage(wname);
+        if (src) {
+            if (int8)
+                op(launch_pack_weight_s8(static_cast<uint8_t*>(L.w), L.s, src, kind, n, K, kp, co, k, ci, nullptr),
+                   "pack_weight_s8");
+            else
+                op(launch_half_weight<__half>(static_cast<__half*>(L.w), src, kind, n, K, kp, co, k, ci, cip,
+                                              nullptr),
+                   "half_weight");
+            if (kind == 1 && L.b) {
+                const float* b = f32(bname);
+                op(launch_expand_bias(const_cast<float*>(L.b), b, co, k * k, nullptr), "expand_bias");
+            }
+            cuda_check(cudaDeviceSynchronize(), "weight prep");
+        } else if (kind == 1 && L.b) {
+            f32(bname);  // sizing of the per-channel bias
+        }
+        return L;
+    }
+
+    void build_weights() {
+        const Arch& a = arch_;
+        const bool q = int8_;
+        cls_ = f32("pretrained.cls_token");
+        pos_ = f32("pretrained.pos_embed");
+        patch_ = make_linear("pretrained.patch_embed.proj.weight", "pretrained.patch_embed.proj.bias", q, 0, a.d, 588,
+                             592);
+        norm_w_ = f32("pretrained.norm.weight");
+        norm_b_ = f32("pretrained.norm.bias");
+        blocks_.resize(a.blocks);
+        for (uint32_t i = 0; i < a.blocks; ++i) {
+            const std::string p = "pretrained.blocks." + std::to_string(i);
+            Block& b = blocks_[i];
+            b.ln1_w = f32(p + ".norm1.weight");
+            b.ln1_b = f32(p + ".norm1.bias");
+            b.ln2_w = f32(p + ".norm2.weight");
+            b.ln2_b = f32(p + ".norm2.bias");
+            b.ls1 = f32(p + ".ls1.gamma");
+            b.ls2 = f32(p + ".ls2.gamma");
+            b.qkv = make_linear(p + ".attn.qkv.weight", p + ".attn.qkv.bias", q, 0, 3 * a.d, a.d, a.d);
+            b.proj = make_linear(p + ".attn.proj.weight", p + ".attn.proj.bias", q, 0, a.d, a.d, a.d);
+            b.fc1 = make_linear(p + ".mlp.fc1.weight", p + ".mlp.fc1.bias", q, 0, 4 * a.d, a.d, a.d);
+            b.fc2 = make_linear(p + ".mlp.fc2.weight", p + ".mlp.fc2.bias", q, 0, a.d, 4 * a.d, 4 * a.d);
+        }
+        const std::string h = "depth_head.";
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t oc = a.oc[i];
+            cp_[i] = up(oc, 64);
+            projects_[i] = make_linear(h + "projects." + std::to_string(i) + ".weight",
+                                       h + "projects." + std::to_string(i) + ".bias", q, 0, oc, a.d, a.d);
+        }
+        for (int i = 0; i < 2; ++i) {
+            const uint32_t oc = a.oc[i], k = i == 0 ? 4 : 2;
+            const std::string r = h + "resize_layers." + std::to_string(i);
+            resize_[i] = make_linear(r + ".weight", r + ".bias", q, 1, k * k * oc, oc, q ? up(oc, 16) : cp_[i], oc, k,
+                                     oc);
+        }
+        {
+            const uint32_t oc = a.oc[3];
+            const std::string r = h + "resize_layers.3";
+            resize_[3] = q ? make_linear(r + ".weight", r + ".bias", true, 2, oc, 9 * oc, 9 * oc, oc, 3, oc)
+                           : make_linear(r + ".weight", r + ".bias", false, 2, oc, 9 * oc, 9 * cp_[3], oc, 3, oc, cp_[3]);
+        }
+        const uint32_t F = a.f;
+        for (int i = 0; i < 4; ++i)
+            layer_rn_[i] = make_linear(h + "scratch.layer" + std::to_string(i + 1) + "_rn.weight", "", false, 2, F,
+                                       9 * a.oc[i], 9 * cp_[i], F, 3, a.oc[i], cp_[i]);
+        for (int i = 0; i < 4; ++i) {
+            const std::string r = h + "scratch.refinenet" + std::to_string(i + 1);
+            for (int u = 0; u < 2; ++u)
+                for (int c = 0; c < 2; ++c) {
+                    const std::string n = r + ".resConfUnit" + std::to_string(u + 1) + ".conv" + std::to_string(c + 1);
+                    refine_[i].rcu[u][c] = make_linear(n + ".weight", n + ".bias", false, 2, F, 9 * F, 9 * F, F, 3, F, F);
+                }
+            refine_[i].out = make_linear(r + ".out_conv.weight", r + ".out_conv.bias", false, 0, F, F, F);
+        }
+        half_f_ = F / 2;
+        cp_half_ = up(F / 2, 64);
+        out_conv1_ = make_linear(h + "scratch.output_conv1.weight", h + "scratch.output_conv1.bias", false, 2, F / 2,
+                                 9 * F, 9 * F, F / 2, 3, F, F);
+        out_conv2_ = make_linear(h + "scratch.output_conv2.0.weight", h + "scratch.output_conv2.0.bias", false, 2, 32,
+                                 9 * (F / 2), 9 * cp_half_, 32, 3, F / 2, cp_half_);
+        head_w_ = f32(h + "scratch.output_conv2.2.weight");
+        head_b_ = t(h + "scratch.output_conv2.2.bias").data[0];
+    }
+
+    void load_weights() {
+        // pass 1 sizes the arena, pass 2 fills it
+        uint64_t largest = 0;
+        for (auto n : model_.names()) largest = std::max<uint64_t>(largest, model_.tensor(n).elements * 4);
+        wa_used_pass_ = false;
+        build_weights();
+        const uint64_t need = wa_.used() + 4096;
+        wa_.rewind();
+        wa_.reserve(need);
+        cuda_check(cudaMalloc(&wstage_, largest), "cudaMalloc staging");
+        wa_used_pass_ = true;
+        build_weights();
+        cudaFree(wstage_);
+        wstage_ = nullptr;
+        cuda_check(cudaDeviceSynchronize(), "weights");
+    }
+
+    // --------------------------------------------------------------- plans
+    struct Plan {
+        uint32_t B = 0, W = 0, H = 0, pw = 0, ph = 0, hw = 0, T = 0;
+        std::unique_ptr<Arena> arena;
+        float* image = nullptr;   // [B][3][H][W]
+        float* depth = nullptr;   // [B][H][W]
+        float* pos = nullptr;     // [hw][D]
+        void* patch_a = nullptr;  // int8 [B*hw][592] or f16
+        float* patch_s = nullptr;
+        float* x = nullptr;
+        void* xn = nullptr;
+        float* xn_s = nullptr;
+        __half* qkv = nullptr;
+        __half* att = nullptr;
+        void* att_q = nullptr;
+        float* att_s = nullptr;
+        __half* hid = nullptr;
+        void* hid_q = nullptr;
+        float* hid_s = nullptr;
+        void* taps[4] = {};
+        float* taps_s[4] = {};
+        __half* proj[4] = {};
+        void* ct_q[2] = {};
+        float* ct_s[2] = {};
+        __half* layer[4] = {};
+        void* r3_col = nullptr;
+        float* r3_s = nullptr;
+        uint32_t lh[4] = {}, lw[4] = {};
+        __half *rn[4] = {}, *rn_relu[4] = {};
+        __half *t = nullptr, *y = nullptr, *pth = nullptr, *pth_relu = nullptr, *upb = nullptr;
+        __half *path[2] = {};
+        __half *oc1 = nullptr, *full = nullptr;
+        cudaGraphExec_t graph = nullptr;
+        uint64_t kernels = 0;  // kernel nodes in the captured graph
+    };
+
+    void alloc(Plan& p, Arena& A) {
+        const Arch& a = arch_;
+        const uint64_t B = p.B, R = B * p.T, PH = B * p.hw, D = a.d, F = a.f;
+        const bool q = int8_;
+        p.image = A.take<float>(B * 3 * p.H * p.W * 4);
+        p.depth = A.take<float>(B * p.H * p.W * 4);
+        p.pos = A.take<float>(uint64_t(p.hw) * D * 4);
+        p.patch_a = A.take<uint8_t>(PH * 592 * (q ? 1 : 2));
+        if (q) p.patch_s = A.take<float>(PH * 4);
+        p.x = A.take<float>(R * D * 4);
+        p.xn = A.take<uint8_t>(R * D * (q ? 1 : 2));
+        if (q) p.xn_s = A.take<float>(R * 4);
+        p.qkv = A.take<__half>(R * 3 * D * 2);
+        p.att = A.take<__half>(R * D * 2);
+        if (q) {
+            p.att_q = A.take<uint8_t>(R * D);
+            p.att_s = A.take<float>(R * 4);
+        }
+        p.hid = A.take<__half>(R * 4 * D * 2);
+        if (q) {
+            p.hid_q = A.take<uint8_t>(R * 4 * D);
+            p.hid_s = A.take<float>(R * 4);
+        }
+        for (int i = 0; i < 4; ++i) {
+            p.taps[i] = A.take<uint8_t>(PH * D * (q ? 1 : 2));
+            if (q) p.taps_s[i] = A.take<float>(PH * 4);
+            p.proj[i] = A.take<__half>(PH * cp_[i] * 2);
+        }
+        for (int i = 0; i < 2; ++i) {
+            const uint32_t k = i == 0 ? 4 : 2;
+            if (q) {
+                p.ct_q[i] = A.take<uint8_t>(PH * up(a.oc[i], 16));
+                p.ct_s[i] = A.take<float>(PH * 4);
+            }
+            p.lh[i] = p.ph * k;
+            p.lw[i] = p.pw * k;
+            p.layer[i] = A.take<__half>(B * p.lh[i] * p.lw[i] * cp_[i] * 2);
+        }
+        p.lh[2] = p.ph;
+        p.lw[2] = p.pw;
+        p.layer[2] = p.proj[2];
+        p.lh[3] = (p.ph - 1) / 2 + 1;
+        p.lw[3] = (p.pw - 1) / 2 + 1;
+        p.layer[3] = A.take<__half>(B * p.lh[3] * p.lw[3] * cp_[3] * 2);
+        const uint64_t r3rows = B * p.lh[3] * p.lw[3];
+        if (q) {
+            p.r3_col = A.take<uint8_t>(r3rows * 9 * a.oc[3]);
+            p.r3_s = A.take<float>(r3rows * 4);
+        } else {
+            p.r3_col = A.take<__half>(r3rows * 9 * cp_[3] * 2);
+        }
+        for (int i = 0; i < 4; ++i) {
+            const uint64_t n = B * p.lh[i] * p.lw[i] * F * 2;
+            p.rn[i] = A.take<__half>(n);
+            p.rn_relu[i] = A.take<__half>(n);
+        }
+        const uint64_t big = B * p.lh[0] * p.lw[0] * F * 2;  // largest RCU scale
+        p.t = A.take<__half>(big);
+        p.y = A.take<__half>(big);
+        p.pth = A.take<__half>(big);
+        p.pth_relu = A.take<__half>(big);
+        p.upb = A.take<__half>(4 * big);
+        p.path[0] = A.take<__half>(4 * big);
+        p.path[1] = A.take<__half>(4 * big);
+        p.oc1 = A.take<__half>(B * 4 * p.lh[0] * p.lw[0] * cp_half_ * 2);
+        p.full = A.take<__half>(B * p.H * p.W * cp_half_ * 2);
+    }
+
+    Plan& plan(int batch, int w, int h) {
+        if (w <= 0 || h <= 0 || w % 14 || h % 14)
+            throw std::invalid_argument("network dimensions must be positive multiples of 14");
+        const auto key = std::make_tuple(batch, w, h);
+        auto it = plans_.find(key);
+        if (it != plans_.end()) return it->second;
+        Plan& p = plans_[key];
+        p.B = batch;
+        p.W = w;
+        p.H = h;
+        p.pw = w / 14;
+        p.ph = h / 14;
+        p.hw = p.pw * p.ph;
+        p.T = p.hw + 1;
+        Arena sizing;
+        alloc(p, sizing);
+        p.arena = std::make_unique<Arena>();
+        p.arena->reserve(sizing.used() + 4096);
+        alloc(p, *p.arena);
+        op(launch_position_bicubic(p.pos, pos_, arch_.d, p.pw, p.ph, stream_), "position_bicubic");
+        // warm-up run (sets kernel attributes), then capture
+        enqueue(p, stream_);
+        cuda_check(cudaStreamSynchronize(stream_), "warm-up");
+        check_device_error();
+        cudaGraph_t g = nullptr;
+        cuda_check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "capture");
+        try {
+            enqueue(p, stream_);
+        } catch (...) {
+            cudaStreamEndCapture(stream_, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+        }
+        cuda_check(cudaStreamEndCapture(stream_, &g), "end capture");
+        size_t nodes = 0;
+        cuda_check(cudaGraphGetNodes(g, nullptr, &nodes), "graph nodes");
+        p.kernels = nodes;
+        cuda_check(cudaGraphInstantiate(&p.graph, g, 0), "instantiate");
+        cudaGraphDestroy(g);
+        return p;
+    }
+
+    // Launch bookkeeping: in profiling mode every launch is followed by an
+    // event on the launching stream (the analogue of DAV2_VULKAN_PROFILE=1,
+    // src/vulkan.cpp:628-644), giving per-operation device durations.
+    void step(cudaStream_t st, int rc, const char* name) {
+        op(rc, name);
+        if (profiling_) {
+            cudaEvent_t e;
+            cuda_check(cudaEventCreate(&e), "event");
+            cuda_check(cudaEventRecord(e, st), "event record");
+            marks_.push_back({name, e});
+        }
+    }
+
+public:
+    std::string profile(int batch, int w, int h) {
+        std::lock_guard<std::mutex> lock(mutex_);
+        cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+        Plan& p = plan(batch, w, h);
+        cudaEvent_t start;
+        cuda_check(cudaEventCreate(&start), "event");
+        marks_.clear();
+        cuda_check(cudaStreamSynchronize(stream_), "sync");
+        cuda_check(cudaEventRecord(start, stream_), "event record");
+        profiling_ = true;
+        try {
+            enqueue(p, stream_);
+        } catch (...) {
+            profiling_ = false;
+            throw;
+        }
+        profiling_ = false;
+        cuda_check(cudaStreamSynchronize(stream_), "sync");
+        check_device_error();
+        std::string out = "{\"batch\": " + std::to_string(batch) + ", \"width\": " + std::to_string(w) +
+                          ", \"height\": " + std::to_string(h) + ", \"ops\": [";
+        cudaEvent_t prev = start;
+        float total = 0.f;
+        for (size_t i = 0; i < marks_.size(); ++i) {
+            float ms = 0.f;
+            cuda_check(cudaEventElapsedTime(&ms, prev, marks_[i].second), "elapsed");
+            total += ms;
+            char buf[160];
+            snprintf(buf, sizeof buf, "%s{\"name\": \"%s\", \"ms\": %.6f}", i ? ", " : "", marks_[i].first, ms);
+            out += buf;
+            if (prev != start) cudaEventDestroy(prev);
+            prev = marks_[i].second;
+        }
+        if (prev != start) cudaEventDestroy(prev);
+        cudaEventDestroy(start);
+        marks_.clear();
+        char tail[64];
+        snprintf(tail, sizeof tail, "], \"total_ms\": %.6f}", total);
+        return out + tail;
+    }
+
+private:
+    void launch_plan(Plan& p, cudaStream_t st) {
+        cuda_check(cudaGraphLaunch(p.graph, st), "graph launch");
+        launches_ += p.kernels;
+    }
+
+    // ---------------------------------------------------------- the graph
+    GemmArgs gemm(const Linear& L, const void* a, uint64_t lda, uint32_t m, bool int8_operands) const {
+        GemmArgs g;
+        g.elem = int8_operands ? kElemS8 : kElemF16;
+        g.a = a;
+        g.lda = lda;
+        g.b = L.w;
+        g.ldb = L.kp;
+        g.m = m;
+        g.n = L.n;
+        g.k = L.kp;
+        g.bias = L.b;
+        g.flags = L.b ? kEpiBias : 0u;
+        if (int8_operands) {
+            g.flags |= kEpiDequant;
+            g.s_w = L.s;
+        }
+        return g;
+    }
+
+    GemmArgs conv3x3(const Linear& L, const __half* in, uint32_t B, uint32_t h, uint32_t w, uint32_t c) const {
+        GemmArgs g = gemm(L, in, 0, B * h * w, false);
+        g.a_mode = kAModeConv3x3;
+        g.conv_batch = B;
+        g.conv_h = h;
+        g.conv_w = w;
+        g.conv_c = c;
+        return g;
+    }
+
+    void enqueue(Plan& p, cudaStream_t st) {
+        const Arch& a = arch_;
+        const bool q = int8_;
+        const uint32_t B = p.B, D = a.d, F = a.f;
+        const uint32_t R = B * p.T, PH = B * p.hw;
+
+        // ---- patch embedding + cls + positions (src/operators.cpp:1211-1406)
+        step(st, launch_fill_tokens(p.x, cls_, pos_, p.pos, D, p.T, B, st), "fill_tokens");
+        if (q)
+            step(st, launch_im2col_quantize(static_cast<uint32_t*>(p.patch_a), p.patch_s, p.image, B, p.W, p.H, 3, p.pw,
+                                      p.ph, 14, 14, 0, 592 / 4, st),
+               "patch im2col_quantize");
+        else
+            step(st, launch_patch_im2col<__half>(static_cast<__half*>(p.patch_a), p.image, B, p.H, p.W, 592, st),
+               "patch im2col");
+        {
+            GemmArgs g = gemm(patch_, p.patch_a, 592, PH, q);
+            g.s_in = p.patch_s;
+            g.flags |= kEpiResidual1;
+            g.res1 = p.x;
+            g.out = p.x;
+            g.out_kind = kOutF32Rows;
+            g.ldo = D;
+            g.rows_per_img = p.hw;
+            g.out_rows_per_img = p.T;
+            g.row_offset = 1;
+            step(st, launch_gemm(g, st), "patch gemm");
+        }
+        // ---- transformer blocks (src/encoder.cpp:426-591)
+        int tap = 0;
+        for (uint32_t i = 0; i < a.blocks; ++i) {
+            const Block& b = blocks_[i];
+            step(st, launch_layer_norm(p.xn, p.xn_s, p.x, b.ln1_w, b.ln1_b, R, D, 1e-6f, q ? kLnOutS8 : kLnOutF16, 1, 1, 0,
+                                 st),
+               "ln1");
+            {
+                GemmArgs g = gemm(b.qkv, p.xn, D, R, q);
+                g.s_in = p.xn_s;
+                g.out = p.qkv;
+                g.out_kind = kOutHalfRows;
+                g.ldo = 3 * D;
+                step(st, launch_gemm(g, st), "qkv");
+            }
+            step(st, launch_attention<__half>(p.att, p.qkv, B, p.T, a.heads, 3 * D, D, st), "attention");
+            const void* att_in = p.att;
+            if (q) {
+                step(st, launch_quantize_rows<__half>(static_cast<uint32_t*>(p.att_q), p.att_s, p.att, R, D, 0, R, 0, D,
+                                                D / 4, st),
+                   "quantize attention");
+                att_in = p.att_q;
+            }
+            {
+                GemmArgs g = gemm(b.proj, att_in, D, R, q);
+                g.s_in = p.att_s;
+                g.flags |= kEpiLayerScale;
+                g.gamma = b.ls1;
+                g.res1 = p.x;
+                g.out = p.x;
+                g.out_kind = kOutF32Rows;
+                g.ldo = D;
+                step(st, launch_gemm(g, st), "proj");
+            }
+            step(st, launch_layer_norm(p.xn, p.xn_s, p.x, b.ln2_w, b.ln2_b, R, D, 1e-6f, q ? kLnOutS8 : kLnOutF16, 1, 1, 0,
+                                 st),
+               "ln2");
+            {
+                GemmArgs g = gemm(b.fc1, p.xn, D, R, q);
+                g.s_in = p.xn_s;
+                g.flags |= kEpiGelu;
+                g.out = p.hid;
+                g.out_kind = kOutHalfRows;
+                g.ldo = 4 * D;
+                step(st, launch_gemm(g, st), "fc1");
+            }
+            const void* hid_in = p.hid;
+            if (q) {
+                step(st, launch_quantize_rows<__half>(static_cast<uint32_t*>(p.hid_q), p.hid_s, p.hid, R, 4 * D, 0, R, 0,
+                                                4 * D, D, st),
+                   "quantize hidden");
+                hid_in = p.hid_q;
+            }
+            {
+                GemmArgs g = gemm(b.fc2, hid_in, 4 * D, R, q);
+                g.s_in = p.hid_s;
+                g.flags |= kEpiLayerScale;
+                g.gamma = b.ls2;
+                g.res1 = p.x;
+                g.out = p.x;
+                g.out_kind = kOutF32Rows;
+                g.ldo = D;
+                step(st, launch_gemm(g, st), "fc2");
+            }
+            if (tap < 4 && i == a.taps[tap]) {
+                // pretrained.norm on the patch rows only (cls dropped)
+                step(st, launch_layer_norm(p.taps[tap], p.taps_s[tap], p.x, norm_w_, norm_b_, PH, D, 1e-6f,
+                                     q ? kLnOutS8 : kLnOutF16, p.hw, p.T, 1, st),
+                   "tap norm");
+                ++tap;
+            }
+        }
+        // ---- DPT projections and resize layers (src/dpt.cpp:641-731)
+        for (int i = 0; i < 4; ++i) {
+            GemmArgs g = gemm(projects_[i], p.taps[i], D, PH, q);
+            g.s_in = p.taps_s[i];
+            g.out = p.proj[i];
+            g.out_kind = kOutHalfRows;
+            g.ldo = cp_[i];
+            step(st, launch_gemm(g, st), "project");
+        }
+        for (int i = 0; i < 2; ++i) {
+            const uint32_t k = i == 0 ? 4 : 2, oc = a.oc[i];
+            GemmArgs g;
+            if (q) {
+                const uint32_t kp = up(oc, 16);
+                step(st, launch_quantize_rows<__half>(static_cast<uint32_t*>(p.ct_q[i]), p.ct_s[i], p.proj[i], PH, oc, 0,
+                                                PH, 0, cp_[i], kp / 4, st),
+                   "quantize convT input");
+                g = gemm(resize_[i], p.ct_q[i], kp, PH, true);
+                g.s_in = p.ct_s[i];
+            } else {
+                g = gemm(resize_[i], p.proj[i], cp_[i], PH, false);
+            }
+            g.out = p.layer[i];
+            g.out_kind = kOutConvTHalf;
+            g.ldo = cp_[i];
+            g.convt_k = k;
+            g.convt_cout = oc;
+            g.convt_w = p.pw;
+            g.convt_h = p.ph;
+            step(st, launch_gemm(g, st), "conv transpose");
+        }
+        {
+            const uint32_t oc = a.oc[3], rows = B * p.lh[3] * p.lw[3];
+            GemmArgs g;
+            if (q) {
+                step(st, launch_im2col_quantize_nhwc<__half>(static_cast<uint8_t*>(p.r3_col), p.r3_s, p.proj[3], B, p.ph,
+                                                       p.pw, oc, cp_[3], 3, 2, 1, p.lh[3], p.lw[3], 9 * oc, st),
+                   "resize3 im2col_quantize");
+                g = gemm(resize_[3], p.r3_col, 9 * oc, rows, true);
+                g.s_in = p.r3_s;
+            } else {
+                step(st, launch_im2col_nhwc<__half>(static_cast<__half*>(p.r3_col), p.proj[3], B, p.ph, p.pw, cp_[3], 3, 2, 1,
+                                              p.lh[3], p.lw[3], 9 * cp_[3], st),
+                   "resize3 im2col");
+                g = gemm(resize_[3], p.r3_col, 9 * cp_[3], rows, false);
+            }
+            g.out = p.layer[3];
+            g.out_kind = kOutHalfRows;
+            g.ldo = cp_[3];
+            step(st, launch_gemm(g, st), "resize3");
+        }
+        // ---- scratch.layerN_rn (3x3, no bias) with a ReLU copy for the RCUs
+        for (int i = 0; i < 4; ++i) {
+            GemmArgs g = conv3x3(layer_rn_[i], p.layer[i], B, p.lh[i], p.lw[i], cp_[i]);
+            g.out = p.rn[i];
+            g.out2 = p.rn_relu[i];
+            g.flags |= kEpiReluCopy;
+            g.out_kind = kOutHalfRows;
+            g.ldo = F;
+            step(st, launch_gemm(g, st), "layer_rn");
+        }
+        // ---- refinenets (src/dpt.cpp:537-615, 759-790)
+        const __half* path = nullptr;
+        int pi = 0;
+        for (int r = 3; r >= 0; --r) {
+            const RefineNet& rf = refine_[r];
+            const uint32_t h = p.lh[r], w = p.lw[r];
+            const __half* x = p.rn[r];
+            const __half* xr = p.rn_relu[r];
+            if (path) {
+                // RCU1 on the skip, fused with the fusion add: p' = path + (conv2(...) + skip)
+                GemmArgs g1 = conv3x3(rf.rcu[0][0], xr, B, h, w, F);
+                g1.flags |= kEpiRelu;
+                g1.out = p.t;
+                g1.out_kind = kOutHalfRows;
+                g1.ldo = F;
+                step(st, launch_gemm(g1, st), "rcu1.conv1");
+                GemmArgs g2 = conv3x3(rf.rcu[0][1], p.t, B, h, w, F);
+                g2.flags |= kEpiResidual1 | kEpiResidual2 | kEpiReluCopy;
+                g2.res1 = x;
+                g2.res2 = path;
+                g2.out = p.pth;
+                g2.out2 = p.pth_relu;
+                g2.out_kind = kOutHalfRows;
+                g2.ldo = F;
+                step(st, launch_gemm(g2, st), "rcu1.conv2");
+                x = p.pth;
+                xr = p.pth_relu;
+            }
+            GemmArgs g3 = conv3x3(rf.rcu[1][0], xr, B, h, w, F);
+            g3.flags |= kEpiRelu;
+            g3.out = p.t;
+            g3.out_kind = kOutHalfRows;
+            g3.ldo = F;
+            step(st, launch_gemm(g3, st), "rcu2.conv1");
+            GemmArgs g4 = conv3x3(rf.rcu[1][1], p.t, B, h, w, F);
+            g4.flags |= kEpiResidual1;
+            g4.res1 = x;
+            g4.out = p.y;
+            g4.out_kind = kOutHalfRows;
+            g4.ldo = F;
+            step(st, launch_gemm(g4, st), "rcu2.conv2");
+            const uint32_t oh = r > 0 ? p.lh[r - 1] : 2 * p.lh[0];
+            const uint32_t ow = r > 0 ? p.lw[r - 1] : 2 * p.lw[0];
+            step(st, launch_bilinear_nhwc<__half>(p.upb, p.y, B, h, w, oh, ow, F, st), "fusion resize");
+            GemmArgs g5 = gemm(rf.out, p.upb, F, B * oh * ow, false);
+            g5.out = p.path[pi];
+            g5.out_kind = kOutHalfRows;
+            g5.ldo = F;
+            step(st, launch_gemm(g5, st), "out_conv");
+            path = p.path[pi];
+            pi ^= 1;
+        }
+        // ---- output head (src/dpt.cpp:813-854)
+        const uint32_t h1 = 2 * p.lh[0], w1 = 2 * p.lw[0];
+        {
+            GemmArgs g = conv3x3(out_conv1_, path, B, h1, w1, F);
+            g.out = p.oc1;
+            g.out_kind = kOutHalfRows;
+            g.ldo = cp_half_;
+            step(st, launch_gemm(g, st), "output_conv1");
+        }
+        step(st, launch_bilinear_nhwc<__half>(p.full, p.oc1, B, h1, w1, p.H, p.W, cp_half_, st), "head resize");
+        {
+            GemmArgs g = conv3x3(out_conv2_, p.full, B, p.H, p.W, cp_half_);
+            g.flags |= kEpiHeadDot | (model_.metric_max_depth() > 0 ? kEpiMetricHead : 0u);
+            g.head_w = head_w_;
+            g.head_b = head_b_;
+            g.head_max_depth = model_.metric_max_depth();
+            g.out = p.depth;
+            g.out_kind = kOutHeadF32;
+            step(st, launch_gemm(g, st), "output_conv2");
+        }
+    }
+
+    void run_host_tensor(const float* chw, int batch, int w, int h, float* depth, int ow, int oh) {
+        if (!chw || !depth || batch <= 0) throw std::invalid_argument("null inference argument");
+        std::lock_guard<std::mutex> lock(mutex_);
+        cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+        Plan& p = plan(batch, w, h);
+        const uint64_t in_bytes = uint64_t(batch) * 3 * w * h * 4;
+        const uint64_t out_bytes = uint64_t(batch) * ow * oh * 4;
+        ensure_host(in_bytes, out_bytes);
+        std::memcpy(host_in_, chw, in_bytes);
+        cuda_check(cudaMemcpyAsync(p.image, host_in_, in_bytes, cudaMemcpyHostToDevice, stream_), "H2D");
+        upload_bytes_ += in_bytes;
+        launch_plan(p, stream_);
+        float* result = p.depth;
+        if (ow != w || oh != h) {
+            float* resized = resized_buffer(uint64_t(batch) * ow * oh);
+            op(launch_bilinear_align<float, float>(resized, p.depth, w, h, ow, oh, batch, stream_), "resize depth");
+            ++launches_;
+            result = resized;
+        }
+        cuda_check(cudaMemcpyAsync(host_out_, result, out_bytes, cudaMemcpyDeviceToHost, stream_), "D2H");
+        cuda_check(cudaStreamSynchronize(stream_), "sync");
+        std::memcpy(depth, host_out_, out_bytes);
+        download_bytes_ += out_bytes;
+        check_device_error();
+    }
+
+    void ensure_host(uint64_t in, uint64_t out) {
+        if (in > host_in_cap_) {
+            if (host_in_) cudaFreeHost(host_in_);
+            cuda_check(cudaMallocHost(&host_in_, in), "cudaMallocHost");
+            host_in_cap_ = in;
+        }
+        if (out > host_out_cap_) {
+            if (host_out_) cudaFreeHost(host_out_);
+            cuda_check(cudaMallocHost(&host_out_, out), "cudaMallocHost");
+            host_out_cap_ = out;
+        }
+    }
+
+    void ensure_staging(uint64_t bytes) {
+        if (bytes > staging_cap_) {
+            if (staging_) cudaFree(staging_);
+            cuda_check(cudaMalloc(&staging_, bytes), "cudaMalloc");
+            staging_cap_ = bytes;
+        }
+    }
+
+    float* resized_buffer(uint64_t n) {
+        if (n * 4 > resized_cap_) {
+            resized_.reset();
+            resized_ = std::make_unique<Arena>();
+            resized_->reserve(n * 4 + 256);
+            resized_cap_ = n * 4;
+            resized_ptr_ = resized_->take<float>(n * 4);
+        }
+        return resized_ptr_;
+    }
+
+    void check_device_error() {
+        int* word = device_error_word();
+        int value = 0;
+        if (word && cudaMemcpy(&value, word, sizeof value, cudaMemcpyDeviceToHost) == cudaSuccess && value != 0) {
+            const int zero = 0;
+            cudaMemcpy(word, &zero, sizeof zero, cudaMemcpyHostToDevice);
+            throw std::runtime_error("a kernel pipeline wait timed out on the device");
+        }
+    }
+
+    ModelFile model_;
+    dav2_encoder encoder_;
+    int device_;
+    Arch arch_;
+    bool int8_ = false;
+    cudaStream_t stream_ = nullptr;
+    std::mutex mutex_;
+
+    Arena wa_;
+    bool wa_used_pass_ = false;
+    float* wstage_ = nullptr;
+    const float *cls_ = nullptr, *pos_ = nullptr, *norm_w_ = nullptr, *norm_b_ = nullptr, *head_w_ = nullptr;
+    float head_b_ = 0.f;
+    Linear patch_;
+    std::vector<Block> blocks_;
+    Linear projects_[4], resize_[4], layer_rn_[4];
+    RefineNet refine_[4];
+    Linear out_conv1_, out_conv2_;
+    uint32_t cp_[4] = {}, half_f_ = 0, cp_half_ = 0;
+
+    std::map<std::tuple<int, int, int>, Plan> plans_;
+    uint8_t* staging_ = nullptr;
+    uint64_t staging_cap_ = 0;
+    void* host_in_ = nullptr;
+    void* host_out_ = nullptr;
+    uint64_t host_in_cap_ = 0, host_out_cap_ = 0;
+    std::unique_ptr<Arena> resized_;
+    uint64_t resized_cap_ = 0;
+    float* resized_ptr_ = nullptr;
+    uint64_t upload_bytes_ = 0, download_bytes_ = 0;
+    uint64_t launches_ = 0;
+    bool profiling_ = false;
+    std::vector<std::pair<const char*, cudaEvent_t>> marks_;
+};
+
+}  // namespace
+
+std::unique_ptr<Executor> create_executor(const std::string& model_path, dav2_encoder encoder, int device_index,
+                                          std::uint32_t flags, const std::string& cache_path) {
+    (void)cache_path;
+    if ((flags & DAV2_CREATE_FORCE_METAL) && (flags & DAV2_CREATE_FORCE_VULKAN))
+        throw std::invalid_argument("Metal and Vulkan cannot both be forced");
+    return std::make_unique<CudaExecutor>(model_path, encoder, device_index, flags);
+}
+
+GpuCapabilities probe_gpu_capabilities(int device_index) {
+    GpuCapabilities c;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) == cudaSuccess && device_index >= 0 && device_index < count) {
+        c.flags = DAV2_GPU_CAP_NO_HOST_PIXEL_STAGING | DAV2_GPU_CAP_NO_HOST_DEPTH_STAGING;
+        c.maximum_in_flight_jobs = 1;
+    }
+    return c;
+}
+
+}  // namespace dav2

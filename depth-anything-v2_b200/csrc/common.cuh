@@ -70,6 +70,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     const unsigned long long start = globaltimer();
     for (uint32_t spin = 1;; ++spin) {
         if (mbar_try_wait(a, parity)) return true;
+        if (spin > 8) __nanosleep(32);  // back off: leave issue slots to working warps
         if ((spin & 255u) == 0) {
             if (*abort) return false;
             if (globaltimer() - start > kWaitTimeoutNs) {

@@ -9,16 +9,18 @@
 // offset (kx-1, ky-1) — the tensor-memory-access unit zero-fills the halo.
 // B is a K-major weight matrix ([Cout][ky][kx][Cin] for convolutions).
 //
-// Roles per CTA (192 threads, one CTA per SM):
+// Roles per CTA (320 threads, one CTA per SM):
 //   warp 0        TMA producer: fills a STAGES-deep ring of 128-byte-swizzled
 //                 A/B tiles (128 x 128 B and BN x 128 B);
 //   warp 1        TMEM allocator + MMA issuer: 4 tcgen05.mma (K=32 bytes) per
 //                 ring slot into one of two TMEM accumulators (128 lanes x
 //                 BN columns each), tcgen05.commit frees slots / publishes
 //                 accumulators;
-//   warps 2..5    epilogue: tcgen05.ld 32x32b rows out of TMEM, fused
-//                 dequant / bias / GELU / LayerScale-residual / ReLU /
-//                 residual adds / output-head dot, then global stores.
+//   warps 2..9    epilogue, two warps per TMEM lane quarter: tcgen05.ld
+//                 32x32b rows out of TMEM, fused dequant / bias / GELU /
+//                 LayerScale-residual / ReLU / residual adds / output-head
+//                 dot; row-major results go through a shared-memory
+//                 transpose so that global stores are whole 128-byte lines.
 // The two accumulators let the epilogue of tile i overlap the MMAs of
 // tile i+1. Every wait is bounded (common.cuh: mbar_wait); a timeout sets
 // the device error word and the CTA drains and returns instead of hanging.
@@ -54,6 +56,7 @@ struct GemmParamsDev {
     uint64_t img_stride, col_stride;
     uint32_t ct_k, ct_cout, ct_w, ct_h;
     int* err;
+    int program;  // RowProgram for row-major outputs
 };
 
 __device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
@@ -70,6 +73,18 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b, bool bf16) {
 __device__ __forceinline__ float half_at(const void* p, uint64_t i, bool bf16) {
     if (bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
     return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+
+__device__ __forceinline__ void unpack4(uint2 t, bool bf16, float (&o)[4]) {
+    if (bf16) {
+        const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&t.x);
+        const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&t.y);
+        o[0] = __low2float(a); o[1] = __high2float(a); o[2] = __low2float(b); o[3] = __high2float(b);
+    } else {
+        const __half2 a = *reinterpret_cast<const __half2*>(&t.x);
+        const __half2 b = *reinterpret_cast<const __half2*>(&t.y);
+        o[0] = __low2float(a); o[1] = __high2float(a); o[2] = __low2float(b); o[3] = __high2float(b);
+    }
 }
 
 template <bool kInt8>
@@ -238,8 +253,183 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParamsDev& p, const uin
     }
 }
 
+// Row-major outputs (linear layers, channels-last maps): the 32x32 chunk a
+// warp reads from TMEM (thread = row) is staged through a padded shared
+// slab (stride 33 floats: conflict-free both ways) and re-read with 8 lanes
+// per row and 4 consecutive columns per lane, so residual loads and output
+// stores are 16-byte vectors covering whole 128-byte lines (64 bytes for half
+// outputs). Per-row scaling happens before the transpose, per-column work
+// (weight scale, bias, GELU, LayerScale, residuals, ReLU) after it, where
+// each lane needs the parameters of only its 4 columns.
+template <bool kInt8, bool F32, bool BIAS, bool GELU, bool LS, bool R1, bool R2, bool RELU, bool RC>
+__device__ __forceinline__ void epilogue_rows(const GemmParamsDev& p, const uint32_t (&acc)[32], bool valid,
+                                              uint64_t r, uint32_t col0, float* slab, uint32_t lane) {
+    float si = 1.0f;
+    if (kInt8 && valid) si = __ldg(p.s_in + r);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        float v = kInt8 ? (float)(int32_t)acc[j] : __uint_as_float(acc[j]);
+        if (kInt8) v = __fmul_rn(v, si);
+        slab[lane * 33 + j] = v;
+    }
+    __syncwarp();
+    uint64_t orow_l = r;
+    if (p.rows_per_img) orow_l = (r / p.rows_per_img) * p.out_rows_per_img + p.row_offset + r % p.rows_per_img;
+    const uint32_t cq = (lane & 7u) * 4u;
+    const uint32_t c = col0 + cq;
+    const bool cols_full = c + 4 <= p.n;
+    float sw[4], bs[4], gm[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const bool ok = c + k < p.n;
+        sw[k] = (kInt8 && ok) ? __ldg(p.s_w + c + k) : 1.0f;
+        bs[k] = (BIAS && ok) ? __ldg(p.bias + c + k) : 0.0f;
+        gm[k] = (LS && ok) ? __ldg(p.gamma + c + k) : 0.0f;
+    }
+    const bool hb = p.out_bf16 != 0;
+    const int my_valid = valid ? 1 : 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t src = 4u * i + (lane >> 3);
+        const int vrow = __shfl_sync(0xffffffffu, my_valid, src);
+        const unsigned long long orow = __shfl_sync(0xffffffffu, (unsigned long long)orow_l, src);
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = slab[src * 33 + cq + k];
+        if (vrow && c < p.n) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (kInt8) v[k] = __fmul_rn(v[k], sw[k]);
+                if (BIAS) v[k] = __fadd_rn(v[k], bs[k]);
+                if (GELU) v[k] = gelu_erf(v[k]);
+            }
+            const uint64_t base = orow * p.ldo + c;
+            const bool vec = cols_full && ((base & 3u) == 0);
+            if (F32) {
+                float a[4] = {0, 0, 0, 0}, b2[4] = {0, 0, 0, 0};
+                if (LS || R1) {
+                    const float* r1 = reinterpret_cast<const float*>(p.res1) + base;
+                    if (vec) {
+                        const float4 t = *reinterpret_cast<const float4*>(r1);
+                        a[0] = t.x; a[1] = t.y; a[2] = t.z; a[3] = t.w;
+                    } else {
+                        for (int k = 0; k < 4; ++k) a[k] = c + k < p.n ? r1[k] : 0.f;
+                    }
+                }
+                if (R2) {
+                    const float* r2 = reinterpret_cast<const float*>(p.res2) + base;
+                    if (vec) {
+                        const float4 t = *reinterpret_cast<const float4*>(r2);
+                        b2[0] = t.x; b2[1] = t.y; b2[2] = t.z; b2[3] = t.w;
+                    } else {
+                        for (int k = 0; k < 4; ++k) b2[k] = c + k < p.n ? r2[k] : 0.f;
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if (LS) v[k] = __fadd_rn(a[k], __fmul_rn(v[k], gm[k]));
+                    else if (R1) v[k] = v[k] + a[k];
+                    if (R2) v[k] = b2[k] + v[k];
+                    if (RELU) v[k] = fmaxf(v[k], 0.f);
+                }
+                float* o = reinterpret_cast<float*>(p.out) + base;
+                if (vec) {
+                    *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
+                    if (RC)
+                        *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out2) + base) =
+                            make_float4(fmaxf(v[0], 0.f), fmaxf(v[1], 0.f), fmaxf(v[2], 0.f), fmaxf(v[3], 0.f));
+                } else {
+                    for (int k = 0; k < 4; ++k)
+                        if (c + k < p.n) {
+                            o[k] = v[k];
+                            if (RC) reinterpret_cast<float*>(p.out2)[base + k] = fmaxf(v[k], 0.f);
+                        }
+                }
+            } else {
+                if (R1 || R2) {
+                    float a[4] = {0, 0, 0, 0}, b2[4] = {0, 0, 0, 0};
+                    if (vec) {
+                        if (R1) unpack4(*reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p.res1) + base), hb, a);
+                        if (R2) unpack4(*reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p.res2) + base), hb, b2);
+                    } else {
+                        for (int k = 0; k < 4; ++k) {
+                            if (c + k >= p.n) break;
+                            if (R1) a[k] = half_at(p.res1, base + k, hb);
+                            if (R2) b2[k] = half_at(p.res2, base + k, hb);
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        if (R1) v[k] = v[k] + a[k];
+                        if (R2) v[k] = b2[k] + v[k];
+                    }
+                }
+                if (RELU) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) v[k] = fmaxf(v[k], 0.f);
+                }
+                uint16_t* o = reinterpret_cast<uint16_t*>(p.out) + base;
+                if (vec) {
+                    *reinterpret_cast<uint2*>(o) = make_uint2(pack_half2(v[0], v[1], hb), pack_half2(v[2], v[3], hb));
+                    if (RC)
+                        *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.out2) + base) =
+                            make_uint2(pack_half2(fmaxf(v[0], 0.f), fmaxf(v[1], 0.f), hb),
+                                       pack_half2(fmaxf(v[2], 0.f), fmaxf(v[3], 0.f), hb));
+                } else {
+                    for (int k = 0; k < 4; ++k) {
+                        if (c + k >= p.n) break;
+                        o[k] = (uint16_t)(pack_half2(v[k], 0.f, hb) & 0xffffu);
+                        if (RC)
+                            reinterpret_cast<uint16_t*>(p.out2)[base + k] =
+                                (uint16_t)(pack_half2(fmaxf(v[k], 0.f), 0.f, hb) & 0xffffu);
+                    }
+                }
+            }
+        }
+    }
+    __syncwarp();
+}
+
+// Row-epilogue programs with a compiled instance (flags -> id); other flag
+// combinations use the generic per-element path (epilogue_chunk).
+enum RowProgram : int {
+    kRowGeneric = 0,
+    kRowF32,            // f32 (+bias)
+    kRowF32Bias,
+    kRowF32BiasGelu,
+    kRowF32BiasLS,      // LayerScale residual (proj, fc2)
+    kRowF32BiasR1,      // residual (patch embedding onto positions)
+    kRowHalf,
+    kRowHalfBias,
+    kRowHalfBiasGelu,   // fc1
+    kRowHalfBiasRelu,   // RCU conv1
+    kRowHalfRC,         // layer_rn
+    kRowHalfBiasR1,     // RCU2 conv2
+    kRowHalfBiasR1R2RC, // RCU1 conv2 + fusion add
+};
+
+template <bool kInt8>
+__device__ __forceinline__ void epilogue_dispatch(const GemmParamsDev& p, int prog, const uint32_t (&acc)[32],
+                                                  bool valid, uint64_t r, uint32_t col0, float* slab, uint32_t lane) {
+    switch (prog) {
+        case kRowF32: epilogue_rows<kInt8, true, false, false, false, false, false, false, false>(p, acc, valid, r, col0, slab, lane); break;
+        case kRowF32Bias: epilogue_rows<kInt8, true, true, false, false, false, false, false, false>(p, acc, valid, r, col0, slab, lane); break;
+        case kRowF32BiasGelu: epilogue_rows<kInt8, true, true, true, false, false, false, false, false>(p, acc, valid, r, col0, slab, lane); break;
+        case kRowF32BiasLS: epilogue_rows<kInt8, true, true, false, true, false, false, false, false>(p, acc, valid, r, col0, slab, lane); break;
+        case kRowF32BiasR1: epilogue_rows<kInt8, true, true, false, false, true, false, false, false>(p, acc, valid, r, col0, slab, lane); break;
+        case kRowHalf: epilogue_rows<kInt8, false, false, false, false, false, false, false, false>(p, acc, valid, r, col0, slab, lane); break;
+        case kRowHalfBias: epilogue_rows<kInt8, false, true, false, false, false, false, false, false>(p, acc, valid, r, col0, slab, lane); break;
+        case kRowHalfBiasGelu: epilogue_rows<kInt8, false, true, true, false, false, false, false, false>(p, acc, valid, r, col0, slab, lane); break;
+        case kRowHalfBiasRelu: epilogue_rows<kInt8, false, true, false, false, false, false, true, false>(p, acc, valid, r, col0, slab, lane); break;
+        case kRowHalfRC: epilogue_rows<kInt8, false, false, false, false, false, false, false, true>(p, acc, valid, r, col0, slab, lane); break;
+        case kRowHalfBiasR1: epilogue_rows<kInt8, false, true, false, false, true, false, false, false>(p, acc, valid, r, col0, slab, lane); break;
+        case kRowHalfBiasR1R2RC: epilogue_rows<kInt8, false, true, false, false, true, true, false, true>(p, acc, valid, r, col0, slab, lane); break;
+        default: epilogue_chunk<kInt8>(p, acc, valid, r, col0); break;
+    }
+}
+
 template <int BN, int STAGES, int ELEM, int AMODE>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const GemmParamsDev p) {
     constexpr bool kInt8 = ELEM == kElemS8;
@@ -260,6 +450,7 @@ __global__ void __launch_bounds__(192, 1)
     uint64_t* drain = tempty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* slabs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);  // 8 x 32 x 33 floats
 
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31;
@@ -273,8 +464,8 @@ __global__ void __launch_bounds__(192, 1)
         }
         mbar_init(&tfull[0], 1);
         mbar_init(&tfull[1], 1);
-        mbar_init(&tempty[0], 4);
-        mbar_init(&tempty[1], 4);
+        mbar_init(&tempty[0], 8);
+        mbar_init(&tempty[1], 8);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -356,8 +547,11 @@ __global__ void __launch_bounds__(192, 1)
             }
         }
     } else {
+        // warps 2..9: two warps per TMEM lane quarter, splitting the chunks
         const uint32_t quarter = warp & 3u;
+        const uint32_t half = (warp - 2u) >> 2;  // 0 or 1
         const uint32_t row_in_tile = quarter * 32u + lane;
+        float* slab = slabs + (warp - 2u) * (32u * 33u);
         uint32_t local = 0;
         for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
             const uint32_t buf = local & 1u;
@@ -380,13 +574,18 @@ __global__ void __launch_bounds__(192, 1)
                 r = ((uint64_t)img * p.conv_h + y) * p.conv_w + x;
             }
             const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + buf * (uint32_t)BN;
+            // chunk c (32 columns) belongs to this warp when (c/32) % 2 == half;
+            // two chunks are loaded from TMEM before waiting.
 #pragma unroll 1
-            for (uint32_t c = 0; c < (uint32_t)BN; c += 32) {
-                uint32_t acc[32];
-                tmem_ld_32x32b_x32(taddr + c, acc);
+            for (uint32_t c = half * 32u; c < (uint32_t)BN; c += 128u) {
+                uint32_t acc0[32], acc1[32];
+                const bool two = c + 64u < (uint32_t)BN;
+                tmem_ld_32x32b_x32(taddr + c, acc0);
+                if (two) tmem_ld_32x32b_x32(taddr + c + 64u, acc1);
                 tmem_ld_wait();
                 const uint32_t col0 = n_blk * (uint32_t)BN + c;
-                if (col0 < p.n) epilogue_chunk<kInt8>(p, acc, valid, r, col0);
+                if (col0 < p.n) epilogue_dispatch<kInt8>(p, p.program, acc0, valid, r, col0, slab, lane);
+                if (two && col0 + 64u < p.n) epilogue_dispatch<kInt8>(p, p.program, acc1, valid, r, col0 + 64u, slab, lane);
             }
             tc_fence_before();
             __syncwarp();
@@ -462,7 +661,7 @@ constexpr int stages_for() {
 
 template <int BN>
 constexpr size_t smem_for() {
-    return (size_t)stages_for<BN>() * (128 * 128 + BN * 128) + 256 + 1024;
+    return (size_t)stages_for<BN>() * (128 * 128 + BN * 128) + 256 + 8 * 32 * 33 * 4 + 1024;
 }
 
 int g_num_sms = 0;
@@ -487,7 +686,7 @@ int run(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParamsDev& p, in
     const uint32_t tiles = p.num_m_tiles * p.num_n_tiles;
     uint32_t grid = (uint32_t)(max_ctas > 0 ? max_ctas : g_num_sms);
     if (grid > tiles) grid = tiles;
-    kernel<<<grid, 192, smem, st>>>(ma, mb, p);
+    kernel<<<grid, 320, smem, st>>>(ma, mb, p);
     return check_launch("gemm_tc");
 }
 
@@ -544,6 +743,27 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.ct_w = g.convt_w;
     p.ct_h = g.convt_h;
     p.num_n_tiles = (g.n + bn - 1) / bn;
+    p.program = kRowGeneric;
+    if ((g.out_kind == kOutF32Rows || g.out_kind == kOutHalfRows) && !(g.flags & kEpiHeadDot)) {
+        const uint32_t f = g.flags & ~uint32_t(kEpiDequant);
+        const bool f32 = g.out_kind == kOutF32Rows;
+        if (f32) {
+            if (f == 0) p.program = kRowF32;
+            else if (f == kEpiBias) p.program = kRowF32Bias;
+            else if (f == (kEpiBias | kEpiGelu)) p.program = kRowF32BiasGelu;
+            else if (f == (kEpiBias | kEpiLayerScale)) p.program = kRowF32BiasLS;
+            else if (f == (kEpiBias | kEpiResidual1)) p.program = kRowF32BiasR1;
+        } else {
+            if (f == 0) p.program = kRowHalf;
+            else if (f == kEpiBias) p.program = kRowHalfBias;
+            else if (f == (kEpiBias | kEpiGelu)) p.program = kRowHalfBiasGelu;
+            else if (f == (kEpiBias | kEpiRelu)) p.program = kRowHalfBiasRelu;
+            else if (f == kEpiReluCopy) p.program = kRowHalfRC;
+            else if (f == (kEpiBias | kEpiResidual1)) p.program = kRowHalfBiasR1;
+            else if (f == (kEpiBias | kEpiResidual1 | kEpiResidual2 | kEpiReluCopy)) p.program = kRowHalfBiasR1R2RC;
+        }
+        if (((g.flags & kEpiDequant) != 0) != (g.elem == kElemS8)) p.program = kRowGeneric;
+    }
     p.err = device_error_word();
     if (!p.err) return set_error(DAV2CUDA_INTERNAL_ERROR, "gemm: no device error word");
 

@@ -189,6 +189,23 @@ DAV2CUDA_API int dav2cuda_linear_int8(float* output, const float* input, const u
                                       uint32_t input_columns, uint32_t output_columns, uint32_t gelu,
                                       void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* dav2cuda_linear_int8 for callers that may not allocate device memory —
+ * host applications that own the device heap (video pipelines, game
+ * engines, inference servers that reserve memory at start-up and treat a
+ * later cudaMalloc as a failure) or run on real-time paths where an
+ * allocation is not allowed. No counterpart in the reference (its operators
+ * own a reusable workspace). Scratch: one 16 MiB device array per GPU that
+ * loads the library (dav2cuda_linear_int8_noalloc_scratch_limit()), held
+ * until exit; larger problems return DAV2CUDA_INVALID_ARGUMENT. The first
+ * call on a device resolves the array's address (make it before any stream
+ * capture). All calls share the array: calls that overlap on the GPU race.
+ * Allocates nothing. */
+DAV2CUDA_API uint64_t dav2cuda_linear_int8_noalloc_scratch_limit(void);
+DAV2CUDA_API int dav2cuda_linear_int8_noalloc(float* output, const float* input,
+                                              const uint32_t* int8_weight, const float* weight_scales,
+                                              const float* bias, uint32_t rows, uint32_t input_columns,
+                                              uint32_t output_columns, uint32_t gelu, void* stream);
+
 /* VulkanOperators::conv2d_int8 (src/operators.h:183-196,
  * src/operators.cpp:1735-1805): im2col-quantize -> s8 GEMM -> planar
  * dequantized output [Co, OH, OW]. */

@@ -34,6 +34,8 @@
 namespace dav2cuda {
 namespace {
 
+constexpr int kMaxStages = 8;
+
 struct GemmParamsDev {
     uint32_t m, n, num_kb, num_m_tiles, num_n_tiles;
     uint32_t a_mode;
@@ -56,10 +58,22 @@ struct GemmParamsDev {
     uint64_t img_stride, col_stride;
     uint32_t ct_k, ct_cout, ct_w, ct_h;
     int* err;
-    int program;  // RowProgram for row-major outputs
+    int program;      // RowProgram for row-major outputs (transposed-store path)
+    int tma_program;  // TmaProgram: thread-row epilogue with TMA stores, or 0
+    uint32_t stages;  // depth of the A/B shared-memory ring
 };
 
-__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
+// Exact-erf GELU (torch.nn.GELU) with erf from Abramowitz & Stegun 7.1.26
+// (|error| <= 1.5e-7): erf(z) = 1 - t(a1 + t(a2 + t(a3 + t(a4 + t a5)))) e^{-z^2},
+// t = 1/(1 + p z) for z >= 0, odd extension for z < 0.
+__device__ __forceinline__ float gelu_erf(float v) {
+    const float z = fabsf(v) * 0.70710678118654752f;
+    const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+    const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f),
+                                     -0.284496736f), 0.254829592f);
+    const float e = 1.0f - poly * __expf(-z * z);
+    return 0.5f * v * (1.0f + copysignf(e, v));
+}
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b, bool bf16) {
     if (bf16) {
@@ -261,7 +275,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParamsDev& p, const uin
 // outputs). Per-row scaling happens before the transpose, per-column work
 // (weight scale, bias, GELU, LayerScale, residuals, ReLU) after it, where
 // each lane needs the parameters of only its 4 columns.
-template <bool kInt8, bool F32, bool BIAS, bool GELU, bool LS, bool R1, bool R2, bool RELU, bool RC>
+template <bool kInt8, bool F32, bool BIAS, bool GELU, bool LS, bool R1, bool R2, bool RELU, bool RC, bool CT = false>
 __device__ __forceinline__ void epilogue_rows(const GemmParamsDev& p, const uint32_t (&acc)[32], bool valid,
                                               uint64_t r, uint32_t col0, float* slab, uint32_t lane) {
     float si = 1.0f;
@@ -288,91 +302,113 @@ __device__ __forceinline__ void epilogue_rows(const GemmParamsDev& p, const uint
     }
     const bool hb = p.out_bf16 != 0;
     const int my_valid = valid ? 1 : 0;
+    // Output element offsets of the 8 row groups this lane stores, and (for
+    // residual programs) the residual values there. All residual loads of
+    // the chunk are issued before any store: the output usually aliases the
+    // residual (in-place update), so loads interleaved with stores would
+    // serialise into one memory round trip per row group.
+    uint64_t base[8];
+    bool live[8];
+    float ra[8][4], rb[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const uint32_t src = 4u * i + (lane >> 3);
         const int vrow = __shfl_sync(0xffffffffu, my_valid, src);
         const unsigned long long orow = __shfl_sync(0xffffffffu, (unsigned long long)orow_l, src);
+        live[i] = vrow && c < p.n;
+        base[i] = orow * p.ldo + c;
+        if (CT) {
+            // conv-transpose (kernel == stride): GEMM row = input pixel,
+            // column = (ky*k + kx)*Cout + co -> channels-last output pixel
+            const uint32_t hw = p.ct_w * p.ct_h;
+            const uint64_t img = orow / hw;
+            const uint32_t pp = (uint32_t)(orow % hw);
+            const uint32_t kk = c / p.ct_cout, co = c % p.ct_cout;
+            const uint32_t oy = (pp / p.ct_w) * p.ct_k + kk / p.ct_k, ox = (pp % p.ct_w) * p.ct_k + kk % p.ct_k;
+            base[i] = ((img * p.ct_h * p.ct_k + oy) * (uint64_t)(p.ct_w * p.ct_k) + ox) * p.ldo + co;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ra[i][k] = rb[i][k] = 0.f;
+        if ((LS || R1 || R2) && live[i]) {
+            const bool vec = cols_full && ((base[i] & 3u) == 0);
+            if (F32) {
+                if (LS || R1) {
+                    const float* r1 = reinterpret_cast<const float*>(p.res1) + base[i];
+                    if (vec) {
+                        const float4 t = *reinterpret_cast<const float4*>(r1);
+                        ra[i][0] = t.x; ra[i][1] = t.y; ra[i][2] = t.z; ra[i][3] = t.w;
+                    } else {
+                        for (int k = 0; k < 4; ++k) ra[i][k] = c + k < p.n ? r1[k] : 0.f;
+                    }
+                }
+                if (R2) {
+                    const float* r2 = reinterpret_cast<const float*>(p.res2) + base[i];
+                    if (vec) {
+                        const float4 t = *reinterpret_cast<const float4*>(r2);
+                        rb[i][0] = t.x; rb[i][1] = t.y; rb[i][2] = t.z; rb[i][3] = t.w;
+                    } else {
+                        for (int k = 0; k < 4; ++k) rb[i][k] = c + k < p.n ? r2[k] : 0.f;
+                    }
+                }
+            } else if (vec) {
+                if (R1) unpack4(*reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p.res1) + base[i]), hb, ra[i]);
+                if (R2) unpack4(*reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p.res2) + base[i]), hb, rb[i]);
+            } else {
+                for (int k = 0; k < 4; ++k) {
+                    if (c + k >= p.n) break;
+                    if (R1) ra[i][k] = half_at(p.res1, base[i] + k, hb);
+                    if (R2) rb[i][k] = half_at(p.res2, base[i] + k, hb);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t src = 4u * i + (lane >> 3);
         float v[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) v[k] = slab[src * 33 + cq + k];
-        if (vrow && c < p.n) {
+        if (live[i]) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 if (kInt8) v[k] = __fmul_rn(v[k], sw[k]);
                 if (BIAS) v[k] = __fadd_rn(v[k], bs[k]);
                 if (GELU) v[k] = gelu_erf(v[k]);
             }
-            const uint64_t base = orow * p.ldo + c;
-            const bool vec = cols_full && ((base & 3u) == 0);
+            const bool vec = cols_full && ((base[i] & 3u) == 0) && (!CT || (p.ct_cout & 3u) == 0);
             if (F32) {
-                float a[4] = {0, 0, 0, 0}, b2[4] = {0, 0, 0, 0};
-                if (LS || R1) {
-                    const float* r1 = reinterpret_cast<const float*>(p.res1) + base;
-                    if (vec) {
-                        const float4 t = *reinterpret_cast<const float4*>(r1);
-                        a[0] = t.x; a[1] = t.y; a[2] = t.z; a[3] = t.w;
-                    } else {
-                        for (int k = 0; k < 4; ++k) a[k] = c + k < p.n ? r1[k] : 0.f;
-                    }
-                }
-                if (R2) {
-                    const float* r2 = reinterpret_cast<const float*>(p.res2) + base;
-                    if (vec) {
-                        const float4 t = *reinterpret_cast<const float4*>(r2);
-                        b2[0] = t.x; b2[1] = t.y; b2[2] = t.z; b2[3] = t.w;
-                    } else {
-                        for (int k = 0; k < 4; ++k) b2[k] = c + k < p.n ? r2[k] : 0.f;
-                    }
-                }
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    if (LS) v[k] = __fadd_rn(a[k], __fmul_rn(v[k], gm[k]));
-                    else if (R1) v[k] = v[k] + a[k];
-                    if (R2) v[k] = b2[k] + v[k];
+                    if (LS) v[k] = __fadd_rn(ra[i][k], __fmul_rn(v[k], gm[k]));
+                    else if (R1) v[k] = v[k] + ra[i][k];
+                    if (R2) v[k] = rb[i][k] + v[k];
                     if (RELU) v[k] = fmaxf(v[k], 0.f);
                 }
-                float* o = reinterpret_cast<float*>(p.out) + base;
+                float* o = reinterpret_cast<float*>(p.out) + base[i];
                 if (vec) {
                     *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
                     if (RC)
-                        *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out2) + base) =
+                        *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out2) + base[i]) =
                             make_float4(fmaxf(v[0], 0.f), fmaxf(v[1], 0.f), fmaxf(v[2], 0.f), fmaxf(v[3], 0.f));
                 } else {
                     for (int k = 0; k < 4; ++k)
                         if (c + k < p.n) {
                             o[k] = v[k];
-                            if (RC) reinterpret_cast<float*>(p.out2)[base + k] = fmaxf(v[k], 0.f);
+                            if (RC) reinterpret_cast<float*>(p.out2)[base[i] + k] = fmaxf(v[k], 0.f);
                         }
                 }
             } else {
-                if (R1 || R2) {
-                    float a[4] = {0, 0, 0, 0}, b2[4] = {0, 0, 0, 0};
-                    if (vec) {
-                        if (R1) unpack4(*reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p.res1) + base), hb, a);
-                        if (R2) unpack4(*reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p.res2) + base), hb, b2);
-                    } else {
-                        for (int k = 0; k < 4; ++k) {
-                            if (c + k >= p.n) break;
-                            if (R1) a[k] = half_at(p.res1, base + k, hb);
-                            if (R2) b2[k] = half_at(p.res2, base + k, hb);
-                        }
-                    }
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        if (R1) v[k] = v[k] + a[k];
-                        if (R2) v[k] = b2[k] + v[k];
-                    }
+                for (int k = 0; k < 4; ++k) {
+                    if (R1) v[k] = v[k] + ra[i][k];
+                    if (R2) v[k] = rb[i][k] + v[k];
+                    if (RELU) v[k] = fmaxf(v[k], 0.f);
                 }
-                if (RELU) {
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) v[k] = fmaxf(v[k], 0.f);
-                }
-                uint16_t* o = reinterpret_cast<uint16_t*>(p.out) + base;
+                uint16_t* o = reinterpret_cast<uint16_t*>(p.out) + base[i];
                 if (vec) {
                     *reinterpret_cast<uint2*>(o) = make_uint2(pack_half2(v[0], v[1], hb), pack_half2(v[2], v[3], hb));
                     if (RC)
-                        *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.out2) + base) =
+                        *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.out2) + base[i]) =
                             make_uint2(pack_half2(fmaxf(v[0], 0.f), fmaxf(v[1], 0.f), hb),
                                        pack_half2(fmaxf(v[2], 0.f), fmaxf(v[3], 0.f), hb));
                 } else {
@@ -380,7 +416,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmParamsDev& p, const uint
                         if (c + k >= p.n) break;
                         o[k] = (uint16_t)(pack_half2(v[k], 0.f, hb) & 0xffffu);
                         if (RC)
-                            reinterpret_cast<uint16_t*>(p.out2)[base + k] =
+                            reinterpret_cast<uint16_t*>(p.out2)[base[i] + k] =
                                 (uint16_t)(pack_half2(fmaxf(v[k], 0.f), 0.f, hb) & 0xffffu);
                     }
                 }
@@ -406,6 +442,7 @@ enum RowProgram : int {
     kRowHalfRC,         // layer_rn
     kRowHalfBiasR1,     // RCU2 conv2
     kRowHalfBiasR1R2RC, // RCU1 conv2 + fusion add
+    kRowHalfBiasCT,     // conv-transpose scatter into channels-last half
 };
 
 template <bool kInt8>
@@ -424,33 +461,248 @@ __device__ __forceinline__ void epilogue_dispatch(const GemmParamsDev& p, int pr
         case kRowHalfRC: epilogue_rows<kInt8, false, false, false, false, false, false, false, true>(p, acc, valid, r, col0, slab, lane); break;
         case kRowHalfBiasR1: epilogue_rows<kInt8, false, true, false, false, true, false, false, false>(p, acc, valid, r, col0, slab, lane); break;
         case kRowHalfBiasR1R2RC: epilogue_rows<kInt8, false, true, false, false, true, true, false, true>(p, acc, valid, r, col0, slab, lane); break;
+        case kRowHalfBiasCT: epilogue_rows<kInt8, false, true, false, false, false, false, false, false, true>(p, acc, valid, r, col0, slab, lane); break;
         default: epilogue_chunk<kInt8>(p, acc, valid, r, col0); break;
     }
 }
 
-template <int BN, int STAGES, int ELEM, int AMODE>
+// ------------------------------------------------- thread-row TMA epilogue
+// For row-major outputs whose column count is a multiple of the tile width:
+// each epilogue thread owns one accumulator row (its TMEM lane) and 32
+// consecutive columns per chunk, exactly as tcgen05.ld 32x32b delivers them,
+// so there is no transpose, shuffle or per-row address arithmetic. Per-column
+// parameters (weight scales, bias, LayerScale) are warp-uniform vector loads.
+// Results are written into a 32-row shared-memory box in the tensor map's
+// swizzled layout (128-byte swizzle for f32 rows of 128 B, 64-byte swizzle
+// for f16 rows of 64 B; both conflict-free for 16-byte row-wise writes) and
+// leave with one TMA store per box; rows beyond M are clipped by the map.
+// The LayerScale residual (x += gamma * y, in place) arrives by TMA into the
+// other staging buffer one chunk ahead of its use.
+enum TmaProgram : int {
+    kTmaNone = 0,
+    kTmaHalf,
+    kTmaHalfBias,
+    kTmaHalfBiasGelu,  // fc1
+    kTmaHalfBiasRelu,
+    kTmaF32,
+    kTmaF32Bias,
+    kTmaF32BiasGelu,
+    kTmaF32BiasLS,  // attention projection, fc2
+};
+
+constexpr uint32_t kStageBufBytes = 4096;  // one 32-row box: 32 x 128 B (f32) or 32 x 64 B (f16)
+
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+template <bool kInt8, bool BIAS, bool GELU>
+__device__ __forceinline__ void dequant4(const uint32_t* acc, float si, const float* s_w, const float* bias,
+                                         uint32_t c, float* v) {
+    float4 w = make_float4(1.f, 1.f, 1.f, 1.f), b = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (kInt8) w = ldg4(s_w + c);
+    if (BIAS) b = ldg4(bias + c);
+    const float ws[4] = {w.x, w.y, w.z, w.w}, bs[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float t = kInt8 ? (float)(int32_t)acc[k] : __uint_as_float(acc[k]);
+        if (kInt8) t = __fmul_rn(__fmul_rn(t, si), ws[k]);
+        if (BIAS) t = __fadd_rn(t, bs[k]);
+        if (GELU) t = gelu_erf(t);
+        v[k] = t;
+    }
+}
+
+// One 32x32 chunk: registers -> swizzled staging box (residual, if any, is
+// already in the box).
+template <bool kInt8, bool F32, bool BIAS, bool GELU, bool LS, bool RELU>
+__device__ __forceinline__ void tma_chunk_compute(const GemmParamsDev& p, const uint32_t (&acc)[32], float si,
+                                                  uint32_t col0, uint8_t* box, uint32_t lane) {
+    const bool hb = p.out_bf16 != 0;
+    if (F32) {
+        uint8_t* row = box + lane * 128u;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const uint32_t c = col0 + 4u * g;
+            float v[4];
+            dequant4<kInt8, BIAS, GELU>(&acc[4 * g], si, p.s_w, p.bias, c, v);
+            float4* q = reinterpret_cast<float4*>(row + (((uint32_t)g ^ (lane & 7u)) << 4));
+            if (LS) {
+                const float4 gm = ldg4(p.gamma + c);
+                const float4 r = *q;
+                v[0] = __fadd_rn(r.x, __fmul_rn(v[0], gm.x));
+                v[1] = __fadd_rn(r.y, __fmul_rn(v[1], gm.y));
+                v[2] = __fadd_rn(r.z, __fmul_rn(v[2], gm.z));
+                v[3] = __fadd_rn(r.w, __fmul_rn(v[3], gm.w));
+            }
+            if (RELU) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[k] = fmaxf(v[k], 0.f);
+            }
+            *q = make_float4(v[0], v[1], v[2], v[3]);
+        }
+    } else {
+        uint8_t* row = box + lane * 64u;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint32_t c = col0 + 8u * u;
+            float v[8];
+            dequant4<kInt8, BIAS, GELU>(&acc[8 * u], si, p.s_w, p.bias, c, v);
+            dequant4<kInt8, BIAS, GELU>(&acc[8 * u + 4], si, p.s_w, p.bias, c + 4u, v + 4);
+            if (RELU) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = fmaxf(v[k], 0.f);
+            }
+            *reinterpret_cast<uint4*>(row + (((uint32_t)u ^ ((lane >> 1) & 3u)) << 4)) =
+                make_uint4(pack_half2(v[0], v[1], hb), pack_half2(v[2], v[3], hb), pack_half2(v[4], v[5], hb),
+                           pack_half2(v[6], v[7], hb));
+        }
+    }
+}
+
+// The epilogue warp's whole tile loop for one program. `bufs` is this
+// warp's pair of staging boxes, `rbar` its pair of residual mbarriers.
+template <int BN, bool kInt8, bool F32, bool BIAS, bool GELU, bool LS, bool RELU>
+__device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const CUtensorMap* tm_o, const CUtensorMap* tm_r,
+                                               uint32_t tmem_base, uint64_t* tfull, uint64_t* tempty, uint64_t* rbar,
+                                               uint8_t* bufs, volatile int* abort_flag, uint32_t warp,
+                                               uint32_t lane) {
+    const uint32_t quarter = warp & 3u;
+    const uint32_t half = (warp - 2u) >> 2;
+    const uint32_t num_tiles = p.num_m_tiles * p.num_n_tiles;
+    const uint32_t first_c = half * 32u;
+    const bool has_chunks = first_c < (uint32_t)BN;
+    uint32_t seq = 0;  // chunks processed by this warp
+    // residual box of chunk (tile, c) -> staging buffer b
+    auto load_residual = [&](uint32_t tile, uint32_t c, uint32_t b) {
+        const uint32_t n_blk = tile % p.num_n_tiles, m_blk = tile / p.num_n_tiles;
+        mbar_arrive_expect_tx(&rbar[b], kStageBufBytes);
+        tma_load_2d(bufs + b * kStageBufBytes, tm_r, &rbar[b], (int)(n_blk * (uint32_t)BN + c),
+                    (int)(m_blk * 128u + quarter * 32u));
+    };
+    if (LS && has_chunks && lane == 0 && blockIdx.x < num_tiles) load_residual(blockIdx.x, first_c, 0);
+
+    uint32_t local = 0;
+    for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+        const uint32_t buf = local & 1u;
+        if (!mbar_wait(&tfull[buf], (local >> 1) & 1u, abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t n_blk = tile % p.num_n_tiles;
+        const uint32_t m_blk = tile / p.num_n_tiles;
+        const uint64_t r = (uint64_t)m_blk * 128u + quarter * 32u + lane;
+        const float si = (kInt8 && r < p.m) ? __ldg(p.s_in + r) : 0.f;
+        const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + buf * (uint32_t)BN;
+        bool ok = true;
+        if (!has_chunks) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+            continue;
+        }
+#pragma unroll 1
+        for (uint32_t c = first_c; c < (uint32_t)BN && ok; c += 128u) {
+            uint32_t acc[2][32];
+            const bool two = c + 64u < (uint32_t)BN;
+            tmem_ld_32x32b_x32(taddr + c, acc[0]);
+            if (two) tmem_ld_32x32b_x32(taddr + c + 64u, acc[1]);
+            tmem_ld_wait();
+            if (c + 128u >= (uint32_t)BN) {  // last TMEM read of this tile: release the accumulator
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[buf]);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (h == 1 && !two) break;
+                const uint32_t cc = c + 64u * h;
+                const uint32_t b = seq & 1u;
+                uint8_t* box = bufs + b * kStageBufBytes;
+                if (LS) {
+                    if (lane == 0) {
+                        // prefetch the next chunk's residual into the other box, once
+                        // the store that last used that box has read it out
+                        uint32_t nt = tile, nc = cc + 64u;
+                        if (nc >= (uint32_t)BN) {
+                            nt = tile + gridDim.x;
+                            nc = first_c;
+                        }
+                        if (nt < num_tiles) {
+                            bulk_wait_group_read<0>();
+                            load_residual(nt, nc, b ^ 1u);
+                        }
+                    }
+                    if (!mbar_wait(&rbar[b], (seq >> 1) & 1u, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                } else {
+                    if (lane == 0) bulk_wait_group_read<1>();
+                    __syncwarp();
+                }
+                const uint32_t col0 = n_blk * (uint32_t)BN + cc;
+                tma_chunk_compute<kInt8, F32, BIAS, GELU, LS, RELU>(p, acc[h], si, col0, box, lane);
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(tm_o, box, (int)col0, (int)(m_blk * 128u + quarter * 32u));
+                    bulk_commit_group();
+                }
+                ++seq;
+            }
+        }
+        if (!ok) break;
+    }
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
+}
+
+template <int BN, bool kInt8>
+__device__ __forceinline__ void epilogue_tma_dispatch(const GemmParamsDev& p, const CUtensorMap* tm_o,
+                                                      const CUtensorMap* tm_r, uint32_t tmem_base, uint64_t* tfull,
+                                                      uint64_t* tempty, uint64_t* rbar, uint8_t* bufs,
+                                                      volatile int* abort_flag, uint32_t warp, uint32_t lane) {
+#define DAV2_TMA_EPI(F32, BIAS, GELU, LS, RELU)                                                                      \
+    epilogue_tma_loop<BN, kInt8, F32, BIAS, GELU, LS, RELU>(p, tm_o, tm_r, tmem_base, tfull, tempty, rbar, bufs, \
+                                                            abort_flag, warp, lane)
+    switch (p.tma_program) {
+        case kTmaHalf: DAV2_TMA_EPI(false, false, false, false, false); break;
+        case kTmaHalfBias: DAV2_TMA_EPI(false, true, false, false, false); break;
+        case kTmaHalfBiasGelu: DAV2_TMA_EPI(false, true, true, false, false); break;
+        case kTmaHalfBiasRelu: DAV2_TMA_EPI(false, true, false, false, true); break;
+        case kTmaF32: DAV2_TMA_EPI(true, false, false, false, false); break;
+        case kTmaF32Bias: DAV2_TMA_EPI(true, true, false, false, false); break;
+        case kTmaF32BiasGelu: DAV2_TMA_EPI(true, true, true, false, false); break;
+        default: DAV2_TMA_EPI(true, true, false, true, false); break;
+    }
+#undef DAV2_TMA_EPI
+}
+
+template <int BN, int ELEM, int AMODE>
 __global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                   const GemmParamsDev p) {
+                   const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ CUtensorMap tm_r,
+                   const __grid_constant__ GemmParamsDev p) {
     constexpr bool kInt8 = ELEM == kElemS8;
     constexpr uint32_t kABytes = 128u * 128u;
     constexpr uint32_t kBBytes = (uint32_t)BN * 128u;
     constexpr uint32_t kTmemCols = 2u * BN < 32u ? 32u : 2u * BN;
     // f16: A/B format 0; bf16: 1; s8 (signed): 1. D: f32 = 1, s32 = 2.
     constexpr uint32_t kIdesc = make_idesc(kInt8 ? 2u : 1u, ELEM == kElemF16 ? 0u : 1u, 128u, (uint32_t)BN);
+    const uint32_t STAGES = p.stages;
 
+    // [A ring][B ring][1 KB: barriers, TMEM slot, abort flag][epilogue staging]
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * kABytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * kBBytes);
-    uint64_t* empty = full + STAGES;
-    uint64_t* tfull = empty + STAGES;
+    uint64_t* empty = full + kMaxStages;
+    uint64_t* tfull = empty + kMaxStages;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* rbars = drain + 1;  // 8 epilogue warps x 2 residual barriers
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbars + 16);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    float* slabs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);  // 8 x 32 x 33 floats
+    uint8_t* staging = reinterpret_cast<uint8_t*>(full) + 1024;
+    float* slabs = reinterpret_cast<float*>(staging);  // 8 x 32 x 33 floats (transposed-store path)
 
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31;
@@ -458,7 +710,11 @@ __global__ void __launch_bounds__(320, 1)
     if (threadIdx.x == 0) {
         tma_prefetch_desc(&tm_a);
         tma_prefetch_desc(&tm_b);
-        for (int s = 0; s < STAGES; ++s) {
+        if (p.tma_program != kTmaNone) {
+            tma_prefetch_desc(&tm_o);
+            tma_prefetch_desc(&tm_r);
+        }
+        for (uint32_t s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -467,6 +723,7 @@ __global__ void __launch_bounds__(320, 1)
         mbar_init(&tempty[0], 8);
         mbar_init(&tempty[1], 8);
         mbar_init(drain, 1);
+        for (int i = 0; i < 16; ++i) mbar_init(&rbars[i], 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -546,6 +803,10 @@ __global__ void __launch_bounds__(320, 1)
                 umma_commit(&tfull[buf]);
             }
         }
+    } else if (AMODE == kAModeRows && p.tma_program != kTmaNone) {
+        if constexpr (AMODE == kAModeRows)
+            epilogue_tma_dispatch<BN, kInt8>(p, &tm_o, &tm_r, tmem_base, tfull, tempty, rbars + 2u * (warp - 2u),
+                                             staging + 2u * kStageBufBytes * (warp - 2u), abort_flag, warp, lane);
     } else {
         // warps 2..9: two warps per TMEM lane quarter, splitting the chunks
         const uint32_t quarter = warp & 3u;
@@ -639,13 +900,13 @@ CUtensorMapDataType tm_type(int elem) {
     }
 }
 
-int make_map(CUtensorMap* map, int elem, int rank, const void* base, const cuuint64_t* dims,
-             const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+int make_map_typed(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base, const cuuint64_t* dims,
+                   const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swizzle) {
     if (!get_encoder()) return set_error(DAV2CUDA_INTERNAL_ERROR, "cuTensorMapEncodeTiled unavailable");
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    const CUresult rc = g_encode(map, tm_type(elem), rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
-                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult rc = g_encode(map, type, rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (rc != CUDA_SUCCESS) {
         char msg[160];
         snprintf(msg, sizeof msg, "cuTensorMapEncodeTiled failed (%d)", (int)rc);
@@ -654,28 +915,42 @@ int make_map(CUtensorMap* map, int elem, int rank, const void* base, const cuuin
     return DAV2CUDA_OK;
 }
 
-template <int BN>
-constexpr int stages_for() {
-    return BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
+int make_map(CUtensorMap* map, int elem, int rank, const void* base, const cuuint64_t* dims,
+             const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+    return make_map_typed(map, tm_type(elem), rank, base, dims, strides_bytes, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int BN>
-constexpr size_t smem_for() {
-    return (size_t)stages_for<BN>() * (128 * 128 + BN * 128) + 256 + 8 * 32 * 33 * 4 + 1024;
+constexpr uint32_t kSmemOptin = 232448;      // B200 per-block opt-in limit
+constexpr uint32_t kSlabBytes = 8 * 32 * 33 * 4;  // transposed-store epilogue scratch
+
+// Ring depth that fits beside the epilogue staging area, and the dynamic
+// shared-memory size of that configuration.
+uint32_t stages_for(int bn, uint32_t staging) {
+    const uint32_t per_stage = 128u * 128u + (uint32_t)bn * 128u;
+    uint32_t s = (kSmemOptin - 2048u - staging) / per_stage;
+    return s > (uint32_t)kMaxStages ? (uint32_t)kMaxStages : s;
+}
+
+size_t smem_for(int bn, uint32_t stages, uint32_t staging) {
+    return (size_t)stages * (128u * 128u + (uint32_t)bn * 128u) + 1024u + staging + 1024u;
 }
 
 int g_num_sms = 0;
 
 template <int BN, int ELEM, int AMODE>
-int run(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParamsDev& p, int max_ctas, cudaStream_t st) {
-    constexpr int S = stages_for<BN>();
-    constexpr size_t smem = smem_for<BN>();
-    auto kernel = gemm_tc_kernel<BN, S, ELEM, AMODE>;
+int run(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const CUtensorMap& mr, GemmParamsDev p,
+        uint32_t staging, int max_ctas, cudaStream_t st) {
+    auto kernel = gemm_tc_kernel<BN, ELEM, AMODE>;
+    p.stages = stages_for(BN, staging);
+    const size_t smem = smem_for(BN, p.stages, staging);
+    if (p.stages < 2 || smem > kSmemOptin) return set_error(DAV2CUDA_INTERNAL_ERROR, "gemm: shared memory plan");
     static uint64_t configured = 0;  // one bit per device ordinal
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(configured >> (dev & 63) & 1ull)) {
-        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemOptin) != cudaSuccess ||
+            cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return set_error(DAV2CUDA_LAUNCH_FAILED, "gemm: cannot set shared memory size");
         configured |= 1ull << (dev & 63);
     }
@@ -686,18 +961,18 @@ int run(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParamsDev& p, in
     const uint32_t tiles = p.num_m_tiles * p.num_n_tiles;
     uint32_t grid = (uint32_t)(max_ctas > 0 ? max_ctas : g_num_sms);
     if (grid > tiles) grid = tiles;
-    kernel<<<grid, 320, smem, st>>>(ma, mb, p);
+    kernel<<<grid, 320, smem, st>>>(ma, mb, mo, mr, p);
     return check_launch("gemm_tc");
 }
 
 template <int ELEM, int AMODE>
-int dispatch_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmParamsDev& p, int max_ctas,
-                cudaStream_t st) {
+int dispatch_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const CUtensorMap& mr,
+                const GemmParamsDev& p, uint32_t staging, int max_ctas, cudaStream_t st) {
     switch (bn) {
-        case 256: return run<256, ELEM, AMODE>(ma, mb, p, max_ctas, st);
-        case 128: return run<128, ELEM, AMODE>(ma, mb, p, max_ctas, st);
-        case 64: return run<64, ELEM, AMODE>(ma, mb, p, max_ctas, st);
-        default: return run<32, ELEM, AMODE>(ma, mb, p, max_ctas, st);
+        case 256: return run<256, ELEM, AMODE>(ma, mb, mo, mr, p, staging, max_ctas, st);
+        case 128: return run<128, ELEM, AMODE>(ma, mb, mo, mr, p, staging, max_ctas, st);
+        case 64: return run<64, ELEM, AMODE>(ma, mb, mo, mr, p, staging, max_ctas, st);
+        default: return run<32, ELEM, AMODE>(ma, mb, mo, mr, p, staging, max_ctas, st);
     }
 }
 
@@ -744,6 +1019,9 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     p.ct_h = g.convt_h;
     p.num_n_tiles = (g.n + bn - 1) / bn;
     p.program = kRowGeneric;
+    if (g.out_kind == kOutConvTHalf && (g.flags & ~uint32_t(kEpiDequant)) == kEpiBias &&
+        ((g.flags & kEpiDequant) != 0) == (g.elem == kElemS8))
+        p.program = kRowHalfBiasCT;
     if ((g.out_kind == kOutF32Rows || g.out_kind == kOutHalfRows) && !(g.flags & kEpiHeadDot)) {
         const uint32_t f = g.flags & ~uint32_t(kEpiDequant);
         const bool f32 = g.out_kind == kOutF32Rows;
@@ -800,18 +1078,60 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
         if (g.m != g.conv_batch * g.conv_h * g.conv_w)
             return set_error(DAV2CUDA_INVALID_ARGUMENT, "gemm: conv M must be batch*H*W");
     }
+    // Thread-row epilogue with TMA stores: plain row-major outputs (no row
+    // remap), whole tiles along N, 16-byte aligned rows.
+    CUtensorMap mo = mb, mr = mb;  // placeholders when unused (never read)
+    uint32_t staging = kSlabBytes;
+    p.tma_program = kTmaNone;
+    if (g.a_mode == kAModeRows && !p.rows_per_img && (g.out_kind == kOutF32Rows || g.out_kind == kOutHalfRows) &&
+        !(g.flags & kEpiHeadDot) && ((g.flags & kEpiDequant) != 0) == (g.elem == kElemS8) && g.n % bn == 0) {
+        const bool f32 = g.out_kind == kOutF32Rows;
+        const uint32_t oes = f32 ? 4u : 2u;
+        const uint32_t f = g.flags & ~uint32_t(kEpiDequant);
+        int prog = kTmaNone;
+        if (f32) {
+            if (f == 0) prog = kTmaF32;
+            else if (f == kEpiBias) prog = kTmaF32Bias;
+            else if (f == (kEpiBias | kEpiGelu)) prog = kTmaF32BiasGelu;
+            else if (f == (kEpiBias | kEpiLayerScale)) prog = kTmaF32BiasLS;
+        } else {
+            if (f == 0) prog = kTmaHalf;
+            else if (f == kEpiBias) prog = kTmaHalfBias;
+            else if (f == (kEpiBias | kEpiGelu)) prog = kTmaHalfBiasGelu;
+            else if (f == (kEpiBias | kEpiRelu)) prog = kTmaHalfBiasRelu;
+        }
+        const bool aligned = reinterpret_cast<uintptr_t>(g.out) % 16 == 0 && (g.ldo * oes) % 16 == 0 &&
+                             (prog != kTmaF32BiasLS || reinterpret_cast<uintptr_t>(g.res1) % 16 == 0);
+        const bool params_aligned = (!(g.flags & kEpiDequant) || reinterpret_cast<uintptr_t>(g.s_w) % 16 == 0) &&
+                                    (!(g.flags & kEpiBias) || reinterpret_cast<uintptr_t>(g.bias) % 16 == 0) &&
+                                    (prog != kTmaF32BiasLS || reinterpret_cast<uintptr_t>(g.gamma) % 16 == 0);
+        if (prog != kTmaNone && aligned && params_aligned) {
+            const cuuint64_t dims[2] = {g.n, g.m};
+            const cuuint64_t strides[1] = {g.ldo * oes};
+            const cuuint32_t box[2] = {32, 32};
+            const CUtensorMapDataType t =
+                f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                    : (g.out_half_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+            const CUtensorMapSwizzle sw = f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+            if (int rc = make_map_typed(&mo, t, 2, g.out, dims, strides, box, sw)) return rc;
+            if (prog == kTmaF32BiasLS)
+                if (int rc = make_map_typed(&mr, t, 2, g.res1, dims, strides, box, sw)) return rc;
+            p.tma_program = prog;
+            staging = 16u * kStageBufBytes;
+        }
+    }
     const int mc = g.max_ctas;
     if (g.a_mode == kAModeRows) {
         switch (g.elem) {
-            case kElemS8: return dispatch_bn<kElemS8, kAModeRows>(bn, ma, mb, p, mc, st);
-            case kElemF16: return dispatch_bn<kElemF16, kAModeRows>(bn, ma, mb, p, mc, st);
-            default: return dispatch_bn<kElemBF16, kAModeRows>(bn, ma, mb, p, mc, st);
+            case kElemS8: return dispatch_bn<kElemS8, kAModeRows>(bn, ma, mb, mo, mr, p, staging, mc, st);
+            case kElemF16: return dispatch_bn<kElemF16, kAModeRows>(bn, ma, mb, mo, mr, p, staging, mc, st);
+            default: return dispatch_bn<kElemBF16, kAModeRows>(bn, ma, mb, mo, mr, p, staging, mc, st);
         }
     }
     switch (g.elem) {
-        case kElemS8: return dispatch_bn<kElemS8, kAModeConv3x3>(bn, ma, mb, p, mc, st);
-        case kElemF16: return dispatch_bn<kElemF16, kAModeConv3x3>(bn, ma, mb, p, mc, st);
-        default: return dispatch_bn<kElemBF16, kAModeConv3x3>(bn, ma, mb, p, mc, st);
+        case kElemS8: return dispatch_bn<kElemS8, kAModeConv3x3>(bn, ma, mb, mo, mr, p, staging, mc, st);
+        case kElemF16: return dispatch_bn<kElemF16, kAModeConv3x3>(bn, ma, mb, mo, mr, p, staging, mc, st);
+        default: return dispatch_bn<kElemBF16, kAModeConv3x3>(bn, ma, mb, mo, mr, p, staging, mc, st);
     }
 }
 

@@ -557,6 +557,44 @@ __global__ void __launch_bounds__(128) quantize_rows_kernel(uint32_t* __restrict
     }
 }
 
+// Register-resident form of the same quantizer for half rows whose width
+// is a multiple of 1024: each of the 128 threads holds VEC x 8 values
+// (16-byte loads), so the row is read from HBM once and written once.
+template <int VEC>
+__global__ void __launch_bounds__(128) quantize_rows_half_vec_kernel(uint32_t* __restrict__ packed,
+                                                                     float* __restrict__ scales,
+                                                                     const __half* __restrict__ in, uint32_t cols,
+                                                                     uint32_t row_stride, uint32_t out_words) {
+    __shared__ float red[4];
+    const uint64_t row = blockIdx.x;
+    const uint4* x = reinterpret_cast<const uint4*>(in + row * (uint64_t)row_stride);
+    float v[VEC][8];
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+        const uint4 q = __ldcs(x + threadIdx.x + 128 * i);
+        const __half2* h = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(h[j]);
+            v[i][2 * j] = f.x;
+            v[i][2 * j + 1] = f.y;
+            m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+    }
+    m = block_max_128(m, red);
+    const float scale = fmaxf(m / 127.0f, 1.0e-8f);
+    if (threadIdx.x == 0) scales[row] = scale;
+    uint2* o = reinterpret_cast<uint2*>(packed + row * out_words);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+        uint2 w;
+        w.x = q8(v[i][0] / scale) | (q8(v[i][1] / scale) << 8) | (q8(v[i][2] / scale) << 16) | (q8(v[i][3] / scale) << 24);
+        w.y = q8(v[i][4] / scale) | (q8(v[i][5] / scale) << 8) | (q8(v[i][6] / scale) << 16) | (q8(v[i][7] / scale) << 24);
+        o[threadIdx.x + 128 * i] = w;
+    }
+}
+
 // im2col_quantize_int8.glsl:26-84 on planar [C,H,W] input: row = output
 // pixel, column = c*k*k + ky*k + kx, zero padding; code = rint(clamp(x *
 // (1/scale))). Rows are written out_words words apart (>= ceil(K/4));
@@ -737,6 +775,24 @@ int launch_quantize_rows(uint32_t* packed, float* scales, const T* in, uint64_t 
                          uint64_t offset, uint32_t group, uint64_t group_stride, uint32_t row_stride,
                          uint32_t out_words, cudaStream_t st) {
     if (rows == 0) return DAV2CUDA_OK;
+    if constexpr (std::is_same<T, __half>::value) {
+        const bool plain = offset == 0 && (group == rows || group_stride == (uint64_t)group * row_stride);
+        const bool aligned = (reinterpret_cast<uintptr_t>(in) % 16 == 0) && (row_stride % 8 == 0) &&
+                             (reinterpret_cast<uintptr_t>(packed) % 8 == 0) && out_words == cols / 4;
+        if (plain && aligned && cols % 1024 == 0 && cols <= 8192) {
+            switch (cols / 1024) {
+                case 1: quantize_rows_half_vec_kernel<1><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, row_stride, out_words); break;
+                case 2: quantize_rows_half_vec_kernel<2><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, row_stride, out_words); break;
+                case 3: quantize_rows_half_vec_kernel<3><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, row_stride, out_words); break;
+                case 4: quantize_rows_half_vec_kernel<4><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, row_stride, out_words); break;
+                case 6: quantize_rows_half_vec_kernel<6><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, row_stride, out_words); break;
+                case 8: quantize_rows_half_vec_kernel<8><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, row_stride, out_words); break;
+                default: goto generic;
+            }
+            return check_launch("quantize_rows_half_vec");
+        }
+    }
+generic:
     quantize_rows_kernel<T><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, offset, group, group_stride,
                                                             row_stride, out_words);
     return check_launch("quantize_rows");

@@ -95,6 +95,8 @@ int launch_half_weight(H* out, const float* w, int kind, uint64_t rows, uint32_t
 int launch_expand_bias(float* out, const float* bias, uint32_t co, uint32_t reps, cudaStream_t st);
 
 // ------------------------------------------------------------- attention
+int launch_attention_tc(__half* out, const __half* qkv, uint32_t batch, uint32_t tokens, uint32_t heads,
+                        uint64_t qkv_ld, uint64_t out_ld, cudaStream_t st);
 template <typename H>
 int launch_attention(H* out, const H* qkv, uint32_t batch, uint32_t tokens, uint32_t heads, uint64_t qkv_ld,
                      uint64_t out_ld, cudaStream_t st);

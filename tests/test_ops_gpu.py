@@ -361,7 +361,8 @@ def test_attention_reference_kat(cuda, dav2lib):
     assert np.abs(host(out) - oracle.attention_head64(qkv, T, Hh)).max() <= 3e-4
 
 
-@pytest.mark.parametrize("batch,tokens,heads", [(1, 1370, 6), (2, 130, 16), (1, 63, 2), (1, 5477, 1)])
+@pytest.mark.parametrize("batch,tokens,heads", [(1, 1370, 6), (2, 130, 16), (1, 63, 2), (1, 5477, 1),
+                                                 (1, 1300, 2), (3, 384, 3)])
 def test_attention(cuda, dav2lib, batch, tokens, heads):
     qkv = (rng(tokens).standard_normal((batch, tokens, 3 * heads * 64)) * 0.5).astype(np.float32)
     ws = dav2lib.dav2cuda_attention_head64_workspace_size(batch, tokens, heads)

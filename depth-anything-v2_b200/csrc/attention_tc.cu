@@ -4,25 +4,33 @@
 // the [heads, T, T] scores.
 //
 // One CTA = one (image, head, 256-query block) = two 128-query tiles that
-// share every K/V block; 576 threads, one CTA per SM (a kernel that allocates
-// tensor memory is resident once per SM), all 512 TMEM columns:
-// tile t uses columns 256t + [0,128) for S and 256t + 128 + 64*(j%2) for O_j.
+// share every K/V block; 608 threads, one CTA per SM (a kernel that allocates
+// tensor memory is resident once per SM), all 512 TMEM columns: tile t uses
+// columns 256t + [0,128) for S and 256t + 128 + 64h for O_h, h = key half.
 //   warp 0       TMA: the Q tiles once, then K_j / V_j (128 keys x 64 dims
 //                each) into a 3-stage ring. The 3-D tensor map over qkv
 //                [B][T][3E] zero-fills rows past T.
-//   warp 1       MMA issuer, alternating the tiles: S = Q K_j^T (M=128, N=128,
-//                K=64); once tile t has published P_j it queues S_{j+1} of that
-//                tile first, then O_j = P_j V_j (M=128, N=64, K=128; V read as an
-//                MN-major operand). While one tile's softmax runs, the tensor
-//                core works for the other.
-//   warps 2..9   softmax of tile 0, warps 10..17 of tile 1: two warps per
-//                query row (TMEM lane), 64 keys each (row maxima combined
-//                through shared memory): pass 1 over S for the row maximum,
-//                pass 2 for exp2(s*c - m) -> P_j (f16) written to a 128-byte-
-//                swizzled shared tile, row sum l; then O_{j-1} (complete by
-//                then) is read from TMEM and accumulated in registers with the
-//                running correction o = o*exp2(m_old - m_new) + O. Full key
-//                blocks skip the key-range mask. Finally o / l.
+//   warps 1, 18  MMA issuers, one per tile (so neither tile's pipeline waits
+//                on the other; a K/V stage is released once both have
+//                committed): S_{j+1} = Q K_{j+1}^T
+//                (M=128, N=128, K=64) as soon as the tile's softmax holds S_j in
+//                registers, so it is computed while that softmax works on block
+//                j; then, once P_j is published, O_h += P_j[:, 64h:64h+64]
+//                V_j[64h:64h+64, :] for both key halves (M=128, N=64, K=64; V
+//                read as an MN-major operand), accumulating in TMEM across key
+//                blocks.
+//   warps 2..9   softmax of tile 0, warps 10..17 of tile 1: two warps per query
+//                row (TMEM lane), warp half h owning keys [64h, 64h+64) of every
+//                block with its own running maximum m_h, sum l_h and O_h — an
+//                independent online softmax per key half, merged once at the
+//                end. Per block: S loaded once into registers, row maximum,
+//                P = exp2(s*c - m*c) (f16) into a 128-byte-swizzled shared tile,
+//                l_h += sum(P). The maximum used for P is only raised when the
+//                block maximum exceeds it by more than 8 (log2 units): P stays
+//                <= 2^8 and O_h in TMEM is rescaled only on those rare raises.
+//                Full key blocks skip the key-range mask. The two tiles take
+//                turns for the exponentials (the issue- and MUFU-heavy phase), so each
+//                tile's other work overlaps the other tile's exp phase.
 // Ordering between the roles uses mbarriers; every wait is bounded and a
 // timeout sets the device error word instead of hanging.
 #include "kernels.cuh"
@@ -31,7 +39,6 @@
 
 #include <cstdio>
 #include <mutex>
-#include <type_traits>
 
 namespace dav2cuda {
 namespace {
@@ -46,18 +53,31 @@ struct AttnParams {
 constexpr uint32_t kQTiles = 2;       // 128-query tiles per CTA
 constexpr uint32_t kQ = 128 * kQTiles;  // queries per CTA
 constexpr uint32_t kKV = 128;         // keys per block
-constexpr uint32_t kStages = 3;       // K/V ring depth
+// K/V ring depth and P buffers per tile (P_j in buffer j % kPBufs). Measured
+// on B200 (ViT-L, 64 images): 3 stages x 1 P buffer beats 2 x 2 (the only
+// double-buffered-P layout that fits), whose K/V ring runs dry.
+constexpr uint32_t kStages = 3;
+constexpr uint32_t kPBufs = 1;
 constexpr uint32_t kTile = 128 * 128; // bytes of a 128 x 64 f16 tile
-constexpr uint32_t kThreads = 64 + 256 * kQTiles;
-// Q[2], K[3], V[3], P[2 tiles][2 atoms], 1 KB barriers, 1 KB maxima exchange
-constexpr uint32_t kSmem = kTile * (kQTiles + 2 * kStages + 2 * kQTiles) + 2048;
+constexpr uint32_t kThreads = 64 + 256 * kQTiles + 32;  // TMA, MMA(tile 0), softmax, MMA(tile 1)
+constexpr uint32_t kMma1Warp = 2 + 8 * kQTiles;
+// Q[tile], K[stage], V[stage], P[tile][buffer][key half], 1 KB barriers
+constexpr uint32_t kSmem = kTile * (kQTiles + 2 * kStages + 2 * kPBufs * kQTiles) + 1024;
+constexpr uint32_t kBarrierBytes = 8 * (2 * kStages + (7 + kPBufs) * kQTiles) + 8;
+static_assert(kBarrierBytes <= 1024, "barrier block overflows its 1 KB");
+static_assert(kSmem <= 232448, "shared memory above the per-block limit");
 
-__device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(taddr, r);
-    tmem_ld_wait();
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+// 8-column TMEM row access (the rare O rescale; keeps register use low)
+__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st_x8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -85,20 +105,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* sQ = smem;                                // [tile]
     uint8_t* sK = smem + kQTiles * kTile;              // [stage]
     uint8_t* sV = sK + kStages * kTile;                // [stage]
-    uint8_t* sP = sV + kStages * kTile;                // [tile][2 atoms]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kQTiles * kTile);
-    uint64_t* q_full = bars + 0;     // [tile]
-    uint64_t* kv_full = bars + 2;    // [stage]
-    uint64_t* kv_empty = bars + 5;   // [stage]
-    uint64_t* s_full = bars + 8;     // [tile]
-    uint64_t* p_full = bars + 10;    // [tile]
-    uint64_t* p_empty = bars + 12;   // [tile]
-    uint64_t* o_full = bars + 14;    // [tile][2]
-    uint64_t* o_empty = bars + 18;   // [tile][2]
-    uint64_t* drain = bars + 22;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 24);
-    __half* red = reinterpret_cast<__half*>(bars + 128);  // [tile][half][128 rows] row maxima (f16, rounded up)
+    uint8_t* sP = sV + kStages * kTile;                // [tile][buffer][key half]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBufs * kQTiles * kTile);
+    uint64_t* q_full = bars;                   // [tile]
+    uint64_t* kv_full = q_full + kQTiles;      // [stage]
+    uint64_t* kv_empty = kv_full + kStages;    // [stage]
+    uint64_t* s_full = kv_empty + kStages;     // [tile]
+    uint64_t* s_empty = s_full + kQTiles;      // [tile]
+    uint64_t* p_full = s_empty + kQTiles;      // [tile]
+    uint64_t* p_empty = p_full + kQTiles;      // [tile][buffer]
+    uint64_t* o_full = p_empty + kPBufs * kQTiles;  // [tile]
+    uint64_t* drain = o_full + kQTiles;        // [tile]
+    uint64_t* turn = drain + kQTiles;          // [tile]: the tile may run its exp phase
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + kQTiles);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const uint32_t q0 = blockIdx.x * kQ, head = blockIdx.y, img = blockIdx.z;
     const uint32_t E = p.heads * 64u;
@@ -110,17 +130,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&q_full[t], 1);
             mbar_init(&s_full[t], 1);
             mbar_init(&p_full[t], 8);
-            mbar_init(&p_empty[t], 1);
-            mbar_init(&o_full[2 * t], 1);
-            mbar_init(&o_full[2 * t + 1], 1);
-            mbar_init(&o_empty[2 * t], 8);
-            mbar_init(&o_empty[2 * t + 1], 8);
+            for (uint32_t b = 0; b < kPBufs; ++b) mbar_init(&p_empty[kPBufs * t + b], 1);
+            mbar_init(&o_full[t], 1);
+            mbar_init(&s_empty[t], 8);
+            mbar_init(&drain[t], 1);
+            mbar_init(&turn[t], 8);
         }
         for (uint32_t st = 0; st < kStages; ++st) {
             mbar_init(&kv_full[st], 1);
-            mbar_init(&kv_empty[st], 1);
+            mbar_init(&kv_empty[st], ntiles);  // released by every active tile's MMA issuer
         }
-        mbar_init(drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -146,12 +165,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_load_3d(sV + st * kTile, &tm, &kv_full[st], (int)(2 * E + head * 64u), (int)(j * kKV), (int)img);
             }
         }
-    } else if (warp == 1) {
-        if (lane == 0) {
+    } else if (warp == 1 || warp == kMma1Warp) {
+        // one MMA issuer per tile, so that neither tile's pipeline waits on the other
+        const uint32_t t = warp == 1 ? 0u : 1u;
+        if (lane == 0 && t < ntiles) {
             constexpr uint32_t idesc_s = make_idesc(1u, 0u, 128u, 128u);
             constexpr uint32_t idesc_o = make_idesc(1u, 0u, 128u, 64u) | (1u << 16);  // B (V) MN-major
-            auto issue_s = [&](uint32_t t, uint32_t j) {
-                const uint32_t q_addr = smem_addr(sQ + t * kTile);
+            const uint32_t q_addr = smem_addr(sQ + t * kTile);
+            auto issue_s = [&](uint32_t j) {
                 const uint32_t k_addr = smem_addr(sK + (j % kStages) * kTile);
 #pragma unroll
                 for (uint32_t kk = 0; kk < 4; ++kk)
@@ -159,64 +180,62 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 idesc_s, kk ? 1u : 0u);
                 umma_commit(&s_full[t]);
             };
-            auto issue_o = [&](uint32_t t, uint32_t j) {
-                const uint32_t p_addr = smem_addr(sP + 2u * t * kTile);
+            auto issue_o = [&](uint32_t j) {
                 const uint32_t v_addr = smem_addr(sV + (j % kStages) * kTile);
 #pragma unroll
-                for (uint32_t kk = 0; kk < 8; ++kk)
-                    umma<false>(tmem + 256u * t + 128u + 64u * (j & 1u),
-                                smem_desc_sw128(p_addr + (kk >> 2) * kTile + 32u * (kk & 3u)),
-                                desc_mn_sw128(v_addr + kk * 2048u), idesc_o, kk ? 1u : 0u);
-                umma_commit(&o_full[2 * t + (j & 1u)]);
-                umma_commit(&p_empty[t]);
+                for (uint32_t h = 0; h < 2; ++h) {
+                    const uint32_t p_addr = smem_addr(sP + ((kPBufs * t + j % kPBufs) * 2u + h) * kTile);
+#pragma unroll
+                    for (uint32_t kk = 0; kk < 4; ++kk)
+                        umma<false>(tmem + 256u * t + 128u + 64u * h, smem_desc_sw128(p_addr + 32u * kk),
+                                    desc_mn_sw128(v_addr + (4u * h + kk) * 2048u), idesc_o, (j | kk) ? 1u : 0u);
+                }
+                umma_commit(&o_full[t]);
+                umma_commit(&p_empty[kPBufs * t + j % kPBufs]);
+                umma_commit(&kv_empty[j % kStages]);
             };
-            bool ok = mbar_wait(&kv_full[0], 0, abort_flag, p.err);
-            for (uint32_t t = 0; ok && t < ntiles; ++t) {
-                ok = mbar_wait(&q_full[t], 0, abort_flag, p.err);
-                if (!ok) break;
+            bool ok = mbar_wait(&kv_full[0], 0, abort_flag, p.err) && mbar_wait(&q_full[t], 0, abort_flag, p.err);
+            if (ok) {
                 tc_fence_after();
-                issue_s(t, 0);
+                issue_s(0);
                 mma_issued = true;
             }
             for (uint32_t j = 0; ok && j < nkb; ++j) {
+                // S_{j+1} as soon as the softmax holds S_j in registers (it is
+                // computed while that softmax works on block j) ...
                 if (j + 1 < nkb) {
-                    ok = mbar_wait(&kv_full[(j + 1) % kStages], ((j + 1) / kStages) & 1u, abort_flag, p.err);
-                    if (!ok) break;
-                }
-                for (uint32_t t = 0; ok && t < ntiles; ++t) {
-                    // P_j of tile t ready (its softmax has also finished reading S_j):
-                    // queue S_{j+1} first so that softmax can start on it, then O_j.
-                    ok = mbar_wait(&p_full[t], j & 1u, abort_flag, p.err);
+                    ok = mbar_wait(&kv_full[(j + 1) % kStages], ((j + 1) / kStages) & 1u, abort_flag, p.err) &&
+                         mbar_wait(&s_empty[t], j & 1u, abort_flag, p.err);
                     if (!ok) break;
                     tc_fence_after();
-                    if (j + 1 < nkb) issue_s(t, j + 1);
-                    // O buffer j%2 of tile t was last used by block j-2
-                    ok = mbar_wait(&o_empty[2 * t + (j & 1u)], ((j >> 1) & 1u) ^ 1u, abort_flag, p.err);
-                    if (!ok) break;
-                    tc_fence_after();
-                    issue_o(t, j);
+                    issue_s(j + 1);
                 }
-                if (ok) umma_commit(&kv_empty[j % kStages]);
+                // ... and the O updates of block j once its P is published (the
+                // softmax has also rescaled O by then, if it had to)
+                ok = mbar_wait(&p_full[t], j & 1u, abort_flag, p.err);
+                if (!ok) break;
+                tc_fence_after();
+                issue_o(j);
             }
         }
     } else if ((warp - 2u) / 8u < ntiles) {
-        // softmax: two warps per TMEM lane quarter of tile t; `half` selects keys
-        // [64*half, 64*half+64) of S and dims [32*half, 32*half+32) of O.
         const uint32_t t = (warp - 2u) / 8u;
         const uint32_t quarter = warp & 3u;
         const uint32_t half = ((warp - 2u) >> 2) & 1u;
         const uint32_t row = quarter * 32u + lane;
-        const uint32_t tb = tmem + 256u * t + ((quarter * 32u) << 16);
+        const uint32_t tS = tmem + 256u * t + ((quarter * 32u) << 16);  // S of this lane quarter
+        const uint32_t tO = tS + 128u + 64u * half;                      // this key half's O
         const uint32_t pair_id = t * 4u + quarter;  // named barrier 1 + pair_id, shared by the two warps
         const float c = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
-        __half* my_red = red + (2u * t + half) * 128u + row;
-        __half* partner_red = red + (2u * t + (half ^ 1u)) * 128u + row;
-        uint8_t* atom = sP + (2u * t + half) * kTile + row * 128u;
-        float o[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = 0.f;
-        float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+        constexpr float kRaise = 8.0f;                 // raise the maximum only beyond 2^8
+        uint8_t* atoms = sP + (kPBufs * t * 2u + half) * kTile + row * 128u;  // + 2*kTile per buffer
+        float m = -INFINITY, l = 0.f;
         bool ok = true;
+        // warp-uniform wait: on a timeout every lane leaves together, so the
+        // warp-collective TMEM accesses and votes below never diverge
+        auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+            return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.err));
+        };
         // literal barrier ids keep the CTA's named-barrier count small
         auto pair_sync = [&]() {
             switch (pair_id) {
@@ -230,131 +249,147 @@ __global__ void __launch_bounds__(kThreads, 1)
                 default: asm volatile("bar.sync 8, 64;" ::: "memory"); break;
             }
         };
-        auto accumulate = [&](uint32_t b, float alpha_b) -> bool {
-            if (!mbar_wait(&o_full[2 * t + (b & 1u)], (b >> 1) & 1u, abort_flag, p.err)) return false;
+        for (uint32_t j = 0; j < nkb; ++j) {
+            if (!warp_wait(&s_full[t], j & 1u)) {
+                ok = false;
+                break;
+            }
             tc_fence_after();
-            float ov[32];
-            tmem_ld_x32(tb + 128u + 64u * (b & 1u) + 32u * half, ov);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = fmaf(o[i], alpha_b, ov[i]);
+            uint32_t sr[2][32];
+            tmem_ld_32x32b_x32(tS + 64u * half, sr[0]);
+            tmem_ld_32x32b_x32(tS + 64u * half + 32u, sr[1]);
+            tmem_ld_wait();
+            // S_j is in registers: its TMEM columns may take S_{j+1}
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&o_empty[2 * t + (b & 1u)]);
-            return true;
-        };
-        // pass 1 / pass 2 over this warp's 64 keys; kMask limits them to keys < T
-        auto row_max = [&](auto mask_tag, uint32_t kbase, float mx) -> float {
-            constexpr bool kMask = decltype(mask_tag)::value;
-#pragma unroll 1
-            for (uint32_t cc = 0; cc < 2; ++cc) {
-                float s[32];
-                tmem_ld_x32(tb + 64u * half + cc * 32u, s);
+            if (lane == 0) mbar_arrive(&s_empty[t]);
+            float s[64];
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (!kMask || kbase + cc * 32u + i < p.tokens) mx = fmaxf(mx, s[i]);
+            for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(sr[i >> 5][i & 31]);
+            const uint32_t kbase = j * kKV + 64u * half;
+            if (kbase + 64u > p.tokens) {  // tail block: keys >= T do not exist
+#pragma unroll
+                for (int i = 0; i < 64; ++i)
+                    if (kbase + i >= p.tokens) s[i] = -INFINITY;
             }
-            return mx;
-        };
-        auto exp_pass = [&](auto mask_tag, uint32_t kbase, float mc) -> float {
-            constexpr bool kMask = decltype(mask_tag)::value;
-            float ls = 0.f;
-#pragma unroll 1
-            for (uint32_t cc = 0; cc < 2; ++cc) {
-                float s[32];
-                tmem_ld_x32(tb + 64u * half + cc * 32u, s);
-                uint32_t h[16];
+            // row maximum by a tree (short dependency chains)
+            float mt[16];
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    float p0 = ex2_approx(fmaf(s[i], c, -mc));
-                    float p1 = ex2_approx(fmaf(s[i + 1], c, -mc));
-                    if (kMask) {
-                        if (kbase + cc * 32u + i >= p.tokens) p0 = 0.f;
-                        if (kbase + cc * 32u + i + 1 >= p.tokens) p1 = 0.f;
+            for (int i = 0; i < 16; ++i) mt[i] = fmaxf(fmaxf(s[i], s[i + 16]), fmaxf(s[i + 32], s[i + 48]));
+#pragma unroll
+            for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+                for (int i = 0; i < w; ++i) mt[i] = fmaxf(mt[i], mt[i + w]);
+            const float mx = fmaxf(m, mt[0]);
+            if (j == 0) {
+                m = mx;
+            } else {
+                const bool raise = (mx - m) * c > kRaise;  // false while both are -inf
+                if (__any_sync(0xffffffffu, raise)) {
+                    // O_h must hold blocks 0..j-1 before it is rescaled
+                    if (!warp_wait(&o_full[t], (j - 1) & 1u)) {
+                        ok = false;
+                        break;
                     }
+                    tc_fence_after();
+                    const float alpha = raise ? ex2_approx((m - mx) * c) : 1.0f;
+#pragma unroll 1
+                    for (uint32_t k = 0; k < 8; ++k) {
+                        uint32_t ov[8];
+                        tmem_ld_x8(tO + 8u * k, ov);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+                        tmem_st_x8(tO + 8u * k, ov);
+                    }
+                    tmem_st_wait();
+                    if (raise) {
+                        l *= alpha;
+                        m = mx;
+                    }
+                }
+            }
+            const float mc = m == -INFINITY ? 0.f : m * c;  // a half with no key yet has P = 0
+            // the MMA that last read this P buffer (block j - kPBufs) must be done
+            if (!warp_wait(&p_empty[kPBufs * t + j % kPBufs], ((j / kPBufs) & 1u) ^ 1u)) {
+                ok = false;
+                break;
+            }
+            // ping-pong: with two tiles the exp phases alternate (tile 0 block j,
+            // tile 1 block j, tile 0 block j+1, ...), so that each tile's max,
+            // loads and waits overlap the other tile's exponentials
+            if (ntiles == 2 && (t == 1 || j > 0) && !warp_wait(&turn[t], (t == 0 ? j - 1 : j) & 1u)) {
+                ok = false;
+                break;
+            }
+            float ls = 0.f;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                uint32_t h[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float p0 = ex2_approx(fmaf(s[8 * q + 2 * u], c, -mc));
+                    const float p1 = ex2_approx(fmaf(s[8 * q + 2 * u + 1], c, -mc));
                     ls += p0 + p1;
                     __half2 hh = __floats2half2_rn(p0, p1);
-                    h[i >> 1] = *reinterpret_cast<uint32_t*>(&hh);
+                    h[u] = *reinterpret_cast<uint32_t*>(&hh);
                 }
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint32_t chunk = cc * 4u + q;
-                    *reinterpret_cast<uint4*>(atom + ((chunk ^ (row & 7u)) << 4)) =
-                        make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
-                }
+                *reinterpret_cast<uint4*>(atoms + (j % kPBufs) * 2u * kTile + (((uint32_t)q ^ (row & 7u)) << 4)) =
+                    make_uint4(h[0], h[1], h[2], h[3]);
             }
-            return ls;
-        };
-        for (uint32_t j = 0; j < nkb; ++j) {
-            if (!mbar_wait(&s_full[t], j & 1u, abort_flag, p.err)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const uint32_t kbase = j * kKV + 64u * half;
-            const bool full = kbase + 64u <= p.tokens;
-            float mx = full ? row_max(std::false_type{}, kbase, m) : row_max(std::true_type{}, kbase, m);
-            // common row maximum: both warps round their partial maximum up to
-            // f16, exchange it and take the larger, so they use the identical
-            // value (>= the true maximum: every exp2 argument stays <= 0)
-            const __half mine = __float2half_ru(mx);
-            *my_red = mine;
-            pair_sync();
-            mx = __half2float(__hmax(mine, *partner_red));
-            pair_sync();  // both have read before the next block overwrites
-            const float alpha = ex2_approx((m - mx) * c);  // 0 on the first block
-            m = mx;
-            const float mc = m * c;
-            // P of the previous block must have been consumed by its MMA
-            if (!mbar_wait(&p_empty[t], (j & 1u) ^ 1u, abort_flag, p.err)) {
-                ok = false;
-                break;
-            }
-            const float ls = full ? exp_pass(std::false_type{}, kbase, mc) : exp_pass(std::true_type{}, kbase, mc);
-            l = l * alpha + ls;
+            l += ls;
             tc_fence_before();
             fence_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[t]);
-            // the previous block's O is complete by now (its P was released)
-            if (j > 0 && !accumulate(j - 1, alpha_prev)) {
-                ok = false;
-                break;
+            if (lane == 0) {
+                mbar_arrive(&p_full[t]);
+                if (ntiles == 2) mbar_arrive(&turn[t ^ 1u]);
             }
-            alpha_prev = alpha;
         }
-        if (ok && nkb > 0) ok = accumulate(nkb - 1, alpha_prev);
-        // row sum = both halves' partial sums (same maximum); the tile's P
-        // region is free once its last O MMA has completed
-        float* lx = reinterpret_cast<float*>(sP + 2u * t * kTile);
-        lx[half * 128u + row] = l;
+        // merge the two key halves: m = max(m0, m1), weights exp2((m_h - m) c)
+        if (ok && nkb > 0) ok = warp_wait(&o_full[t], (nkb - 1) & 1u);
+        tc_fence_after();
+        float* xch = reinterpret_cast<float*>(sP + kPBufs * t * 2u * kTile);  // free once the last O MMA completed
+        xch[half * 128u + row] = m;
+        xch[256u + half * 128u + row] = l;
         pair_sync();
-        l += lx[(half ^ 1u) * 128u + row];
+        const float m_o = xch[(half ^ 1u) * 128u + row];
+        const float l_o = xch[256u + (half ^ 1u) * 128u + row];
+        const float mm = fmaxf(m, m_o);
+        const float f_own = ex2_approx((m - mm) * c), f_oth = ex2_approx((m_o - mm) * c);
+        const float inv = 1.0f / fmaxf(l * f_own + l_o * f_oth, 1.0e-30f);
+        // this warp writes output dims [32*half, 32*half+32): its own O_h and the
+        // partner's O_{1-h} for those dims
+        uint32_t oa[32], ob[32];
+        tmem_ld_32x32b_x32(tO + 32u * half, oa);
+        tmem_ld_32x32b_x32(tS + 128u + 64u * (half ^ 1u) + 32u * half, ob);
+        tmem_ld_wait();
         const uint32_t qrow = q0 + 128u * t + row;
         if (ok && qrow < p.tokens) {
-            const float inv = 1.0f / fmaxf(l, 1.0e-20f);
+            const float wa = f_own * inv, wb = f_oth * inv;
             __half* dst = p.out + ((uint64_t)img * p.tokens + qrow) * p.out_ld + head * 64u + half * 32u;
 #pragma unroll
             for (int i = 0; i < 32; i += 8) {
-                uint4 w;
-                __half2 a = __floats2half2_rn(o[i] * inv, o[i + 1] * inv);
-                __half2 b = __floats2half2_rn(o[i + 2] * inv, o[i + 3] * inv);
-                __half2 cc2 = __floats2half2_rn(o[i + 4] * inv, o[i + 5] * inv);
-                __half2 d = __floats2half2_rn(o[i + 6] * inv, o[i + 7] * inv);
-                w.x = *reinterpret_cast<uint32_t*>(&a);
-                w.y = *reinterpret_cast<uint32_t*>(&b);
-                w.z = *reinterpret_cast<uint32_t*>(&cc2);
-                w.w = *reinterpret_cast<uint32_t*>(&d);
-                *reinterpret_cast<uint4*>(dst + i) = w;
+                uint32_t w[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float x0 = __uint_as_float(oa[i + 2 * u]) * wa + __uint_as_float(ob[i + 2 * u]) * wb;
+                    const float x1 = __uint_as_float(oa[i + 2 * u + 1]) * wa + __uint_as_float(ob[i + 2 * u + 1]) * wb;
+                    __half2 hh = __floats2half2_rn(x0, x1);
+                    w[u] = *reinterpret_cast<uint32_t*>(&hh);
+                }
+                *reinterpret_cast<uint4*>(dst + i) = make_uint4(w[0], w[1], w[2], w[3]);
             }
         }
     }
 
     __syncthreads();
     if (*abort_flag) {
-        if (warp == 1 && lane == 0 && mma_issued) {
-            umma_commit(drain);
+        if ((warp == 1 || warp == kMma1Warp) && lane == 0 && mma_issued) {
+            uint64_t* d = &drain[warp == 1 ? 0 : 1];
+            umma_commit(d);
             const unsigned long long t0 = globaltimer();
-            while (!mbar_try_wait(smem_addr(drain), 0) && globaltimer() - t0 < 100000000ull) {
+            while (!mbar_try_wait(smem_addr(d), 0) && globaltimer() - t0 < 100000000ull) {
             }
         }
         if (threadIdx.x == 0) {

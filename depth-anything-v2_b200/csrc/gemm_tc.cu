@@ -490,7 +490,7 @@ enum TmaProgram : int {
     kTmaF32BiasLS,  // attention projection, fc2
 };
 
-constexpr uint32_t kStageBufBytes = 4096;  // one 32-row box: 32 x 128 B (f32) or 32 x 64 B (f16)
+constexpr uint32_t kStageBufBytes = 2048;  // one 32-row box of 64-byte rows (32 f16 or 16 f32 columns)
 
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 
@@ -511,23 +511,26 @@ __device__ __forceinline__ void dequant4(const uint32_t* acc, float si, const fl
     }
 }
 
-// One 32x32 chunk: registers -> swizzled staging box (residual, if any, is
-// already in the box).
+// One chunk (64 bytes of output per row: 16 f32 or 32 f16 columns):
+// registers -> 64-byte-swizzled staging box (the residual, if any, is
+// already in the box). Row `lane` is at lane*64; its 16-byte unit u sits at
+// unit u ^ ((lane >> 1) & 3), conflict-free for row-wise 16-byte writes.
 template <bool kInt8, bool F32, bool BIAS, bool GELU, bool LS, bool RELU>
-__device__ __forceinline__ void tma_chunk_compute(const GemmParamsDev& p, const uint32_t (&acc)[32], float si,
+__device__ __forceinline__ void tma_chunk_compute(const GemmParamsDev& p, const uint32_t* acc, float si,
                                                   uint32_t col0, uint8_t* box, uint32_t lane) {
     const bool hb = p.out_bf16 != 0;
-    if (F32) {
-        uint8_t* row = box + lane * 128u;
+    uint8_t* row = box + lane * 64u;
+    const uint32_t sw = (lane >> 1) & 3u;
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-            const uint32_t c = col0 + 4u * g;
+    for (int u = 0; u < 4; ++u) {
+        uint8_t* q = row + (((uint32_t)u ^ sw) << 4);
+        if (F32) {
+            const uint32_t c = col0 + 4u * u;
             float v[4];
-            dequant4<kInt8, BIAS, GELU>(&acc[4 * g], si, p.s_w, p.bias, c, v);
-            float4* q = reinterpret_cast<float4*>(row + (((uint32_t)g ^ (lane & 7u)) << 4));
+            dequant4<kInt8, BIAS, GELU>(acc + 4 * u, si, p.s_w, p.bias, c, v);
             if (LS) {
                 const float4 gm = ldg4(p.gamma + c);
-                const float4 r = *q;
+                const float4 r = *reinterpret_cast<const float4*>(q);
                 v[0] = __fadd_rn(r.x, __fmul_rn(v[0], gm.x));
                 v[1] = __fadd_rn(r.y, __fmul_rn(v[1], gm.y));
                 v[2] = __fadd_rn(r.z, __fmul_rn(v[2], gm.z));
@@ -537,38 +540,37 @@ __device__ __forceinline__ void tma_chunk_compute(const GemmParamsDev& p, const 
 #pragma unroll
                 for (int k = 0; k < 4; ++k) v[k] = fmaxf(v[k], 0.f);
             }
-            *q = make_float4(v[0], v[1], v[2], v[3]);
-        }
-    } else {
-        uint8_t* row = box + lane * 64u;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
+            *reinterpret_cast<float4*>(q) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
             const uint32_t c = col0 + 8u * u;
             float v[8];
-            dequant4<kInt8, BIAS, GELU>(&acc[8 * u], si, p.s_w, p.bias, c, v);
-            dequant4<kInt8, BIAS, GELU>(&acc[8 * u + 4], si, p.s_w, p.bias, c + 4u, v + 4);
+            dequant4<kInt8, BIAS, GELU>(acc + 8 * u, si, p.s_w, p.bias, c, v);
+            dequant4<kInt8, BIAS, GELU>(acc + 8 * u + 4, si, p.s_w, p.bias, c + 4u, v + 4);
             if (RELU) {
 #pragma unroll
                 for (int k = 0; k < 8; ++k) v[k] = fmaxf(v[k], 0.f);
             }
-            *reinterpret_cast<uint4*>(row + (((uint32_t)u ^ ((lane >> 1) & 3u)) << 4)) =
-                make_uint4(pack_half2(v[0], v[1], hb), pack_half2(v[2], v[3], hb), pack_half2(v[4], v[5], hb),
-                           pack_half2(v[6], v[7], hb));
+            *reinterpret_cast<uint4*>(q) = make_uint4(pack_half2(v[0], v[1], hb), pack_half2(v[2], v[3], hb),
+                                                      pack_half2(v[4], v[5], hb), pack_half2(v[6], v[7], hb));
         }
     }
 }
 
-// The epilogue warp's whole tile loop for one program. `bufs` is this
-// warp's pair of staging boxes, `rbar` its pair of residual mbarriers.
-template <int BN, bool kInt8, bool F32, bool BIAS, bool GELU, bool LS, bool RELU>
+// The epilogue warp's whole tile loop for one program. EPI epilogue warps:
+// EPI/4 per TMEM lane quarter, sharing the quarter's chunks round-robin.
+// `bufs` is this warp's pair of staging boxes, `rbar` its pair of residual
+// mbarriers.
+template <int BN, int EPI, bool kInt8, bool F32, bool BIAS, bool GELU, bool LS, bool RELU>
 __device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const CUtensorMap* tm_o, const CUtensorMap* tm_r,
                                                uint32_t tmem_base, uint64_t* tfull, uint64_t* tempty, uint64_t* rbar,
                                                uint8_t* bufs, volatile int* abort_flag, uint32_t warp,
                                                uint32_t lane) {
+    constexpr uint32_t CW = F32 ? 16u : 32u;           // columns per chunk
+    constexpr uint32_t kStride = (EPI / 4) * CW;        // column step between this warp's chunks
     const uint32_t quarter = warp & 3u;
-    const uint32_t half = (warp - 2u) >> 2;
+    const uint32_t sub = (warp - 2u) >> 2;
     const uint32_t num_tiles = p.num_m_tiles * p.num_n_tiles;
-    const uint32_t first_c = half * 32u;
+    const uint32_t first_c = sub * CW;
     const bool has_chunks = first_c < (uint32_t)BN;
     uint32_t seq = 0;  // chunks processed by this warp
     // residual box of chunk (tile, c) -> staging buffer b
@@ -591,62 +593,58 @@ __device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const CUt
         const float si = (kInt8 && r < p.m) ? __ldg(p.s_in + r) : 0.f;
         const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + buf * (uint32_t)BN;
         bool ok = true;
-        if (!has_chunks) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[buf]);
-            continue;
-        }
 #pragma unroll 1
-        for (uint32_t c = first_c; c < (uint32_t)BN && ok; c += 128u) {
-            uint32_t acc[2][32];
-            const bool two = c + 64u < (uint32_t)BN;
-            tmem_ld_32x32b_x32(taddr + c, acc[0]);
-            if (two) tmem_ld_32x32b_x32(taddr + c + 64u, acc[1]);
+        for (uint32_t c = first_c; c < (uint32_t)BN; c += kStride) {
+            uint32_t acc[CW];
+            if constexpr (CW == 32) {
+                tmem_ld_32x32b_x32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(acc));
+            } else {
+                tmem_ld_32x32b_x16(taddr + c, *reinterpret_cast<uint32_t(*)[16]>(acc));
+            }
             tmem_ld_wait();
-            if (c + 128u >= (uint32_t)BN) {  // last TMEM read of this tile: release the accumulator
+            if (c + kStride >= (uint32_t)BN) {  // last TMEM read of this tile: release the accumulator
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[buf]);
             }
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                if (h == 1 && !two) break;
-                const uint32_t cc = c + 64u * h;
-                const uint32_t b = seq & 1u;
-                uint8_t* box = bufs + b * kStageBufBytes;
-                if (LS) {
-                    if (lane == 0) {
-                        // prefetch the next chunk's residual into the other box, once
-                        // the store that last used that box has read it out
-                        uint32_t nt = tile, nc = cc + 64u;
-                        if (nc >= (uint32_t)BN) {
-                            nt = tile + gridDim.x;
-                            nc = first_c;
-                        }
-                        if (nt < num_tiles) {
-                            bulk_wait_group_read<0>();
-                            load_residual(nt, nc, b ^ 1u);
-                        }
-                    }
-                    if (!mbar_wait(&rbar[b], (seq >> 1) & 1u, abort_flag, p.err)) {
-                        ok = false;
-                        break;
-                    }
-                } else {
-                    if (lane == 0) bulk_wait_group_read<1>();
-                    __syncwarp();
-                }
-                const uint32_t col0 = n_blk * (uint32_t)BN + cc;
-                tma_chunk_compute<kInt8, F32, BIAS, GELU, LS, RELU>(p, acc[h], si, col0, box, lane);
-                fence_async_smem();
-                __syncwarp();
+            const uint32_t b = seq & 1u;
+            uint8_t* box = bufs + b * kStageBufBytes;
+            if (LS) {
                 if (lane == 0) {
-                    tma_store_2d(tm_o, box, (int)col0, (int)(m_blk * 128u + quarter * 32u));
-                    bulk_commit_group();
+                    // prefetch the next chunk's residual into the other box, once
+                    // the store that last used that box has read it out
+                    uint32_t nt = tile, nc = c + kStride;
+                    if (nc >= (uint32_t)BN) {
+                        nt = tile + gridDim.x;
+                        nc = first_c;
+                    }
+                    if (nt < num_tiles) {
+                        bulk_wait_group_read<0>();
+                        load_residual(nt, nc, b ^ 1u);
+                    }
                 }
-                ++seq;
+                if (!mbar_wait(&rbar[b], (seq >> 1) & 1u, abort_flag, p.err)) {
+                    ok = false;
+                    break;
+                }
+            } else {
+                if (lane == 0) bulk_wait_group_read<1>();
+                __syncwarp();
             }
+            const uint32_t col0 = n_blk * (uint32_t)BN + c;
+            tma_chunk_compute<kInt8, F32, BIAS, GELU, LS, RELU>(p, acc, si, col0, box, lane);
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(tm_o, box, (int)col0, (int)(m_blk * 128u + quarter * 32u));
+                bulk_commit_group();
+            }
+            ++seq;
+        }
+        if (!has_chunks) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
         }
         if (!ok) break;
     }
@@ -654,14 +652,14 @@ __device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const CUt
     __syncwarp();
 }
 
-template <int BN, bool kInt8>
+template <int BN, int EPI, bool kInt8>
 __device__ __forceinline__ void epilogue_tma_dispatch(const GemmParamsDev& p, const CUtensorMap* tm_o,
                                                       const CUtensorMap* tm_r, uint32_t tmem_base, uint64_t* tfull,
                                                       uint64_t* tempty, uint64_t* rbar, uint8_t* bufs,
                                                       volatile int* abort_flag, uint32_t warp, uint32_t lane) {
 #define DAV2_TMA_EPI(F32, BIAS, GELU, LS, RELU)                                                                      \
-    epilogue_tma_loop<BN, kInt8, F32, BIAS, GELU, LS, RELU>(p, tm_o, tm_r, tmem_base, tfull, tempty, rbar, bufs, \
-                                                            abort_flag, warp, lane)
+    epilogue_tma_loop<BN, EPI, kInt8, F32, BIAS, GELU, LS, RELU>(p, tm_o, tm_r, tmem_base, tfull, tempty, rbar, \
+                                                                 bufs, abort_flag, warp, lane)
     switch (p.tma_program) {
         case kTmaHalf: DAV2_TMA_EPI(false, false, false, false, false); break;
         case kTmaHalfBias: DAV2_TMA_EPI(false, true, false, false, false); break;
@@ -675,8 +673,8 @@ __device__ __forceinline__ void epilogue_tma_dispatch(const GemmParamsDev& p, co
 #undef DAV2_TMA_EPI
 }
 
-template <int BN, int ELEM, int AMODE>
-__global__ void __launch_bounds__(320, 1)
+template <int BN, int ELEM, int AMODE, int EPI>
+__global__ void __launch_bounds__(64 + 32 * EPI, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ CUtensorMap tm_r,
                    const __grid_constant__ GemmParamsDev p) {
@@ -698,8 +696,8 @@ __global__ void __launch_bounds__(320, 1)
     uint64_t* tfull = empty + kMaxStages;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
-    uint64_t* rbars = drain + 1;  // 8 epilogue warps x 2 residual barriers
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbars + 16);
+    uint64_t* rbars = drain + 1;  // epilogue warps x 2 residual barriers
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbars + 2 * EPI);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     uint8_t* staging = reinterpret_cast<uint8_t*>(full) + 1024;
     float* slabs = reinterpret_cast<float*>(staging);  // 8 x 32 x 33 floats (transposed-store path)
@@ -720,10 +718,10 @@ __global__ void __launch_bounds__(320, 1)
         }
         mbar_init(&tfull[0], 1);
         mbar_init(&tfull[1], 1);
-        mbar_init(&tempty[0], 8);
-        mbar_init(&tempty[1], 8);
+        mbar_init(&tempty[0], EPI);
+        mbar_init(&tempty[1], EPI);
         mbar_init(drain, 1);
-        for (int i = 0; i < 16; ++i) mbar_init(&rbars[i], 1);
+        for (int i = 0; i < 2 * EPI; ++i) mbar_init(&rbars[i], 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -804,10 +802,10 @@ __global__ void __launch_bounds__(320, 1)
             }
         }
     } else if (AMODE == kAModeRows && p.tma_program != kTmaNone) {
-        if constexpr (AMODE == kAModeRows)
-            epilogue_tma_dispatch<BN, kInt8>(p, &tm_o, &tm_r, tmem_base, tfull, tempty, rbars + 2u * (warp - 2u),
-                                             staging + 2u * kStageBufBytes * (warp - 2u), abort_flag, warp, lane);
-    } else {
+        if constexpr (AMODE == kAModeRows && EPI == 16)
+            epilogue_tma_dispatch<BN, EPI, kInt8>(p, &tm_o, &tm_r, tmem_base, tfull, tempty, rbars + 2u * (warp - 2u),
+                                                  staging + 2u * kStageBufBytes * (warp - 2u), abort_flag, warp, lane);
+    } else if constexpr (EPI == 8) {
         // warps 2..9: two warps per TMEM lane quarter, splitting the chunks
         const uint32_t quarter = warp & 3u;
         const uint32_t half = (warp - 2u) >> 2;  // 0 or 1
@@ -937,10 +935,10 @@ size_t smem_for(int bn, uint32_t stages, uint32_t staging) {
 
 int g_num_sms = 0;
 
-template <int BN, int ELEM, int AMODE>
+template <int BN, int ELEM, int AMODE, int EPI>
 int run(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const CUtensorMap& mr, GemmParamsDev p,
         uint32_t staging, int max_ctas, cudaStream_t st) {
-    auto kernel = gemm_tc_kernel<BN, ELEM, AMODE>;
+    auto kernel = gemm_tc_kernel<BN, ELEM, AMODE, EPI>;
     p.stages = stages_for(BN, staging);
     const size_t smem = smem_for(BN, p.stages, staging);
     if (p.stages < 2 || smem > kSmemOptin) return set_error(DAV2CUDA_INTERNAL_ERROR, "gemm: shared memory plan");
@@ -961,18 +959,30 @@ int run(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, con
     const uint32_t tiles = p.num_m_tiles * p.num_n_tiles;
     uint32_t grid = (uint32_t)(max_ctas > 0 ? max_ctas : g_num_sms);
     if (grid > tiles) grid = tiles;
-    kernel<<<grid, 320, smem, st>>>(ma, mb, mo, mr, p);
+    kernel<<<grid, 64 + 32 * EPI, smem, st>>>(ma, mb, mo, mr, p);
     return check_launch("gemm_tc");
 }
 
+// Thread-row TMA epilogue programs (row-major A only) run with 16 epilogue
+// warps; everything else with the 8-warp transposed-store epilogue.
 template <int ELEM, int AMODE>
 int dispatch_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const CUtensorMap& mr,
                 const GemmParamsDev& p, uint32_t staging, int max_ctas, cudaStream_t st) {
+    if constexpr (AMODE == kAModeRows) {
+        if (p.tma_program != kTmaNone) {
+            switch (bn) {
+                case 256: return run<256, ELEM, AMODE, 16>(ma, mb, mo, mr, p, staging, max_ctas, st);
+                case 128: return run<128, ELEM, AMODE, 16>(ma, mb, mo, mr, p, staging, max_ctas, st);
+                case 64: return run<64, ELEM, AMODE, 16>(ma, mb, mo, mr, p, staging, max_ctas, st);
+                default: return run<32, ELEM, AMODE, 16>(ma, mb, mo, mr, p, staging, max_ctas, st);
+            }
+        }
+    }
     switch (bn) {
-        case 256: return run<256, ELEM, AMODE>(ma, mb, mo, mr, p, staging, max_ctas, st);
-        case 128: return run<128, ELEM, AMODE>(ma, mb, mo, mr, p, staging, max_ctas, st);
-        case 64: return run<64, ELEM, AMODE>(ma, mb, mo, mr, p, staging, max_ctas, st);
-        default: return run<32, ELEM, AMODE>(ma, mb, mo, mr, p, staging, max_ctas, st);
+        case 256: return run<256, ELEM, AMODE, 8>(ma, mb, mo, mr, p, staging, max_ctas, st);
+        case 128: return run<128, ELEM, AMODE, 8>(ma, mb, mo, mr, p, staging, max_ctas, st);
+        case 64: return run<64, ELEM, AMODE, 8>(ma, mb, mo, mr, p, staging, max_ctas, st);
+        default: return run<32, ELEM, AMODE, 8>(ma, mb, mo, mr, p, staging, max_ctas, st);
     }
 }
 
@@ -1108,16 +1118,16 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
         if (prog != kTmaNone && aligned && params_aligned) {
             const cuuint64_t dims[2] = {g.n, g.m};
             const cuuint64_t strides[1] = {g.ldo * oes};
-            const cuuint32_t box[2] = {32, 32};
+            const cuuint32_t box[2] = {f32 ? 16u : 32u, 32u};  // 64-byte rows
             const CUtensorMapDataType t =
                 f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                     : (g.out_half_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
-            const CUtensorMapSwizzle sw = f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+            const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_64B;
             if (int rc = make_map_typed(&mo, t, 2, g.out, dims, strides, box, sw)) return rc;
             if (prog == kTmaF32BiasLS)
                 if (int rc = make_map_typed(&mr, t, 2, g.res1, dims, strides, box, sw)) return rc;
             p.tma_program = prog;
-            staging = 16u * kStageBufBytes;
+            staging = 16u * 2u * kStageBufBytes;  // 16 epilogue warps x 2 boxes
         }
     }
     const int mc = g.max_ctas;

@@ -60,6 +60,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps until it completes or about hint_ns pass, instead of spinning and
+// taking issue slots from the warps that do the work.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete. Gives up after
 // kWaitTimeoutNs, or as soon as *abort is set by another role of the CTA;
 // on a timeout it records error 1 and sets *abort. Returns false when the
@@ -69,9 +84,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(a, parity)) return true;
     const unsigned long long start = globaltimer();
     for (uint32_t spin = 1;; ++spin) {
-        if (mbar_try_wait(a, parity)) return true;
-        if (spin > 64) __nanosleep(20);  // back off: leave issue slots to working warps
-        if ((spin & 255u) == 0) {
+        if (mbar_try_wait_hint(a, parity, 20000u)) return true;
+        if ((spin & 15u) == 0) {
             if (*abort) return false;
             if (globaltimer() - start > kWaitTimeoutNs) {
                 *abort = 1;

@@ -482,12 +482,22 @@ enum TmaProgram : int {
     kTmaNone = 0,
     kTmaHalf,
     kTmaHalfBias,
-    kTmaHalfBiasGelu,  // fc1
-    kTmaHalfBiasRelu,
+    kTmaHalfBiasGelu,    // fc1
+    kTmaHalfBiasRelu,    // RCU conv1
+    kTmaHalfRC,          // layer_rn: output + ReLU copy
+    kTmaHalfBiasR1,      // RCU2 conv2: + residual
+    kTmaHalfBiasR1R2RC,  // RCU1 conv2: + residual + fusion input, ReLU copy
     kTmaF32,
     kTmaF32Bias,
     kTmaF32BiasGelu,
     kTmaF32BiasLS,  // attention projection, fc2
+};
+
+// Tensor maps of the thread-row epilogue: output, ReLU-copy output and the
+// two residual inputs (2-D [rows][ld] for row-major A, 4-D [B][H][W][ld]
+// channels-last for the implicit convolution).
+struct EpiMaps {
+    CUtensorMap out, out2, res1, res2;
 };
 
 constexpr uint32_t kStageBufBytes = 2048;  // one 32-row box of 64-byte rows (32 f16 or 16 f32 columns)
@@ -512,18 +522,20 @@ __device__ __forceinline__ void dequant4(const uint32_t* acc, float si, const fl
 }
 
 // One chunk (64 bytes of output per row: 16 f32 or 32 f16 columns):
-// registers -> 64-byte-swizzled staging box (the residual, if any, is
-// already in the box). Row `lane` is at lane*64; its 16-byte unit u sits at
-// unit u ^ ((lane >> 1) & 3), conflict-free for row-wise 16-byte writes.
-template <bool kInt8, bool F32, bool BIAS, bool GELU, bool LS, bool RELU>
+// registers -> 64-byte-swizzled staging boxes. Row `lane` is at lane*64; its
+// 16-byte unit u sits at unit u ^ ((lane >> 1) & 3), conflict-free for
+// row-wise 16-byte writes. Box A holds the first residual on entry (LS, R1)
+// and the output on exit; box B holds the second residual (R2) on entry and
+// the ReLU copy (RC) on exit.
+template <bool kInt8, bool F32, bool BIAS, bool GELU, bool LS, bool RELU, bool R1, bool R2, bool RC>
 __device__ __forceinline__ void tma_chunk_compute(const GemmParamsDev& p, const uint32_t* acc, float si,
-                                                  uint32_t col0, uint8_t* box, uint32_t lane) {
+                                                  uint32_t col0, uint8_t* box, uint8_t* box2, uint32_t lane) {
     const bool hb = p.out_bf16 != 0;
-    uint8_t* row = box + lane * 64u;
     const uint32_t sw = (lane >> 1) & 3u;
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-        uint8_t* q = row + (((uint32_t)u ^ sw) << 4);
+        const uint32_t off = lane * 64u + (((uint32_t)u ^ sw) << 4);
+        uint8_t* q = box + off;
         if (F32) {
             const uint32_t c = col0 + 4u * u;
             float v[4];
@@ -546,51 +558,120 @@ __device__ __forceinline__ void tma_chunk_compute(const GemmParamsDev& p, const 
             float v[8];
             dequant4<kInt8, BIAS, GELU>(acc + 8 * u, si, p.s_w, p.bias, c, v);
             dequant4<kInt8, BIAS, GELU>(acc + 8 * u + 4, si, p.s_w, p.bias, c + 4u, v + 4);
+            if (R1 || R2) {
+                float a[8], b2[8];
+                if (R1) {
+                    const uint4 t = *reinterpret_cast<const uint4*>(q);
+                    unpack4(make_uint2(t.x, t.y), hb, *reinterpret_cast<float(*)[4]>(a));
+                    unpack4(make_uint2(t.z, t.w), hb, *reinterpret_cast<float(*)[4]>(a + 4));
+                }
+                if (R2) {
+                    const uint4 t = *reinterpret_cast<const uint4*>(box2 + off);
+                    unpack4(make_uint2(t.x, t.y), hb, *reinterpret_cast<float(*)[4]>(b2));
+                    unpack4(make_uint2(t.z, t.w), hb, *reinterpret_cast<float(*)[4]>(b2 + 4));
+                }
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    if (R1) v[k] = v[k] + a[k];
+                    if (R2) v[k] = b2[k] + v[k];
+                }
+            }
             if (RELU) {
 #pragma unroll
                 for (int k = 0; k < 8; ++k) v[k] = fmaxf(v[k], 0.f);
             }
             *reinterpret_cast<uint4*>(q) = make_uint4(pack_half2(v[0], v[1], hb), pack_half2(v[2], v[3], hb),
                                                       pack_half2(v[4], v[5], hb), pack_half2(v[6], v[7], hb));
+            if (RC)
+                *reinterpret_cast<uint4*>(box2 + off) =
+                    make_uint4(pack_half2(fmaxf(v[0], 0.f), fmaxf(v[1], 0.f), hb),
+                               pack_half2(fmaxf(v[2], 0.f), fmaxf(v[3], 0.f), hb),
+                               pack_half2(fmaxf(v[4], 0.f), fmaxf(v[5], 0.f), hb),
+                               pack_half2(fmaxf(v[6], 0.f), fmaxf(v[7], 0.f), hb));
         }
     }
 }
 
+// Box origin of (tile, column) for this warp's 32 rows: rows m_blk*128 +
+// 32*quarter for row-major A; pixels (x0..x0+15, y0+2q..y0+2q+1) of one image
+// for the implicit convolution (an 8 x 16 pixel tile).
+template <int AMODE>
+struct BoxAt {
+    int c, x, y, z;
+    __device__ __forceinline__ BoxAt(const GemmParamsDev& p, uint32_t m_blk, uint32_t quarter, uint32_t col) {
+        c = (int)col;
+        if constexpr (AMODE == kAModeRows) {
+            x = (int)(m_blk * 128u + quarter * 32u);
+            y = z = 0;
+        } else {
+            const uint32_t per_img = p.tiles_x * p.tiles_y;
+            const uint32_t rem = m_blk % per_img;
+            x = (int)((rem % p.tiles_x) * 16u);
+            y = (int)((rem / p.tiles_x) * 8u + 2u * quarter);
+            z = (int)(m_blk / per_img);
+        }
+    }
+    __device__ __forceinline__ void store(const CUtensorMap* m, const void* src) const {
+        if constexpr (AMODE == kAModeRows) tma_store_2d(m, src, c, x);
+        else tma_store_4d(m, src, c, x, y, z);
+    }
+    __device__ __forceinline__ void load(const CUtensorMap* m, void* dst, uint64_t* bar) const {
+        if constexpr (AMODE == kAModeRows) tma_load_2d(dst, m, bar, c, x);
+        else tma_load_4d(dst, m, bar, c, x, y, z);
+    }
+};
+
 // The epilogue warp's whole tile loop for one program. EPI epilogue warps:
 // EPI/4 per TMEM lane quarter, sharing the quarter's chunks round-robin.
 // `bufs` is this warp's pair of staging boxes, `rbar` its pair of residual
-// mbarriers.
-template <int BN, int EPI, bool kInt8, bool F32, bool BIAS, bool GELU, bool LS, bool RELU>
-__device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const CUtensorMap* tm_o, const CUtensorMap* tm_r,
-                                               uint32_t tmem_base, uint64_t* tfull, uint64_t* tempty, uint64_t* rbar,
-                                               uint8_t* bufs, volatile int* abort_flag, uint32_t warp,
-                                               uint32_t lane) {
-    constexpr uint32_t CW = F32 ? 16u : 32u;           // columns per chunk
-    constexpr uint32_t kStride = (EPI / 4) * CW;        // column step between this warp's chunks
+// mbarriers. Programs with one output and at most one residual double-buffer
+// the boxes (a residual is prefetched one chunk ahead); programs with a
+// second residual or a ReLU copy use the pair as boxes A and B of one chunk.
+template <int BN, int EPI, int AMODE, bool kInt8, bool F32, bool BIAS, bool GELU, bool LS, bool RELU, bool R1, bool R2,
+          bool RC>
+__device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const EpiMaps* em, uint32_t tmem_base,
+                                               uint64_t* tfull, uint64_t* tempty, uint64_t* rbar, uint8_t* bufs,
+                                               volatile int* abort_flag, uint32_t warp, uint32_t lane) {
+    constexpr uint32_t CW = F32 ? 16u : 32u;      // columns per chunk
+    constexpr uint32_t kStride = (EPI / 4) * CW;  // column step between this warp's chunks
+    constexpr bool kPair = R2 || RC;
+    constexpr bool kRes = LS || R1;
     const uint32_t quarter = warp & 3u;
     const uint32_t sub = (warp - 2u) >> 2;
     const uint32_t num_tiles = p.num_m_tiles * p.num_n_tiles;
     const uint32_t first_c = sub * CW;
     const bool has_chunks = first_c < (uint32_t)BN;
     uint32_t seq = 0;  // chunks processed by this warp
-    // residual box of chunk (tile, c) -> staging buffer b
-    auto load_residual = [&](uint32_t tile, uint32_t c, uint32_t b) {
-        const uint32_t n_blk = tile % p.num_n_tiles, m_blk = tile / p.num_n_tiles;
-        mbar_arrive_expect_tx(&rbar[b], kStageBufBytes);
-        tma_load_2d(bufs + b * kStageBufBytes, tm_r, &rbar[b], (int)(n_blk * (uint32_t)BN + c),
-                    (int)(m_blk * 128u + quarter * 32u));
+    auto origin = [&](uint32_t tile, uint32_t c) {
+        return BoxAt<AMODE>(p, tile / p.num_n_tiles, quarter, (tile % p.num_n_tiles) * (uint32_t)BN + c);
     };
-    if (LS && has_chunks && lane == 0 && blockIdx.x < num_tiles) load_residual(blockIdx.x, first_c, 0);
+    if (kRes && !kPair && has_chunks && lane == 0 && blockIdx.x < num_tiles) {
+        mbar_arrive_expect_tx(&rbar[0], kStageBufBytes);
+        origin(blockIdx.x, first_c).load(&em->res1, bufs, &rbar[0]);
+    }
 
     uint32_t local = 0;
     for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
         const uint32_t buf = local & 1u;
         if (!mbar_wait(&tfull[buf], (local >> 1) & 1u, abort_flag, p.err)) break;
         tc_fence_after();
-        const uint32_t n_blk = tile % p.num_n_tiles;
         const uint32_t m_blk = tile / p.num_n_tiles;
-        const uint64_t r = (uint64_t)m_blk * 128u + quarter * 32u + lane;
-        const float si = (kInt8 && r < p.m) ? __ldg(p.s_in + r) : 0.f;
+        float si = 0.f;
+        if (kInt8) {
+            uint64_t r;
+            bool valid;
+            if constexpr (AMODE == kAModeRows) {
+                r = (uint64_t)m_blk * 128u + quarter * 32u + lane;
+                valid = r < p.m;
+            } else {
+                const uint32_t per_img = p.tiles_x * p.tiles_y, rem = m_blk % per_img;
+                const uint32_t y = (rem / p.tiles_x) * 8u + 2u * quarter + lane / 16u;
+                const uint32_t x = (rem % p.tiles_x) * 16u + lane % 16u;
+                valid = y < p.conv_h && x < p.conv_w;
+                r = ((uint64_t)(m_blk / per_img) * p.conv_h + y) * p.conv_w + x;
+            }
+            if (valid) si = __ldg(p.s_in + r);
+        }
         const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + buf * (uint32_t)BN;
         bool ok = true;
 #pragma unroll 1
@@ -607,9 +688,30 @@ __device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const CUt
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[buf]);
             }
-            const uint32_t b = seq & 1u;
-            uint8_t* box = bufs + b * kStageBufBytes;
-            if (LS) {
+            const BoxAt<AMODE> at = origin(tile, c);
+            uint8_t* box = kPair ? bufs : bufs + (seq & 1u) * kStageBufBytes;
+            uint8_t* box2 = bufs + kStageBufBytes;
+            if (kPair) {
+                // both boxes are reused every chunk: the previous stores must
+                // have read them out before the residuals land
+                if (lane == 0) {
+                    bulk_wait_group_read<0>();
+                    if (R1 || R2) {
+                        mbar_arrive_expect_tx(&rbar[0], (R1 && R2 ? 2u : 1u) * kStageBufBytes);
+                        if (R1) at.load(&em->res1, box, &rbar[0]);
+                        if (R2) at.load(&em->res2, box2, &rbar[0]);
+                    }
+                }
+                if (R1 || R2) {
+                    if (!mbar_wait(&rbar[0], seq & 1u, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                } else {
+                    __syncwarp();
+                }
+            } else if (kRes) {
+                const uint32_t b = seq & 1u;
                 if (lane == 0) {
                     // prefetch the next chunk's residual into the other box, once
                     // the store that last used that box has read it out
@@ -620,7 +722,8 @@ __device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const CUt
                     }
                     if (nt < num_tiles) {
                         bulk_wait_group_read<0>();
-                        load_residual(nt, nc, b ^ 1u);
+                        mbar_arrive_expect_tx(&rbar[b ^ 1u], kStageBufBytes);
+                        origin(nt, nc).load(&em->res1, bufs + (b ^ 1u) * kStageBufBytes, &rbar[b ^ 1u]);
                     }
                 }
                 if (!mbar_wait(&rbar[b], (seq >> 1) & 1u, abort_flag, p.err)) {
@@ -631,12 +734,13 @@ __device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const CUt
                 if (lane == 0) bulk_wait_group_read<1>();
                 __syncwarp();
             }
-            const uint32_t col0 = n_blk * (uint32_t)BN + c;
-            tma_chunk_compute<kInt8, F32, BIAS, GELU, LS, RELU>(p, acc, si, col0, box, lane);
+            tma_chunk_compute<kInt8, F32, BIAS, GELU, LS, RELU, R1, R2, RC>(p, acc, si, (uint32_t)at.c, box, box2,
+                                                                            lane);
             fence_async_smem();
             __syncwarp();
             if (lane == 0) {
-                tma_store_2d(tm_o, box, (int)col0, (int)(m_blk * 128u + quarter * 32u));
+                at.store(&em->out, box);
+                if (RC) at.store(&em->out2, box2);
                 bulk_commit_group();
             }
             ++seq;
@@ -652,23 +756,37 @@ __device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const CUt
     __syncwarp();
 }
 
-template <int BN, int EPI, bool kInt8>
-__device__ __forceinline__ void epilogue_tma_dispatch(const GemmParamsDev& p, const CUtensorMap* tm_o,
-                                                      const CUtensorMap* tm_r, uint32_t tmem_base, uint64_t* tfull,
-                                                      uint64_t* tempty, uint64_t* rbar, uint8_t* bufs,
+template <int BN, int EPI, int AMODE, bool kInt8>
+__device__ __forceinline__ void epilogue_tma_dispatch(const GemmParamsDev& p, const EpiMaps* em, uint32_t tmem_base,
+                                                      uint64_t* tfull, uint64_t* tempty, uint64_t* rbar, uint8_t* bufs,
                                                       volatile int* abort_flag, uint32_t warp, uint32_t lane) {
-#define DAV2_TMA_EPI(F32, BIAS, GELU, LS, RELU)                                                                      \
-    epilogue_tma_loop<BN, EPI, kInt8, F32, BIAS, GELU, LS, RELU>(p, tm_o, tm_r, tmem_base, tfull, tempty, rbar, \
-                                                                 bufs, abort_flag, warp, lane)
+#define DAV2_TMA_EPI(F32, BIAS, GELU, LS, RELU, R1, R2, RC)                                                     \
+    epilogue_tma_loop<BN, EPI, AMODE, kInt8, F32, BIAS, GELU, LS, RELU, R1, R2, RC>(p, em, tmem_base, tfull, \
+                                                                                   tempty, rbar, bufs,        \
+                                                                                   abort_flag, warp, lane)
+    constexpr bool kRows = AMODE == kAModeRows;
     switch (p.tma_program) {
-        case kTmaHalf: DAV2_TMA_EPI(false, false, false, false, false); break;
-        case kTmaHalfBias: DAV2_TMA_EPI(false, true, false, false, false); break;
-        case kTmaHalfBiasGelu: DAV2_TMA_EPI(false, true, true, false, false); break;
-        case kTmaHalfBiasRelu: DAV2_TMA_EPI(false, true, false, false, true); break;
-        case kTmaF32: DAV2_TMA_EPI(true, false, false, false, false); break;
-        case kTmaF32Bias: DAV2_TMA_EPI(true, true, false, false, false); break;
-        case kTmaF32BiasGelu: DAV2_TMA_EPI(true, true, true, false, false); break;
-        default: DAV2_TMA_EPI(true, true, false, true, false); break;
+        case kTmaHalf: DAV2_TMA_EPI(false, false, false, false, false, false, false, false); break;
+        case kTmaHalfBias: DAV2_TMA_EPI(false, true, false, false, false, false, false, false); break;
+        case kTmaHalfBiasRelu: DAV2_TMA_EPI(false, true, false, false, true, false, false, false); break;
+        case kTmaHalfRC: DAV2_TMA_EPI(false, false, false, false, false, false, false, true); break;
+        case kTmaHalfBiasR1: DAV2_TMA_EPI(false, true, false, false, false, true, false, false); break;
+        case kTmaHalfBiasR1R2RC: DAV2_TMA_EPI(false, true, false, false, false, true, true, true); break;
+        case kTmaHalfBiasGelu:
+            if constexpr (kRows) DAV2_TMA_EPI(false, true, true, false, false, false, false, false);
+            break;
+        case kTmaF32:
+            if constexpr (kRows) DAV2_TMA_EPI(true, false, false, false, false, false, false, false);
+            break;
+        case kTmaF32Bias:
+            if constexpr (kRows) DAV2_TMA_EPI(true, true, false, false, false, false, false, false);
+            break;
+        case kTmaF32BiasGelu:
+            if constexpr (kRows) DAV2_TMA_EPI(true, true, true, false, false, false, false, false);
+            break;
+        default:
+            if constexpr (kRows) DAV2_TMA_EPI(true, true, false, true, false, false, false, false);
+            break;
     }
 #undef DAV2_TMA_EPI
 }
@@ -676,7 +794,7 @@ __device__ __forceinline__ void epilogue_tma_dispatch(const GemmParamsDev& p, co
 template <int BN, int ELEM, int AMODE, int EPI>
 __global__ void __launch_bounds__(64 + 32 * EPI, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                   const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ CUtensorMap tm_r,
+                   const __grid_constant__ EpiMaps em,
                    const __grid_constant__ GemmParamsDev p) {
     constexpr bool kInt8 = ELEM == kElemS8;
     constexpr uint32_t kABytes = 128u * 128u;
@@ -709,8 +827,10 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
         tma_prefetch_desc(&tm_a);
         tma_prefetch_desc(&tm_b);
         if (p.tma_program != kTmaNone) {
-            tma_prefetch_desc(&tm_o);
-            tma_prefetch_desc(&tm_r);
+            tma_prefetch_desc(&em.out);
+            tma_prefetch_desc(&em.out2);
+            tma_prefetch_desc(&em.res1);
+            tma_prefetch_desc(&em.res2);
         }
         for (uint32_t s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
@@ -801,10 +921,11 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
                 umma_commit(&tfull[buf]);
             }
         }
-    } else if (AMODE == kAModeRows && p.tma_program != kTmaNone) {
-        if constexpr (AMODE == kAModeRows && EPI == 16)
-            epilogue_tma_dispatch<BN, EPI, kInt8>(p, &tm_o, &tm_r, tmem_base, tfull, tempty, rbars + 2u * (warp - 2u),
-                                                  staging + 2u * kStageBufBytes * (warp - 2u), abort_flag, warp, lane);
+    } else if (p.tma_program != kTmaNone) {
+        if constexpr ((AMODE == kAModeRows && EPI == 16) || (AMODE == kAModeConv3x3 && ELEM == kElemF16 && EPI == 8))
+            epilogue_tma_dispatch<BN, EPI, AMODE, kInt8>(p, &em, tmem_base, tfull, tempty, rbars + 2u * (warp - 2u),
+                                                         staging + 2u * kStageBufBytes * (warp - 2u), abort_flag, warp,
+                                                         lane);
     } else if constexpr (EPI == 8) {
         // warps 2..9: two warps per TMEM lane quarter, splitting the chunks
         const uint32_t quarter = warp & 3u;
@@ -936,7 +1057,7 @@ size_t smem_for(int bn, uint32_t stages, uint32_t staging) {
 int g_num_sms = 0;
 
 template <int BN, int ELEM, int AMODE, int EPI>
-int run(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const CUtensorMap& mr, GemmParamsDev p,
+int run(const CUtensorMap& ma, const CUtensorMap& mb, const EpiMaps& em, GemmParamsDev p,
         uint32_t staging, int max_ctas, cudaStream_t st) {
     auto kernel = gemm_tc_kernel<BN, ELEM, AMODE, EPI>;
     p.stages = stages_for(BN, staging);
@@ -959,30 +1080,32 @@ int run(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, con
     const uint32_t tiles = p.num_m_tiles * p.num_n_tiles;
     uint32_t grid = (uint32_t)(max_ctas > 0 ? max_ctas : g_num_sms);
     if (grid > tiles) grid = tiles;
-    kernel<<<grid, 64 + 32 * EPI, smem, st>>>(ma, mb, mo, mr, p);
+    kernel<<<grid, 64 + 32 * EPI, smem, st>>>(ma, mb, em, p);
     return check_launch("gemm_tc");
 }
 
-// Thread-row TMA epilogue programs (row-major A only) run with 16 epilogue
-// warps; everything else with the 8-warp transposed-store epilogue.
+// Thread-row TMA epilogue programs of row-major A run with 16 epilogue warps;
+// the implicit convolution (its K loop is long enough for 8 epilogue warps to
+// keep up) and the transposed-store programs with 8, which leaves room for a
+// 4-deep ring at BN = 256.
 template <int ELEM, int AMODE>
-int dispatch_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const CUtensorMap& mr,
-                const GemmParamsDev& p, uint32_t staging, int max_ctas, cudaStream_t st) {
+int dispatch_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const EpiMaps& em, const GemmParamsDev& p,
+                uint32_t staging, int max_ctas, cudaStream_t st) {
     if constexpr (AMODE == kAModeRows) {
         if (p.tma_program != kTmaNone) {
             switch (bn) {
-                case 256: return run<256, ELEM, AMODE, 16>(ma, mb, mo, mr, p, staging, max_ctas, st);
-                case 128: return run<128, ELEM, AMODE, 16>(ma, mb, mo, mr, p, staging, max_ctas, st);
-                case 64: return run<64, ELEM, AMODE, 16>(ma, mb, mo, mr, p, staging, max_ctas, st);
-                default: return run<32, ELEM, AMODE, 16>(ma, mb, mo, mr, p, staging, max_ctas, st);
+                case 256: return run<256, ELEM, AMODE, 16>(ma, mb, em, p, staging, max_ctas, st);
+                case 128: return run<128, ELEM, AMODE, 16>(ma, mb, em, p, staging, max_ctas, st);
+                case 64: return run<64, ELEM, AMODE, 16>(ma, mb, em, p, staging, max_ctas, st);
+                default: return run<32, ELEM, AMODE, 16>(ma, mb, em, p, staging, max_ctas, st);
             }
         }
     }
     switch (bn) {
-        case 256: return run<256, ELEM, AMODE, 8>(ma, mb, mo, mr, p, staging, max_ctas, st);
-        case 128: return run<128, ELEM, AMODE, 8>(ma, mb, mo, mr, p, staging, max_ctas, st);
-        case 64: return run<64, ELEM, AMODE, 8>(ma, mb, mo, mr, p, staging, max_ctas, st);
-        default: return run<32, ELEM, AMODE, 8>(ma, mb, mo, mr, p, staging, max_ctas, st);
+        case 256: return run<256, ELEM, AMODE, 8>(ma, mb, em, p, staging, max_ctas, st);
+        case 128: return run<128, ELEM, AMODE, 8>(ma, mb, em, p, staging, max_ctas, st);
+        case 64: return run<64, ELEM, AMODE, 8>(ma, mb, em, p, staging, max_ctas, st);
+        default: return run<32, ELEM, AMODE, 8>(ma, mb, em, p, staging, max_ctas, st);
     }
 }
 
@@ -1088,60 +1211,89 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
         if (g.m != g.conv_batch * g.conv_h * g.conv_w)
             return set_error(DAV2CUDA_INVALID_ARGUMENT, "gemm: conv M must be batch*H*W");
     }
-    // Thread-row epilogue with TMA stores: plain row-major outputs (no row
-    // remap), whole tiles along N, 16-byte aligned rows.
-    CUtensorMap mo = mb, mr = mb;  // placeholders when unused (never read)
+    // Thread-row epilogue with TMA stores: row-major outputs without row
+    // remap (linear layers, 1x1 convolutions) or channels-last outputs of the
+    // implicit convolution with f16 operands; whole tiles along N, 16-byte
+    // aligned rows; residuals in the output's layout.
+    EpiMaps em;
+    em.out = em.out2 = em.res1 = em.res2 = mb;  // placeholders when unused (never read)
     uint32_t staging = kSlabBytes;
     p.tma_program = kTmaNone;
-    if (g.a_mode == kAModeRows && !p.rows_per_img && (g.out_kind == kOutF32Rows || g.out_kind == kOutHalfRows) &&
-        !(g.flags & kEpiHeadDot) && ((g.flags & kEpiDequant) != 0) == (g.elem == kElemS8) && g.n % bn == 0) {
+    const bool conv = g.a_mode != kAModeRows;
+    if ((!conv || g.elem == kElemF16) && !p.rows_per_img &&
+        (g.out_kind == kOutF32Rows || g.out_kind == kOutHalfRows) && !(g.flags & kEpiHeadDot) &&
+        ((g.flags & kEpiDequant) != 0) == (g.elem == kElemS8) && g.n % bn == 0) {
         const bool f32 = g.out_kind == kOutF32Rows;
         const uint32_t oes = f32 ? 4u : 2u;
         const uint32_t f = g.flags & ~uint32_t(kEpiDequant);
         int prog = kTmaNone;
         if (f32) {
-            if (f == 0) prog = kTmaF32;
+            if (conv) prog = kTmaNone;
+            else if (f == 0) prog = kTmaF32;
             else if (f == kEpiBias) prog = kTmaF32Bias;
             else if (f == (kEpiBias | kEpiGelu)) prog = kTmaF32BiasGelu;
             else if (f == (kEpiBias | kEpiLayerScale)) prog = kTmaF32BiasLS;
         } else {
             if (f == 0) prog = kTmaHalf;
             else if (f == kEpiBias) prog = kTmaHalfBias;
-            else if (f == (kEpiBias | kEpiGelu)) prog = kTmaHalfBiasGelu;
+            else if (f == (kEpiBias | kEpiGelu) && !conv) prog = kTmaHalfBiasGelu;
             else if (f == (kEpiBias | kEpiRelu)) prog = kTmaHalfBiasRelu;
+            else if (f == kEpiReluCopy) prog = kTmaHalfRC;
+            else if (f == (kEpiBias | kEpiResidual1)) prog = kTmaHalfBiasR1;
+            else if (f == (kEpiBias | kEpiResidual1 | kEpiResidual2 | kEpiReluCopy)) prog = kTmaHalfBiasR1R2RC;
         }
-        const bool aligned = reinterpret_cast<uintptr_t>(g.out) % 16 == 0 && (g.ldo * oes) % 16 == 0 &&
-                             (prog != kTmaF32BiasLS || reinterpret_cast<uintptr_t>(g.res1) % 16 == 0);
-        const bool params_aligned = (!(g.flags & kEpiDequant) || reinterpret_cast<uintptr_t>(g.s_w) % 16 == 0) &&
-                                    (!(g.flags & kEpiBias) || reinterpret_cast<uintptr_t>(g.bias) % 16 == 0) &&
-                                    (prog != kTmaF32BiasLS || reinterpret_cast<uintptr_t>(g.gamma) % 16 == 0);
+        auto a16 = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+        const bool uses_r1 = prog == kTmaF32BiasLS || prog == kTmaHalfBiasR1 || prog == kTmaHalfBiasR1R2RC;
+        const bool uses_r2 = prog == kTmaHalfBiasR1R2RC;
+        const bool uses_o2 = prog == kTmaHalfRC || prog == kTmaHalfBiasR1R2RC;
+        const bool aligned = a16(g.out) && (g.ldo * oes) % 16 == 0 && (!uses_r1 || a16(g.res1)) &&
+                             (!uses_r2 || a16(g.res2)) && (!uses_o2 || a16(g.out2));
+        const bool params_aligned = (!(g.flags & kEpiDequant) || a16(g.s_w)) && (!(g.flags & kEpiBias) || a16(g.bias)) &&
+                                    (prog != kTmaF32BiasLS || a16(g.gamma));
         if (prog != kTmaNone && aligned && params_aligned) {
-            const cuuint64_t dims[2] = {g.n, g.m};
-            const cuuint64_t strides[1] = {g.ldo * oes};
-            const cuuint32_t box[2] = {f32 ? 16u : 32u, 32u};  // 64-byte rows
             const CUtensorMapDataType t =
                 f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                     : (g.out_half_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
             const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_64B;
-            if (int rc = make_map_typed(&mo, t, 2, g.out, dims, strides, box, sw)) return rc;
-            if (prog == kTmaF32BiasLS)
-                if (int rc = make_map_typed(&mr, t, 2, g.res1, dims, strides, box, sw)) return rc;
+            auto make = [&](CUtensorMap* m, const void* base) -> int {
+                if (!conv) {
+                    const cuuint64_t dims[2] = {g.n, g.m};
+                    const cuuint64_t strides[1] = {g.ldo * oes};
+                    const cuuint32_t box[2] = {f32 ? 16u : 32u, 32u};  // 64-byte rows, 32 rows
+                    return make_map_typed(m, t, 2, base, dims, strides, box, sw);
+                }
+                // channels-last [B][H][W][ldo]; box = 2 image rows x 16 pixels
+                const cuuint64_t dims[4] = {g.n, g.conv_w, g.conv_h, g.conv_batch};
+                const cuuint64_t strides[3] = {g.ldo * oes, (cuuint64_t)g.conv_w * g.ldo * oes,
+                                               (cuuint64_t)g.conv_h * g.conv_w * g.ldo * oes};
+                const cuuint32_t box[4] = {32u, 16u, 2u, 1u};
+                return make_map_typed(m, t, 4, base, dims, strides, box, sw);
+            };
+            if (int rc = make(&em.out, g.out)) return rc;
+            if (uses_o2)
+                if (int rc = make(&em.out2, g.out2)) return rc;
+            if (uses_r1)
+                if (int rc = make(&em.res1, g.res1)) return rc;
+            if (uses_r2)
+                if (int rc = make(&em.res2, g.res2)) return rc;
             p.tma_program = prog;
-            staging = 16u * 2u * kStageBufBytes;  // 16 epilogue warps x 2 boxes
+            // epilogue warps x 2 boxes (the 8-warp kernel's staging area is the
+            // transposed-store slab, which is larger)
+            staging = conv ? kSlabBytes : 16u * 2u * kStageBufBytes;
         }
     }
     const int mc = g.max_ctas;
     if (g.a_mode == kAModeRows) {
         switch (g.elem) {
-            case kElemS8: return dispatch_bn<kElemS8, kAModeRows>(bn, ma, mb, mo, mr, p, staging, mc, st);
-            case kElemF16: return dispatch_bn<kElemF16, kAModeRows>(bn, ma, mb, mo, mr, p, staging, mc, st);
-            default: return dispatch_bn<kElemBF16, kAModeRows>(bn, ma, mb, mo, mr, p, staging, mc, st);
+            case kElemS8: return dispatch_bn<kElemS8, kAModeRows>(bn, ma, mb, em, p, staging, mc, st);
+            case kElemF16: return dispatch_bn<kElemF16, kAModeRows>(bn, ma, mb, em, p, staging, mc, st);
+            default: return dispatch_bn<kElemBF16, kAModeRows>(bn, ma, mb, em, p, staging, mc, st);
         }
     }
     switch (g.elem) {
-        case kElemS8: return dispatch_bn<kElemS8, kAModeConv3x3>(bn, ma, mb, mo, mr, p, staging, mc, st);
-        case kElemF16: return dispatch_bn<kElemF16, kAModeConv3x3>(bn, ma, mb, mo, mr, p, staging, mc, st);
-        default: return dispatch_bn<kElemBF16, kAModeConv3x3>(bn, ma, mb, mo, mr, p, staging, mc, st);
+        case kElemS8: return dispatch_bn<kElemS8, kAModeConv3x3>(bn, ma, mb, em, p, staging, mc, st);
+        case kElemF16: return dispatch_bn<kElemF16, kAModeConv3x3>(bn, ma, mb, em, p, staging, mc, st);
+        default: return dispatch_bn<kElemBF16, kAModeConv3x3>(bn, ma, mb, em, p, staging, mc, st);
     }
 }
 

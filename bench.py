@@ -15,10 +15,13 @@ independent; "scaling": "weak").
   e2e      the same through dav2_infer_bgr8_batch with pinned host buffers:
            host->device copy of the BGR8 batch and device->host copy of the
            depth maps inside the timed region (host clock, max over ranks);
-  roofline the dominant operation of one step, from the executor's live
-           per-operation event timing (dav2_profile_operations) and its
-           algorithmic int8 tensor ops, against the int8 tensor peak measured
-           in this run (cuBLAS int8 GEMM via torch._int_mm, 8192^3);
+  roofline the dominant operation of one step (largest share of the
+           executor's live per-operation event timing, dav2_profile_operations)
+           with its algorithmic tensor work per launch, against the tensor peak
+           of its operand type: int8 = cuBLAS int8 GEMM measured in this run
+           (torch._int_mm, 8192^3); f16 = MEASURED_PEAKS.json's sustained bf16
+           figure, else the pool's stated fallback (1.4 PFLOP/s sustained);
+           `ops` lists the same for every GEMM-family operation;
   cpu_baseline (rank 0, N=1) the reference's CPU path — its PyTorch-CPU fp32
            forward, restated in oracle/torch_graph.py — on one image, all
            host cores.
@@ -149,6 +152,22 @@ def int8_peak_tops(torch):
         e.synchronize()
         best = min(best, s.elapsed_time(e))
     return 2 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def f16_peak_tflops():
+    """Dense 16-bit tensor peak for an operation timed inside a long step:
+    MEASURED_PEAKS.json (driver-written) sustained bf16 figure, else the
+    pool's stated fallback."""
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        try:
+            d = json.loads(f.read_text())
+            for k in ("bf16_tflops_sustained", "bf16_tflops"):
+                if d.get(k):
+                    return float(d[k]), f"MEASURED_PEAKS.json {k} (of measured)"
+        except (ValueError, OSError):
+            pass
+    return 1400.0, "fallback 1.4 PFLOP/s sustained bf16 (of fallback; MEASURED_PEAKS.json absent)"
 
 
 def op_work(encoder, batch, size):
@@ -352,23 +371,34 @@ def main():
             a[0] += 1
             a[1] += o["ms"]
         shares = {k: round(v[1] / prof["total_ms"], 4) for k, v in sorted(agg.items(), key=lambda kv: -kv[1][1])}
-        gemm_names = [k for k in shares if k in work and k != "attention"]
-        dom = max(gemm_names, key=lambda k: agg[k][1])
-        per_launch_ms = agg[dom][1] / agg[dom][0]
-        achieved = work[dom] / (per_launch_ms * 1e-3) / 1e12
-        traffic = None
+        f16_peak, f16_src = f16_peak_tflops()
+        traffic_by_op = {}
         tfile = ROOT / "profiles" / "traffic.txt"
         if tfile.exists():
             for l in tfile.read_text().splitlines():
-                if l.startswith(f"{args.encoder} b{B} {dom}:"):
-                    traffic = int(l.split(":")[1].split()[0])
-        roof = {"bound": "tensor", "kernel": f"gemm_tc int8 ({dom})", "achieved": round(achieved, 1),
-                "peak": round(peak, 1) if peak else None, "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 3) if peak else None, "traffic": traffic,
-                "peak_source": "cuBLAS int8 GEMM (torch._int_mm 8192^3, burst) measured in this run; "
-                               "MEASURED_PEAKS.json has no int8 figure",
-                "per_launch_ms": round(per_launch_ms, 4), "launches_per_step": agg[dom][0],
-                "op_shares": shares}
+                if l.startswith(f"{args.encoder} b{B} ") and ":" in l:
+                    traffic_by_op[l.split(":")[0].split(" ", 2)[2]] = int(l.split(":")[1].split()[0])
+
+        def roofline_of(name):
+            per_launch_ms = agg[name][1] / agg[name][0]
+            achieved = work[name] / (per_launch_ms * 1e-3) / 1e12
+            int8 = args.precision == "int8" and name != "attention"
+            pk = peak if int8 else f16_peak
+            return {"bound": "tensor",
+                    "kernel": f"attention_tc f16 ({name})" if name == "attention" else
+                              f"gemm_tc {'int8' if int8 else 'f16'} ({name})",
+                    "achieved": round(achieved, 1), "peak": round(pk, 1) if pk else None, "unit": "TFLOP/s",
+                    "frac": round(achieved / pk, 3) if pk else None, "traffic": traffic_by_op.get(name),
+                    "peak_source": ("cuBLAS int8 GEMM (torch._int_mm 8192^3, burst) measured in this run; "
+                                    "MEASURED_PEAKS.json has no int8 figure") if int8 else f16_src,
+                    "per_launch_ms": round(per_launch_ms, 4), "launches_per_step": agg[name][0]}
+
+        known = [k for k in shares if k in work]
+        dom = max(known, key=lambda k: agg[k][1])
+        roof = roofline_of(dom)
+        roof["ops"] = {k: {kk: v for kk, v in roofline_of(k).items() if kk in ("achieved", "peak", "frac")}
+                       for k in known}
+        roof["op_shares"] = shares
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(args.encoder, S)

@@ -294,6 +294,20 @@ __device__ __forceinline__ uint32_t q8(float v) {
     return static_cast<uint32_t>(__float2int_rn(v)) & 0xffu;
 }
 
+// The same byte as q8(x / scale) (IEEE quotient), without a division per
+// element. x * rs, rs = the correctly rounded 1/scale, is within 2^-23
+// relative (< 2e-5 for |x/scale| <= 128) of the true quotient, so the two can
+// round to different integers only when the product lies within that
+// distance of a half-integer; elements within 1e-4 of one take the exact
+// quotient (rare, a divergent slow path). The rounding test uses the
+// 1.5*2^23 constant: (q + C) - C = rint(q) for |q| < 2^22.
+__device__ __forceinline__ uint32_t q8_quot(float x, float scale, float rs) {
+    float q = __fmul_rn(x, rs);
+    const float r = __fsub_rn(__fadd_rn(q, 12582912.0f), 12582912.0f);
+    if (fabsf(fabsf(__fsub_rn(q, r)) - 0.5f) < 1.0e-4f) q = __fdiv_rn(x, scale);
+    return q8(q);
+}
+
 }  // namespace dav2cuda
 
 #include "launch.h"

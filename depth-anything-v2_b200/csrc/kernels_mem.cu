@@ -96,14 +96,15 @@ __global__ void __launch_bounds__(256) layer_norm_warp_kernel(
     if constexpr (OUT == kLnS8) {
         amax = warp_max(amax);
         const float scale = fmaxf(amax / 127.0f, 1.0e-8f);
+        const float rs = __frcp_rn(scale);
         if (lane == 0) out_scales[orow] = scale;
         uint32_t* o = reinterpret_cast<uint32_t*>(out) + orow * n4;
 #pragma unroll
         for (int i = 0; i < VPL; ++i) {
             const uint32_t c = lane + 32u * i;
             if (c < n4)
-                o[c] = q8(v[i].x / scale) | (q8(v[i].y / scale) << 8) | (q8(v[i].z / scale) << 16) |
-                       (q8(v[i].w / scale) << 24);
+                o[c] = q8_quot(v[i].x, scale, rs) | (q8_quot(v[i].y, scale, rs) << 8) |
+                       (q8_quot(v[i].z, scale, rs) << 16) | (q8_quot(v[i].w, scale, rs) << 24);
         }
     } else if constexpr (OUT == kLnF32) {
         float4* o = reinterpret_cast<float4*>(out) + orow * n4;
@@ -544,14 +545,15 @@ __global__ void __launch_bounds__(128) quantize_rows_kernel(uint32_t* __restrict
     for (uint32_t c = threadIdx.x; c < cols; c += 128) m = fmaxf(m, fabsf(to_f(x[c])));
     m = block_max_128(m, red);
     const float scale = fmaxf(m / 127.0f, 1.0e-8f);
+    const float rs = __frcp_rn(scale);
     if (threadIdx.x == 0) scales[row] = scale;
     const uint32_t words = cols >> 2;
     uint32_t* o = packed + row * out_words;
     for (uint32_t w = threadIdx.x; w < out_words; w += 128) {
         uint32_t word = 0;
         if (w < words) {
-            word = q8(to_f(x[4 * w]) / scale) | (q8(to_f(x[4 * w + 1]) / scale) << 8) |
-                   (q8(to_f(x[4 * w + 2]) / scale) << 16) | (q8(to_f(x[4 * w + 3]) / scale) << 24);
+            word = q8_quot(to_f(x[4 * w]), scale, rs) | (q8_quot(to_f(x[4 * w + 1]), scale, rs) << 8) |
+                   (q8_quot(to_f(x[4 * w + 2]), scale, rs) << 16) | (q8_quot(to_f(x[4 * w + 3]), scale, rs) << 24);
         }
         o[w] = word;
     }
@@ -584,13 +586,16 @@ __global__ void __launch_bounds__(128) quantize_rows_half_vec_kernel(uint32_t* _
     }
     m = block_max_128(m, red);
     const float scale = fmaxf(m / 127.0f, 1.0e-8f);
+    const float rs = __frcp_rn(scale);
     if (threadIdx.x == 0) scales[row] = scale;
     uint2* o = reinterpret_cast<uint2*>(packed + row * out_words);
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
         uint2 w;
-        w.x = q8(v[i][0] / scale) | (q8(v[i][1] / scale) << 8) | (q8(v[i][2] / scale) << 16) | (q8(v[i][3] / scale) << 24);
-        w.y = q8(v[i][4] / scale) | (q8(v[i][5] / scale) << 8) | (q8(v[i][6] / scale) << 16) | (q8(v[i][7] / scale) << 24);
+        w.x = q8_quot(v[i][0], scale, rs) | (q8_quot(v[i][1], scale, rs) << 8) | (q8_quot(v[i][2], scale, rs) << 16) |
+              (q8_quot(v[i][3], scale, rs) << 24);
+        w.y = q8_quot(v[i][4], scale, rs) | (q8_quot(v[i][5], scale, rs) << 8) | (q8_quot(v[i][6], scale, rs) << 16) |
+              (q8_quot(v[i][7], scale, rs) << 24);
         o[threadIdx.x + 128 * i] = w;
     }
 }

@@ -294,18 +294,33 @@ __device__ __forceinline__ uint32_t q8(float v) {
     return static_cast<uint32_t>(__float2int_rn(v)) & 0xffu;
 }
 
-// The same byte as q8(x / scale) (IEEE quotient), without a division per
-// element. x * rs, rs = the correctly rounded 1/scale, is within 2^-23
-// relative (< 2e-5 for |x/scale| <= 128) of the true quotient, so the two can
-// round to different integers only when the product lies within that
-// distance of a half-integer; elements within 1e-4 of one take the exact
-// quotient (rare, a divergent slow path). The rounding test uses the
-// 1.5*2^23 constant: (q + C) - C = rint(q) for |q| < 2^22.
-__device__ __forceinline__ uint32_t q8_quot(float x, float scale, float rs) {
-    float q = __fmul_rn(x, rs);
-    const float r = __fsub_rn(__fadd_rn(q, 12582912.0f), 12582912.0f);
-    if (fabsf(fabsf(__fsub_rn(q, r)) - 0.5f) < 1.0e-4f) q = __fdiv_rn(x, scale);
-    return q8(q);
+// Four bytes q8(x[k] / scale) (IEEE quotient) packed little-endian, for a
+// per-row scale = max(absmax/127, 1e-8) with |x| <= absmax — the quotient is
+// then at most ~127.00003, so the clamp of q8 never acts. Without a division
+// per element: q = x * rs (rs = correctly rounded 1/scale) is within 2e-5 of
+// the quotient and can round to a different integer only within that
+// distance of a half-integer. The rounding uses C = 1.5*2^23: q + C holds
+// rint(q) in its low mantissa bits (round-half-even, |q| < 2^22), so its low
+// byte is the two's-complement code. A group with an element within 1e-4 of
+// a half-integer (or a NaN) takes the exact quotient (rare).
+__device__ __forceinline__ uint32_t q8x4_quot(float x0, float x1, float x2, float x3, float scale, float rs) {
+    constexpr float C = 12582912.0f;
+    const float xs[4] = {x0, x1, x2, x3};
+    float t[4];
+    bool near_tie = false;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float q = __fmul_rn(xs[k], rs);
+        t[k] = __fadd_rn(q, C);
+        near_tie |= !(fabsf(__fsub_rn(q, __fsub_rn(t[k], C))) <= 0.4999f);
+    }
+    if (near_tie) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) t[k] = __fadd_rn(fminf(fmaxf(__fdiv_rn(xs[k], scale), -127.0f), 127.0f), C);
+    }
+    const uint32_t lo = __byte_perm(__float_as_uint(t[0]), __float_as_uint(t[1]), 0x0040);
+    const uint32_t hi = __byte_perm(__float_as_uint(t[2]), __float_as_uint(t[3]), 0x0040);
+    return __byte_perm(lo, hi, 0x5410);
 }
 
 }  // namespace dav2cuda

@@ -106,27 +106,30 @@ __global__ void fill_tokens_kernel(float* __restrict__ x, const float* __restric
 
 // Align-corners bilinear on channels-last half maps: 8 channels per thread.
 template <typename H>
-__global__ void bilinear_nhwc_kernel(H* __restrict__ out, const H* __restrict__ in, uint32_t ih, uint32_t iw,
-                                     uint32_t oh, uint32_t ow, uint32_t c, uint32_t batch) {
+__global__ void __launch_bounds__(256) bilinear_nhwc_kernel(H* __restrict__ out, const H* __restrict__ in,
+                                                            uint32_t ih, uint32_t iw, uint32_t oh, uint32_t ow,
+                                                            uint32_t c) {
+    // one block per output row (image b, row y): the row's source rows and
+    // weight are computed once; threads stride over (x, 8-channel chunk)
     const uint32_t cv = c / 8;
-    const uint64_t n = (uint64_t)batch * oh * ow * cv;
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-        const uint32_t cc = (uint32_t)(i % cv) * 8;
-        const uint64_t pix = i / cv;
-        const uint32_t x = (uint32_t)(pix % ow);
-        const uint32_t y = (uint32_t)((pix / ow) % oh);
-        const uint64_t b = pix / ((uint64_t)ow * oh);
+    const uint32_t y = blockIdx.x % oh, b = blockIdx.x / oh;
+    const float syf = oh > 1 ? __fdiv_rn(__fmul_rn((float)y, (float)(ih - 1)), (float)(oh - 1)) : 0.f;
+    const uint32_t y0 = (uint32_t)floorf(syf), y1 = min(y0 + 1, ih - 1);
+    const float fy = syf - (float)y0;
+    const H* r0 = in + ((uint64_t)b * ih + y0) * iw * c;
+    const H* r1 = in + ((uint64_t)b * ih + y1) * iw * c;
+    H* o = out + ((uint64_t)b * oh + y) * ow * c;
+    const uint32_t n = ow * cv;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const uint32_t x = i / cv, cc = (i - x * cv) * 8;
         const float sxf = ow > 1 ? __fdiv_rn(__fmul_rn((float)x, (float)(iw - 1)), (float)(ow - 1)) : 0.f;
-        const float syf = oh > 1 ? __fdiv_rn(__fmul_rn((float)y, (float)(ih - 1)), (float)(oh - 1)) : 0.f;
-        const uint32_t x0 = (uint32_t)floorf(sxf), y0 = (uint32_t)floorf(syf);
-        const uint32_t x1 = min(x0 + 1, iw - 1), y1 = min(y0 + 1, ih - 1);
-        const float fx = sxf - (float)x0, fy = syf - (float)y0;
-        const H* base = in + b * ih * iw * c;
-        const uint4 a00 = *reinterpret_cast<const uint4*>(base + ((uint64_t)y0 * iw + x0) * c + cc);
-        const uint4 a01 = *reinterpret_cast<const uint4*>(base + ((uint64_t)y0 * iw + x1) * c + cc);
-        const uint4 a10 = *reinterpret_cast<const uint4*>(base + ((uint64_t)y1 * iw + x0) * c + cc);
-        const uint4 a11 = *reinterpret_cast<const uint4*>(base + ((uint64_t)y1 * iw + x1) * c + cc);
+        const uint32_t x0 = (uint32_t)floorf(sxf);
+        const uint32_t x1 = min(x0 + 1, iw - 1);
+        const float fx = sxf - (float)x0;
+        const uint4 a00 = *reinterpret_cast<const uint4*>(r0 + x0 * c + cc);
+        const uint4 a01 = *reinterpret_cast<const uint4*>(r0 + x1 * c + cc);
+        const uint4 a10 = *reinterpret_cast<const uint4*>(r1 + x0 * c + cc);
+        const uint4 a11 = *reinterpret_cast<const uint4*>(r1 + x1 * c + cc);
         const H* h00 = reinterpret_cast<const H*>(&a00);
         const H* h01 = reinterpret_cast<const H*>(&a01);
         const H* h10 = reinterpret_cast<const H*>(&a10);
@@ -139,7 +142,7 @@ __global__ void bilinear_nhwc_kernel(H* __restrict__ out, const H* __restrict__ 
             const float bot = tof(h10[j]) * (1.f - fx) + tof(h11[j]) * fx;
             r[j] = cvt<H>(top * (1.f - fy) + bot * fy);
         }
-        *reinterpret_cast<uint4*>(out + pix * c + cc) = res;
+        *reinterpret_cast<uint4*>(o + (uint64_t)x * c + cc) = res;
     }
 }
 
@@ -278,8 +281,7 @@ template <typename H>
 int launch_bilinear_nhwc(H* out, const H* in, uint32_t batch, uint32_t ih, uint32_t iw, uint32_t oh, uint32_t ow,
                          uint32_t c, cudaStream_t st) {
     if (c % 8) return set_error(DAV2CUDA_INVALID_ARGUMENT, "bilinear_nhwc: channels % 8");
-    bilinear_nhwc_kernel<H><<<gcap((uint64_t)batch * oh * ow * (c / 8)), 256, 0, st>>>(out, in, ih, iw, oh, ow, c,
-                                                                                       batch);
+    bilinear_nhwc_kernel<H><<<(unsigned)(batch * oh), 256, 0, st>>>(out, in, ih, iw, oh, ow, c);
     return check_launch("bilinear_nhwc");
 }
 

@@ -103,8 +103,7 @@ __global__ void __launch_bounds__(256) layer_norm_warp_kernel(
         for (int i = 0; i < VPL; ++i) {
             const uint32_t c = lane + 32u * i;
             if (c < n4)
-                o[c] = q8_quot(v[i].x, scale, rs) | (q8_quot(v[i].y, scale, rs) << 8) |
-                       (q8_quot(v[i].z, scale, rs) << 16) | (q8_quot(v[i].w, scale, rs) << 24);
+                o[c] = q8x4_quot(v[i].x, v[i].y, v[i].z, v[i].w, scale, rs);
         }
     } else if constexpr (OUT == kLnF32) {
         float4* o = reinterpret_cast<float4*>(out) + orow * n4;
@@ -552,8 +551,7 @@ __global__ void __launch_bounds__(128) quantize_rows_kernel(uint32_t* __restrict
     for (uint32_t w = threadIdx.x; w < out_words; w += 128) {
         uint32_t word = 0;
         if (w < words) {
-            word = q8_quot(to_f(x[4 * w]), scale, rs) | (q8_quot(to_f(x[4 * w + 1]), scale, rs) << 8) |
-                   (q8_quot(to_f(x[4 * w + 2]), scale, rs) << 16) | (q8_quot(to_f(x[4 * w + 3]), scale, rs) << 24);
+            word = q8x4_quot(to_f(x[4 * w]), to_f(x[4 * w + 1]), to_f(x[4 * w + 2]), to_f(x[4 * w + 3]), scale, rs);
         }
         o[w] = word;
     }
@@ -592,10 +590,8 @@ __global__ void __launch_bounds__(128) quantize_rows_half_vec_kernel(uint32_t* _
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
         uint2 w;
-        w.x = q8_quot(v[i][0], scale, rs) | (q8_quot(v[i][1], scale, rs) << 8) | (q8_quot(v[i][2], scale, rs) << 16) |
-              (q8_quot(v[i][3], scale, rs) << 24);
-        w.y = q8_quot(v[i][4], scale, rs) | (q8_quot(v[i][5], scale, rs) << 8) | (q8_quot(v[i][6], scale, rs) << 16) |
-              (q8_quot(v[i][7], scale, rs) << 24);
+        w.x = q8x4_quot(v[i][0], v[i][1], v[i][2], v[i][3], scale, rs);
+        w.y = q8x4_quot(v[i][4], v[i][5], v[i][6], v[i][7], scale, rs);
         o[threadIdx.x + 128 * i] = w;
     }
 }

@@ -322,22 +322,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = false;
                 break;
             }
-            float ls = 0.f;
+            // all 64 exponentials first (independent, in place: the MUFU queue
+            // stays full), then four partial sums and the f16 P tile
+#pragma unroll
+            for (int i = 0; i < 64; ++i) s[i] = ex2_approx(fmaf(s[i], c, -mc));
+
+            float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
                 uint32_t h[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    const float p0 = ex2_approx(fmaf(s[8 * q + 2 * u], c, -mc));
-                    const float p1 = ex2_approx(fmaf(s[8 * q + 2 * u + 1], c, -mc));
-                    ls += p0 + p1;
-                    __half2 hh = __floats2half2_rn(p0, p1);
+                    ls[u] += s[8 * q + 2 * u] + s[8 * q + 2 * u + 1];
+                    __half2 hh = __floats2half2_rn(s[8 * q + 2 * u], s[8 * q + 2 * u + 1]);
                     h[u] = *reinterpret_cast<uint32_t*>(&hh);
                 }
                 *reinterpret_cast<uint4*>(atoms + (j % kPBufs) * 2u * kTile + (((uint32_t)q ^ (row & 7u)) << 4)) =
                     make_uint4(h[0], h[1], h[2], h[3]);
             }
-            l += ls;
+            l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
             tc_fence_before();
             fence_async_smem();
             __syncwarp();

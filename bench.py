@@ -170,6 +170,46 @@ def f16_peak_tflops():
     return 1400.0, "fallback 1.4 PFLOP/s sustained bf16 (of fallback; MEASURED_PEAKS.json absent)"
 
 
+def hbm_peak_gbs():
+    """HBM copy bandwidth: MEASURED_PEAKS.json (driver-written) else the pool's
+    stated fallback."""
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        try:
+            d = json.loads(f.read_text())
+            if d.get("hbm_gbs"):
+                return float(d["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (of measured)"
+        except (ValueError, OSError):
+            pass
+    return 6650.0, "fallback 6.65 TB/s (of fallback; MEASURED_PEAKS.json absent)"
+
+
+def op_bytes(encoder, batch, size, int8):
+    """Algorithmic HBM bytes per launch of the bandwidth-bound operations the
+    executor profiles by name: every tensor read once and written once."""
+    from dav2_b200.dav2file import ARCH
+
+    d, heads, blocks, _, f, oc = ARCH[encoder]
+    p = size // 14
+    r = batch * (p * p + 1)
+    code = 1 if int8 else 2  # int8 codes (+ f32 row scale) or f16 values
+    out = {
+        "ln1": r * d * 4 + r * d * code + (r * 4 if int8 else 0),
+        "ln2": r * d * 4 + r * d * code + (r * 4 if int8 else 0),
+    }
+    if int8:
+        out["quantize hidden"] = r * 4 * d * 2 + r * 4 * d + r * 4
+        out["quantize attention"] = r * d * 2 + r * d + r * 4
+    # align-corners bilinear on channels-last f16 maps (channels padded to 64)
+    fp = -(-f // 64) * 64
+    l4 = (p + 2 - 3) // 2 + 1
+    sizes = [(l4, p), (p, 2 * p), (2 * p, 4 * p), (4 * p, 8 * p)]
+    out["fusion resize"] = sum(batch * (a * a + b * b) * fp * 2 for a, b in sizes) / len(sizes)
+    hp = -(-(f // 2) // 64) * 64
+    out["head resize"] = batch * ((8 * p) ** 2 + size * size) * hp * 2
+    return out
+
+
 def op_work(encoder, batch, size):
     """Algorithmic tensor ops per launch of each GEMM-family operation name
     (2*M*N*K), for the operations the executor profiles by name."""
@@ -393,11 +433,21 @@ def main():
                                     "MEASURED_PEAKS.json has no int8 figure") if int8 else f16_src,
                     "per_launch_ms": round(per_launch_ms, 4), "launches_per_step": agg[name][0]}
 
+        hbm_pk, hbm_src = hbm_peak_gbs()
+        mem = op_bytes(args.encoder, B, S, args.precision == "int8")
+        hbm_ops = {}
+        for k, nbytes in mem.items():
+            if k in agg:
+                gbs = nbytes / (agg[k][1] / agg[k][0] * 1e-3) / 1e9
+                hbm_ops[k] = {"achieved": round(gbs, 1), "peak": hbm_pk, "unit": "GB/s", "frac": round(gbs / hbm_pk, 3),
+                              "bytes_per_launch": int(nbytes)}
         known = [k for k in shares if k in work]
         dom = max(known, key=lambda k: agg[k][1])
         roof = roofline_of(dom)
         roof["ops"] = {k: {kk: v for kk, v in roofline_of(k).items() if kk in ("achieved", "peak", "frac")}
                        for k in known}
+        roof["hbm_ops"] = hbm_ops
+        roof["hbm_peak_source"] = hbm_src
         roof["op_shares"] = shares
         cpu = None
         if world == 1 and not args.no_cpu_baseline:

@@ -13,7 +13,11 @@ Contents:
   model_vits.npz DepthAnythingV2('vits') forward with seeded weights
                  (dav2file.random_state_dict(seed=0)) on seeded tensors;
   image_vits.npz infer_image (cv2 bicubic preprocessing + model + bilinear to
-                 the source size) on a seeded BGR8 image.
+                 the source size) on a seeded BGR8 image;
+  image_vits_518.npz  the same at the benchmark's full size: a 518x518 BGR8
+                 image (np.random.default_rng(0), the BASELINE CPU config's
+                 image), input size 518, ViT-S with random_state_dict(seed=0);
+                 depth stored as float16 (the tests compare at 1e-2).
 """
 from __future__ import annotations
 
@@ -115,6 +119,14 @@ def main(reference: str) -> None:
     tensor, (h, w) = model.image2tensor(bgr, 70)
     depth = model.infer_image(bgr, 70)
     np.savez_compressed(HERE / "image_vits.npz", bgr=bgr, tensor=tensor[0].numpy(), depth=depth.astype(np.float32))
+
+    # full size: 518x518 source, input size 518 (1370 tokens)
+    model = DepthAnythingV2(encoder="vits", features=64, out_channels=[48, 96, 192, 384]).eval()
+    model.load_state_dict({k: torch.from_numpy(v) for k, v in sd.items()})
+    bgr = np.random.default_rng(0).integers(0, 256, (518, 518, 3), dtype=np.uint8)
+    with torch.no_grad():
+        depth = model.infer_image(bgr, 518)
+    np.savez_compressed(HERE / "image_vits_518.npz", depth=depth.astype(np.float16))
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
 
 

@@ -109,27 +109,37 @@ template <typename H>
 __global__ void __launch_bounds__(256) bilinear_nhwc_kernel(H* __restrict__ out, const H* __restrict__ in,
                                                             uint32_t ih, uint32_t iw, uint32_t oh, uint32_t ow,
                                                             uint32_t c) {
-    // one block per output row (image b, row y): the row's source rows and
-    // weight are computed once; threads stride over (x, 8-channel chunk)
+    // one block per output row (image b, row y); the row's x table (source
+    // columns and weight) is computed once into shared memory; each thread
+    // keeps one 8-channel chunk and strides over the pixels (blockDim is a
+    // multiple of the chunk count), so the inner loop has no division
+    extern __shared__ uint32_t xtab[];  // [ow][3]: x0*c, x1*c, fx bits
     const uint32_t cv = c / 8;
     const uint32_t y = blockIdx.x % oh, b = blockIdx.x / oh;
+    for (uint32_t x = threadIdx.x; x < ow; x += blockDim.x) {
+        const float sxf = ow > 1 ? __fdiv_rn(__fmul_rn((float)x, (float)(iw - 1)), (float)(ow - 1)) : 0.f;
+        const uint32_t x0 = (uint32_t)floorf(sxf);
+        const uint32_t x1 = min(x0 + 1, iw - 1);
+        xtab[3 * x] = x0 * c;
+        xtab[3 * x + 1] = x1 * c;
+        xtab[3 * x + 2] = __float_as_uint(sxf - (float)x0);
+    }
     const float syf = oh > 1 ? __fdiv_rn(__fmul_rn((float)y, (float)(ih - 1)), (float)(oh - 1)) : 0.f;
     const uint32_t y0 = (uint32_t)floorf(syf), y1 = min(y0 + 1, ih - 1);
     const float fy = syf - (float)y0;
     const H* r0 = in + ((uint64_t)b * ih + y0) * iw * c;
     const H* r1 = in + ((uint64_t)b * ih + y1) * iw * c;
     H* o = out + ((uint64_t)b * oh + y) * ow * c;
-    const uint32_t n = ow * cv;
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
-        const uint32_t x = i / cv, cc = (i - x * cv) * 8;
-        const float sxf = ow > 1 ? __fdiv_rn(__fmul_rn((float)x, (float)(iw - 1)), (float)(ow - 1)) : 0.f;
-        const uint32_t x0 = (uint32_t)floorf(sxf);
-        const uint32_t x1 = min(x0 + 1, iw - 1);
-        const float fx = sxf - (float)x0;
-        const uint4 a00 = *reinterpret_cast<const uint4*>(r0 + x0 * c + cc);
-        const uint4 a01 = *reinterpret_cast<const uint4*>(r0 + x1 * c + cc);
-        const uint4 a10 = *reinterpret_cast<const uint4*>(r1 + x0 * c + cc);
-        const uint4 a11 = *reinterpret_cast<const uint4*>(r1 + x1 * c + cc);
+    const uint32_t cc = (threadIdx.x % cv) * 8;
+    const uint32_t step = blockDim.x / cv;
+    __syncthreads();
+    for (uint32_t x = threadIdx.x / cv; x < ow; x += step) {
+        const uint32_t o0 = xtab[3 * x] + cc, o1 = xtab[3 * x + 1] + cc;
+        const float fx = __uint_as_float(xtab[3 * x + 2]);
+        const uint4 a00 = *reinterpret_cast<const uint4*>(r0 + o0);
+        const uint4 a01 = *reinterpret_cast<const uint4*>(r0 + o1);
+        const uint4 a10 = *reinterpret_cast<const uint4*>(r1 + o0);
+        const uint4 a11 = *reinterpret_cast<const uint4*>(r1 + o1);
         const H* h00 = reinterpret_cast<const H*>(&a00);
         const H* h01 = reinterpret_cast<const H*>(&a01);
         const H* h10 = reinterpret_cast<const H*>(&a10);
@@ -281,7 +291,11 @@ template <typename H>
 int launch_bilinear_nhwc(H* out, const H* in, uint32_t batch, uint32_t ih, uint32_t iw, uint32_t oh, uint32_t ow,
                          uint32_t c, cudaStream_t st) {
     if (c % 8) return set_error(DAV2CUDA_INVALID_ARGUMENT, "bilinear_nhwc: channels % 8");
-    bilinear_nhwc_kernel<H><<<(unsigned)(batch * oh), 256, 0, st>>>(out, in, ih, iw, oh, ow, c);
+    const uint32_t cv = c / 8;
+    if (cv == 0 || cv > 256) return set_error(DAV2CUDA_INVALID_ARGUMENT, "bilinear_nhwc: channels must be 8..2048");
+    const size_t tab = (size_t)ow * 3 * sizeof(uint32_t);
+    if (tab > 48 * 1024) return set_error(DAV2CUDA_INVALID_ARGUMENT, "bilinear_nhwc: output row too wide");
+    bilinear_nhwc_kernel<H><<<(unsigned)(batch * oh), (256 / cv) * cv, tab, st>>>(out, in, ih, iw, oh, ow, c);
     return check_launch("bilinear_nhwc");
 }
 

@@ -34,7 +34,7 @@
 namespace dav2cuda {
 namespace {
 
-constexpr int kMaxStages = 8;
+constexpr int kMaxStages = 12;
 
 struct GemmParamsDev {
     uint32_t m, n, num_kb, num_m_tiles, num_n_tiles;
@@ -491,6 +491,7 @@ enum TmaProgram : int {
     kTmaF32Bias,
     kTmaF32BiasGelu,
     kTmaF32BiasLS,  // attention projection, fc2
+    kTmaHeadDot,    // output head: relu(acc + b) . w (+ head bias, ReLU or sigmoid*max)
 };
 
 // Tensor maps of the thread-row epilogue: output, ReLU-copy output and the
@@ -756,6 +757,56 @@ __device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const Epi
     __syncwarp();
 }
 
+// Output head on the implicit convolution (N = 32): each thread owns one
+// pixel's accumulator row and reduces it to the depth value,
+// d = sum_j relu(acc_j + b_j) * w_j in column order (the transposed-store
+// path's order), then + head bias and ReLU, or max_depth * sigmoid for a
+// metric head; one f32 store per pixel (a warp's 32 pixels are two 16-pixel
+// runs). Parameters are warp-uniform vector loads.
+template <int BN>
+__device__ __noinline__ void epilogue_head_loop(const GemmParamsDev& p, uint32_t tmem_base, uint64_t* tfull,
+                                                uint64_t* tempty, volatile int* abort_flag, uint32_t warp,
+                                                uint32_t lane) {
+    const uint32_t quarter = warp & 3u;
+    const bool owner = ((warp - 2u) >> 2) == 0u;  // one warp per lane quarter holds the 32 columns
+    const uint32_t num_tiles = p.num_m_tiles * p.num_n_tiles;
+    const bool metric = (p.flags & kEpiMetricHead) != 0;
+    uint32_t local = 0;
+    for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+        const uint32_t buf = local & 1u;
+        if (!mbar_wait(&tfull[buf], (local >> 1) & 1u, abort_flag, p.err)) break;
+        tc_fence_after();
+        uint32_t acc[32];
+        if (owner) {
+            tmem_ld_32x32b_x32(tmem_base + ((quarter * 32u) << 16) + buf * (uint32_t)BN, acc);
+            tmem_ld_wait();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        if (!owner) continue;
+        const uint32_t m_blk = tile / p.num_n_tiles;
+        const uint32_t per_img = p.tiles_x * p.tiles_y, rem = m_blk % per_img;
+        const uint32_t y = (rem / p.tiles_x) * 8u + 2u * quarter + lane / 16u;
+        const uint32_t x = (rem % p.tiles_x) * 16u + lane % 16u;
+        float d = 0.f;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const float4 b4 = ldg4(p.bias + 4 * g), w4 = ldg4(p.head_w + 4 * g);
+            const float bs[4] = {b4.x, b4.y, b4.z, b4.w}, ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float v = __fadd_rn(__uint_as_float(acc[4 * g + k]), bs[k]);
+                d = fmaf(fmaxf(v, 0.0f), ws[k], d);
+            }
+        }
+        d += p.head_b;
+        d = metric ? p.head_max / (1.0f + expf(-d)) : fmaxf(d, 0.0f);
+        if (y < p.conv_h && x < p.conv_w)
+            reinterpret_cast<float*>(p.out)[((uint64_t)(m_blk / per_img) * p.conv_h + y) * p.conv_w + x] = d;
+    }
+}
+
 template <int BN, int EPI, int AMODE, bool kInt8>
 __device__ __forceinline__ void epilogue_tma_dispatch(const GemmParamsDev& p, const EpiMaps* em, uint32_t tmem_base,
                                                       uint64_t* tfull, uint64_t* tempty, uint64_t* rbar, uint8_t* bufs,
@@ -921,6 +972,9 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
                 umma_commit(&tfull[buf]);
             }
         }
+    } else if (p.tma_program == kTmaHeadDot) {
+        if constexpr (BN == 32 && AMODE == kAModeConv3x3 && ELEM == kElemF16 && EPI == 8)
+            epilogue_head_loop<BN>(p, tmem_base, tfull, tempty, abort_flag, warp, lane);
     } else if (p.tma_program != kTmaNone) {
         if constexpr ((AMODE == kAModeRows && EPI == 16) || (AMODE == kAModeConv3x3 && ELEM == kElemF16 && EPI == 8))
             epilogue_tma_dispatch<BN, EPI, AMODE, kInt8>(p, &em, tmem_base, tfull, tempty, rbars + 2u * (warp - 2u),
@@ -1220,7 +1274,12 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     uint32_t staging = kSlabBytes;
     p.tma_program = kTmaNone;
     const bool conv = g.a_mode != kAModeRows;
-    if ((!conv || g.elem == kElemF16) && !p.rows_per_img &&
+    if (conv && g.elem == kElemF16 && bn == 32 && g.n == 32 && g.out_kind == kOutHeadF32 &&
+        (g.flags & ~uint32_t(kEpiMetricHead)) == (kEpiBias | kEpiHeadDot) &&
+        reinterpret_cast<uintptr_t>(g.bias) % 16 == 0 && reinterpret_cast<uintptr_t>(g.head_w) % 16 == 0)
+        p.tma_program = kTmaHeadDot;  // 8-warp kernel; needs no staging area, so the ring can be deeper
+    if (p.tma_program == kTmaHeadDot) staging = 0;
+    if (p.tma_program == kTmaNone && (!conv || g.elem == kElemF16) && !p.rows_per_img &&
         (g.out_kind == kOutF32Rows || g.out_kind == kOutHalfRows) && !(g.flags & kEpiHeadDot) &&
         ((g.flags & kEpiDequant) != 0) == (g.elem == kElemS8) && g.n % bn == 0) {
         const bool f32 = g.out_kind == kOutF32Rows;

@@ -197,6 +197,62 @@ __global__ void __launch_bounds__(256) im2col_quantize_nhwc_kernel(uint8_t* __re
         out[r * kp + col] = col < cols ? (uint8_t)q8(__fmul_rn(value(col), inv)) : 0;
 }
 
+// Vectorised form of the same for 8-aligned channels: each thread holds up to
+// VEC 16-byte groups of 8 channels of one tap in registers, so the row is
+// gathered once; codes and padding as above.
+template <typename H, int VEC>
+__global__ void __launch_bounds__(256) im2col_quantize_nhwc_vec_kernel(uint8_t* __restrict__ out,
+                                                                       float* __restrict__ scales,
+                                                                       const H* __restrict__ in, uint32_t h,
+                                                                       uint32_t w, uint32_t c, uint32_t ldc,
+                                                                       uint32_t k, uint32_t s, uint32_t pad,
+                                                                       uint32_t oh, uint32_t ow, uint32_t kp) {
+    __shared__ float red[8];
+    const uint64_t r = blockIdx.x;
+    const uint64_t b = r / ((uint64_t)oh * ow);
+    const uint32_t pp = (uint32_t)(r % ((uint64_t)oh * ow));
+    const uint32_t oy = pp / ow, ox = pp % ow;
+    const uint32_t cg = c / 8, groups = k * k * cg;
+    uint4 v[VEC];
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+        const uint32_t g = threadIdx.x + 256u * i;
+        v[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (g < groups) {
+            const uint32_t tap = g / cg, ch = (g % cg) * 8;
+            const int iy = (int)(oy * s + tap / k) - (int)pad, ix = (int)(ox * s + tap % k) - (int)pad;
+            if (iy >= 0 && ix >= 0 && iy < (int)h && ix < (int)w)
+                v[i] = *reinterpret_cast<const uint4*>(in + ((b * h + iy) * w + ix) * ldc + ch);
+            const H* hv = reinterpret_cast<const H*>(&v[i]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(tof(hv[j])));
+        }
+    }
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t = fmaxf(t, red[i]);
+    const float scale = fmaxf(t / 127.0f, 1.0e-8f);
+    if (threadIdx.x == 0) scales[r] = scale;
+    const float inv = 1.0f / scale;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+        const uint32_t g = threadIdx.x + 256u * i;
+        if (g < groups) {
+            const H* hv = reinterpret_cast<const H*>(&v[i]);
+            uint32_t q[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) q[j] = q8(__fmul_rn(tof(hv[j]), inv));
+            *reinterpret_cast<uint2*>(out + r * kp + 8ull * g) =
+                make_uint2(q[0] | (q[1] << 8) | (q[2] << 16) | (q[3] << 24), q[4] | (q[5] << 8) | (q[6] << 16) | (q[7] << 24));
+        }
+    }
+    for (uint32_t col = groups * 8 + threadIdx.x; col < kp; col += 256) out[r * kp + col] = 0;
+}
+
 // Per-output-row int8 weight codes (src/gpu_model.cpp:207-284): scale =
 // max(absmax/127, 1e-8), code = nearbyint(clamp(w/scale)). Source element
 // of (row, col) per layout:
@@ -304,6 +360,28 @@ int launch_im2col_quantize_nhwc(uint8_t* out, float* scales, const H* in, uint32
                                 uint32_t c, uint32_t ldc, uint32_t k, uint32_t s, uint32_t pad, uint32_t oh,
                                 uint32_t ow, uint32_t kp, cudaStream_t st) {
     const uint64_t rows = (uint64_t)batch * oh * ow;
+    const uint32_t groups = k * k * (c / 8);
+    if (c % 8 == 0 && ldc % 8 == 0 && kp % 8 == 0 && reinterpret_cast<uintptr_t>(in) % 16 == 0 &&
+        reinterpret_cast<uintptr_t>(out) % 8 == 0 && groups <= 8 * 256) {
+        const int vec = (int)((groups + 255) / 256);
+#define DAV2_IM2COL_VEC(V)                                                                                   \
+    case V:                                                                                                  \
+        im2col_quantize_nhwc_vec_kernel<H, V><<<(unsigned)rows, 256, 0, st>>>(out, scales, in, h, w, c, ldc, k, s, \
+                                                                              pad, oh, ow, kp);              \
+        break;
+        switch (vec) {
+            DAV2_IM2COL_VEC(1)
+            DAV2_IM2COL_VEC(2)
+            DAV2_IM2COL_VEC(3)
+            DAV2_IM2COL_VEC(4)
+            DAV2_IM2COL_VEC(5)
+            DAV2_IM2COL_VEC(6)
+            DAV2_IM2COL_VEC(7)
+            default: DAV2_IM2COL_VEC(8)
+        }
+#undef DAV2_IM2COL_VEC
+        return check_launch("im2col_quantize_nhwc");
+    }
     im2col_quantize_nhwc_kernel<H><<<(unsigned)rows, 256, 0, st>>>(out, scales, in, h, w, c, ldc, k, s, pad, oh, ow,
                                                                     kp);
     return check_launch("im2col_quantize_nhwc");

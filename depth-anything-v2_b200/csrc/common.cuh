@@ -294,6 +294,19 @@ __device__ __forceinline__ uint32_t q8(float v) {
     return static_cast<uint32_t>(__float2int_rn(v)) & 0xffu;
 }
 
+// Exact-erf GELU (torch.nn.GELU) with erf from Abramowitz & Stegun 7.1.26
+// (|error| <= 1.5e-7): erf(z) = 1 - t(a1 + t(a2 + t(a3 + t(a4 + t a5)))) e^{-z^2},
+// t = 1/(1 + p z) for z >= 0, odd extension for z < 0. Used where GELU is
+// fused into another kernel (GEMM epilogue, row quantizer).
+__device__ __forceinline__ float gelu_erf_as(float v) {
+    const float z = fabsf(v) * 0.70710678118654752f;
+    const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+    const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f),
+                                     -0.284496736f), 0.254829592f);
+    const float e = 1.0f - poly * __expf(-z * z);
+    return 0.5f * v * (1.0f + copysignf(e, v));
+}
+
 // Four bytes q8(x[k] / scale) (IEEE quotient) packed little-endian, for a
 // per-row scale = max(absmax/127, 1e-8) with |x| <= absmax — the quotient is
 // then at most ~127.00003, so the clamp of q8 never acts. Without a division

@@ -63,17 +63,6 @@ struct GemmParamsDev {
     uint32_t stages;  // depth of the A/B shared-memory ring
 };
 
-// Exact-erf GELU (torch.nn.GELU) with erf from Abramowitz & Stegun 7.1.26
-// (|error| <= 1.5e-7): erf(z) = 1 - t(a1 + t(a2 + t(a3 + t(a4 + t a5)))) e^{-z^2},
-// t = 1/(1 + p z) for z >= 0, odd extension for z < 0.
-__device__ __forceinline__ float gelu_erf(float v) {
-    const float z = fabsf(v) * 0.70710678118654752f;
-    const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
-    const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f),
-                                     -0.284496736f), 0.254829592f);
-    const float e = 1.0f - poly * __expf(-z * z);
-    return 0.5f * v * (1.0f + copysignf(e, v));
-}
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b, bool bf16) {
     if (bf16) {
@@ -125,7 +114,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParamsDev& p, const uin
     }
     if (f & kEpiGelu) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+        for (int j = 0; j < 32; ++j) v[j] = gelu_erf_as(v[j]);
     }
 
     // --- output-head dot product (one value per row)
@@ -373,7 +362,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmParamsDev& p, const uint
             for (int k = 0; k < 4; ++k) {
                 if (kInt8) v[k] = __fmul_rn(v[k], sw[k]);
                 if (BIAS) v[k] = __fadd_rn(v[k], bs[k]);
-                if (GELU) v[k] = gelu_erf(v[k]);
+                if (GELU) v[k] = gelu_erf_as(v[k]);
             }
             const bool vec = cols_full && ((base[i] & 3u) == 0) && (!CT || (p.ct_cout & 3u) == 0);
             if (F32) {
@@ -517,7 +506,7 @@ __device__ __forceinline__ void dequant4(const uint32_t* acc, float si, const fl
         float t = kInt8 ? (float)(int32_t)acc[k] : __uint_as_float(acc[k]);
         if (kInt8) t = __fmul_rn(__fmul_rn(t, si), ws[k]);
         if (BIAS) t = __fadd_rn(t, bs[k]);
-        if (GELU) t = gelu_erf(t);
+        if (GELU) t = gelu_erf_as(t);
         v[k] = t;
     }
 }

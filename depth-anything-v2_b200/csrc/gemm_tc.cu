@@ -60,7 +60,8 @@ struct GemmParamsDev {
     int* err;
     int program;      // RowProgram for row-major outputs (transposed-store path)
     int tma_program;  // TmaProgram: thread-row epilogue with TMA stores, or 0
-    uint32_t stages;  // depth of the A/B shared-memory ring
+    uint32_t stages;         // depth of the A/B shared-memory ring
+    uint32_t staging_bytes;  // epilogue staging area (TMA boxes or transposed-store slab)
 };
 
 
@@ -620,12 +621,22 @@ struct BoxAt {
 template <int BN, int EPI, int AMODE, bool kInt8, bool F32, bool BIAS, bool GELU, bool LS, bool RELU, bool R1, bool R2,
           bool RC>
 __device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const EpiMaps* em, uint32_t tmem_base,
-                                               uint64_t* tfull, uint64_t* tempty, uint64_t* rbar, uint8_t* bufs,
+                                               uint64_t* tfull, uint64_t* tempty, uint64_t* rbar, uint8_t* staging,
                                                volatile int* abort_flag, uint32_t warp, uint32_t lane) {
     constexpr uint32_t CW = F32 ? 16u : 32u;      // columns per chunk
     constexpr uint32_t kStride = (EPI / 4) * CW;  // column step between this warp's chunks
     constexpr bool kPair = R2 || RC;
     constexpr bool kRes = LS || R1;
+    constexpr uint32_t kBoxes = 2;  // per warp: double-buffered output, residual prefetch, or boxes A and B
+    uint8_t* bufs = staging + kBoxes * kStageBufBytes * (warp - 2u);
+    if ((warp - 1u) * kBoxes * kStageBufBytes > p.staging_bytes) {
+        // the launch's staging area is too small for this program: fail cleanly
+        if (lane == 0) {
+            atomicExch(p.err, 3);
+            *abort_flag = 1;
+        }
+        return;
+    }
     const uint32_t quarter = warp & 3u;
     const uint32_t sub = (warp - 2u) >> 2;
     const uint32_t num_tiles = p.num_m_tiles * p.num_n_tiles;
@@ -798,11 +809,12 @@ __device__ __noinline__ void epilogue_head_loop(const GemmParamsDev& p, uint32_t
 
 template <int BN, int EPI, int AMODE, bool kInt8>
 __device__ __forceinline__ void epilogue_tma_dispatch(const GemmParamsDev& p, const EpiMaps* em, uint32_t tmem_base,
-                                                      uint64_t* tfull, uint64_t* tempty, uint64_t* rbar, uint8_t* bufs,
-                                                      volatile int* abort_flag, uint32_t warp, uint32_t lane) {
+                                                      uint64_t* tfull, uint64_t* tempty, uint64_t* rbar,
+                                                      uint8_t* staging, volatile int* abort_flag, uint32_t warp,
+                                                      uint32_t lane) {
 #define DAV2_TMA_EPI(F32, BIAS, GELU, LS, RELU, R1, R2, RC)                                                     \
     epilogue_tma_loop<BN, EPI, AMODE, kInt8, F32, BIAS, GELU, LS, RELU, R1, R2, RC>(p, em, tmem_base, tfull, \
-                                                                                   tempty, rbar, bufs,        \
+                                                                                   tempty, rbar, staging,     \
                                                                                    abort_flag, warp, lane)
     constexpr bool kRows = AMODE == kAModeRows;
     switch (p.tma_program) {
@@ -967,8 +979,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
     } else if (p.tma_program != kTmaNone) {
         if constexpr ((AMODE == kAModeRows && EPI == 16) || (AMODE == kAModeConv3x3 && ELEM == kElemF16 && EPI == 8))
             epilogue_tma_dispatch<BN, EPI, AMODE, kInt8>(p, &em, tmem_base, tfull, tempty, rbars + 2u * (warp - 2u),
-                                                         staging + 2u * kStageBufBytes * (warp - 2u), abort_flag, warp,
-                                                         lane);
+                                                         staging, abort_flag, warp, lane);
     } else if constexpr (EPI == 8) {
         // warps 2..9: two warps per TMEM lane quarter, splitting the chunks
         const uint32_t quarter = warp & 3u;
@@ -1104,6 +1115,7 @@ int run(const CUtensorMap& ma, const CUtensorMap& mb, const EpiMaps& em, GemmPar
         uint32_t staging, int max_ctas, cudaStream_t st) {
     auto kernel = gemm_tc_kernel<BN, ELEM, AMODE, EPI>;
     p.stages = stages_for(BN, staging);
+    p.staging_bytes = staging;
     const size_t smem = smem_for(BN, p.stages, staging);
     if (p.stages < 2 || smem > kSmemOptin) return set_error(DAV2CUDA_INTERNAL_ERROR, "gemm: shared memory plan");
     static uint64_t configured = 0;  // one bit per device ordinal

@@ -44,7 +44,8 @@ def build(verbose: bool = False, jobs: int | None = None) -> Path:
     BUILD.mkdir(exist_ok=True)
     LIB.parent.mkdir(exist_ok=True)
     cu, cpp = _sources()
-    headers = list(CSRC.glob("*.cuh")) + list((CSRC / "runtime").glob("*.h")) + list((ROOT / "include").glob("*.h"))
+    headers = (list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list((CSRC / "runtime").glob("*.h")) +
+               list((ROOT / "include").glob("*.h")))
     cmds = []
     objs = []
     for src in cu:

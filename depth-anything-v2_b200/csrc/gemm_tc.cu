@@ -482,6 +482,7 @@ enum TmaProgram : int {
     kTmaF32BiasGelu,
     kTmaF32BiasLS,  // attention projection, fc2
     kTmaHeadDot,    // output head: relu(acc + b) . w (+ head bias, ReLU or sigmoid*max)
+    kTmaHalfBiasCT, // conv-transpose (kernel == stride) scatter into a channels-last half map
 };
 
 // Tensor maps of the thread-row epilogue: output, ReLU-copy output and the
@@ -807,6 +808,67 @@ __device__ __noinline__ void epilogue_head_loop(const GemmParamsDev& p, uint32_t
     }
 }
 
+// Conv-transpose with kernel == stride k (row-major A: GEMM row = input pixel
+// (img, py, px), column = (ky*k + kx)*Cout + co): each thread owns one input
+// pixel's row; a 32-column chunk has one (ky, kx) and 32 consecutive output
+// channels, i.e. 64 contiguous bytes of output pixel (py*k + ky, px*k + kx),
+// written with four 16-byte stores. The pixel decomposition is done once per
+// tile. Requires Cout % 32 == 0 and 16-byte aligned output rows.
+template <int BN, int EPI, bool kInt8>
+__device__ __noinline__ void epilogue_ct_loop(const GemmParamsDev& p, uint32_t tmem_base, uint64_t* tfull,
+                                              uint64_t* tempty, volatile int* abort_flag, uint32_t warp,
+                                              uint32_t lane) {
+    constexpr uint32_t kStride = (EPI / 4) * 32u;
+    const uint32_t quarter = warp & 3u;
+    const uint32_t first_c = ((warp - 2u) >> 2) * 32u;
+    const uint32_t num_tiles = p.num_m_tiles * p.num_n_tiles;
+    const bool hb = p.out_bf16 != 0;
+    const uint32_t k = p.ct_k, ow = p.ct_w * k, oh = p.ct_h * k, hw = p.ct_w * p.ct_h;
+    uint32_t local = 0;
+    for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+        const uint32_t buf = local & 1u;
+        if (!mbar_wait(&tfull[buf], (local >> 1) & 1u, abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t n_blk = tile % p.num_n_tiles, m_blk = tile / p.num_n_tiles;
+        const uint32_t r = m_blk * 128u + quarter * 32u + lane;
+        const bool valid = r < p.m;
+        const float si = (kInt8 && valid) ? __ldg(p.s_in + r) : 0.f;
+        const uint32_t img = r / hw, pp = r % hw, py = pp / p.ct_w, px = pp % p.ct_w;
+        const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + buf * (uint32_t)BN;
+        if (first_c >= (uint32_t)BN) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+            continue;
+        }
+#pragma unroll 1
+        for (uint32_t c = first_c; c < (uint32_t)BN; c += kStride) {
+            uint32_t acc[32];
+            tmem_ld_32x32b_x32(taddr + c, acc);
+            tmem_ld_wait();
+            if (c + kStride >= (uint32_t)BN) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[buf]);
+            }
+            const uint32_t col0 = n_blk * (uint32_t)BN + c;
+            const uint32_t kk = col0 / p.ct_cout, co0 = col0 % p.ct_cout;
+            const uint32_t oy = py * k + kk / k, ox = px * k + kk % k;
+            uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) +
+                                                ((uint64_t)(img * oh + oy) * ow + ox) * p.ldo + co0);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                float v[8];
+                dequant4<kInt8, true, false>(acc + 8 * u, si, p.s_w, p.bias, col0 + 8u * u, v);
+                dequant4<kInt8, true, false>(acc + 8 * u + 4, si, p.s_w, p.bias, col0 + 8u * u + 4u, v + 4);
+                if (valid)
+                    o[u] = make_uint4(pack_half2(v[0], v[1], hb), pack_half2(v[2], v[3], hb), pack_half2(v[4], v[5], hb),
+                                      pack_half2(v[6], v[7], hb));
+            }
+        }
+    }
+}
+
 template <int BN, int EPI, int AMODE, bool kInt8>
 __device__ __forceinline__ void epilogue_tma_dispatch(const GemmParamsDev& p, const EpiMaps* em, uint32_t tmem_base,
                                                       uint64_t* tfull, uint64_t* tempty, uint64_t* rbar,
@@ -973,6 +1035,9 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
                 umma_commit(&tfull[buf]);
             }
         }
+    } else if (p.tma_program == kTmaHalfBiasCT) {
+        if constexpr (AMODE == kAModeRows && EPI == 16)
+            epilogue_ct_loop<BN, EPI, kInt8>(p, tmem_base, tfull, tempty, abort_flag, warp, lane);
     } else if (p.tma_program == kTmaHeadDot) {
         if constexpr (BN == 32 && AMODE == kAModeConv3x3 && ELEM == kElemF16 && EPI == 8)
             epilogue_head_loop<BN>(p, tmem_base, tfull, tempty, abort_flag, warp, lane);
@@ -1279,7 +1344,12 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
         (g.flags & ~uint32_t(kEpiMetricHead)) == (kEpiBias | kEpiHeadDot) &&
         reinterpret_cast<uintptr_t>(g.bias) % 16 == 0 && reinterpret_cast<uintptr_t>(g.head_w) % 16 == 0)
         p.tma_program = kTmaHeadDot;  // 8-warp kernel; needs no staging area, so the ring can be deeper
-    if (p.tma_program == kTmaHeadDot) staging = 0;
+    if (!conv && g.out_kind == kOutConvTHalf && (g.flags & ~uint32_t(kEpiDequant)) == kEpiBias &&
+        ((g.flags & kEpiDequant) != 0) == (g.elem == kElemS8) && g.convt_cout % 32 == 0 && g.n % bn == 0 &&
+        reinterpret_cast<uintptr_t>(g.out) % 16 == 0 && g.ldo % 8 == 0 && reinterpret_cast<uintptr_t>(g.bias) % 16 == 0 &&
+        (!(g.flags & kEpiDequant) || reinterpret_cast<uintptr_t>(g.s_w) % 16 == 0))
+        p.tma_program = kTmaHalfBiasCT;  // 16-warp kernel, direct stores: no staging area
+    if (p.tma_program == kTmaHeadDot || p.tma_program == kTmaHalfBiasCT) staging = 0;
     if (p.tma_program == kTmaNone && (!conv || g.elem == kElemF16) && !p.rows_per_img &&
         (g.out_kind == kOutF32Rows || g.out_kind == kOutHalfRows) && !(g.flags & kEpiHeadDot) &&
         ((g.flags & kEpiDequant) != 0) == (g.elem == kElemS8) && g.n % bn == 0) {

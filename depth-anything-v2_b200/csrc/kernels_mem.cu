@@ -596,6 +596,43 @@ __global__ void __launch_bounds__(128) quantize_rows_half_vec_kernel(uint32_t* _
     }
 }
 
+// Warp-per-row form for half rows of 256*VPL columns (VPL <= 8): each lane
+// holds VPL 16-byte groups, the row maximum is a shuffle reduction, and a
+// 128-thread block quantizes four rows (no block barrier).
+template <int VPL>
+__global__ void __launch_bounds__(128) quantize_rows_half_warp_kernel(uint32_t* __restrict__ packed,
+                                                                      float* __restrict__ scales,
+                                                                      const __half* __restrict__ in, uint64_t rows,
+                                                                      uint32_t row_stride, uint32_t out_words) {
+    const uint64_t row = (uint64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+    const uint32_t lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const uint4* x = reinterpret_cast<const uint4*>(in + row * (uint64_t)row_stride);
+    float v[VPL][8];
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const uint4 q = __ldcs(x + lane + 32 * i);
+        const __half2* h = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(h[j]);
+            v[i][2 * j] = f.x;
+            v[i][2 * j + 1] = f.y;
+            m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+    }
+    m = warp_max(m);
+    const float scale = fmaxf(m / 127.0f, 1.0e-8f);
+    const float rs = __frcp_rn(scale);
+    if (lane == 0) scales[row] = scale;
+    uint2* o = reinterpret_cast<uint2*>(packed + row * out_words);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i)
+        o[lane + 32 * i] = make_uint2(q8x4_quot(v[i][0], v[i][1], v[i][2], v[i][3], scale, rs),
+                                      q8x4_quot(v[i][4], v[i][5], v[i][6], v[i][7], scale, rs));
+}
+
 // im2col_quantize_int8.glsl:26-84 on planar [C,H,W] input: row = output
 // pixel, column = c*k*k + ky*k + kx, zero padding; code = rint(clamp(x *
 // (1/scale))). Rows are written out_words words apart (>= ceil(K/4));
@@ -780,6 +817,20 @@ int launch_quantize_rows(uint32_t* packed, float* scales, const T* in, uint64_t 
         const bool plain = offset == 0 && (group == rows || group_stride == (uint64_t)group * row_stride);
         const bool aligned = (reinterpret_cast<uintptr_t>(in) % 16 == 0) && (row_stride % 8 == 0) &&
                              (reinterpret_cast<uintptr_t>(packed) % 8 == 0) && out_words == cols / 4;
+        if (plain && aligned && cols % 256 == 0 && cols <= 2048) {
+            const unsigned grid = (unsigned)((rows + 3) / 4);
+            switch (cols / 256) {
+                case 1: quantize_rows_half_warp_kernel<1><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
+                case 2: quantize_rows_half_warp_kernel<2><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
+                case 3: quantize_rows_half_warp_kernel<3><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
+                case 4: quantize_rows_half_warp_kernel<4><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
+                case 5: quantize_rows_half_warp_kernel<5><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
+                case 6: quantize_rows_half_warp_kernel<6><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
+                case 7: quantize_rows_half_warp_kernel<7><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
+                default: quantize_rows_half_warp_kernel<8><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
+            }
+            return check_launch("quantize_rows_half_warp");
+        }
         if (plain && aligned && cols % 1024 == 0 && cols <= 8192) {
             switch (cols / 1024) {
                 case 1: quantize_rows_half_vec_kernel<1><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, row_stride, out_words); break;

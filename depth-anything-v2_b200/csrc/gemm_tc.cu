@@ -879,24 +879,39 @@ __device__ __forceinline__ void epilogue_tma_dispatch(const GemmParamsDev& p, co
                                                                                    tempty, rbar, staging,     \
                                                                                    abort_flag, warp, lane)
     constexpr bool kRows = AMODE == kAModeRows;
+    // row-major A with 8 epilogue warps: only the long-K LayerScale residual
+    // (the host selects 8 warps for it alone)
+    constexpr bool kLite = kRows && EPI == 8;
     switch (p.tma_program) {
-        case kTmaHalf: DAV2_TMA_EPI(false, false, false, false, false, false, false, false); break;
-        case kTmaHalfBias: DAV2_TMA_EPI(false, true, false, false, false, false, false, false); break;
-        case kTmaHalfBiasRelu: DAV2_TMA_EPI(false, true, false, false, true, false, false, false); break;
-        case kTmaHalfRC: DAV2_TMA_EPI(false, false, false, false, false, false, false, true); break;
-        case kTmaHalfBiasR1: DAV2_TMA_EPI(false, true, false, false, false, true, false, false); break;
-        case kTmaHalfBiasR1R2RC: DAV2_TMA_EPI(false, true, false, false, false, true, true, true); break;
+        case kTmaHalf:
+            if constexpr (!kLite) DAV2_TMA_EPI(false, false, false, false, false, false, false, false);
+            break;
+        case kTmaHalfBias:
+            if constexpr (!kLite) DAV2_TMA_EPI(false, true, false, false, false, false, false, false);
+            break;
+        case kTmaHalfBiasRelu:
+            if constexpr (!kLite) DAV2_TMA_EPI(false, true, false, false, true, false, false, false);
+            break;
+        case kTmaHalfRC:
+            if constexpr (!kLite) DAV2_TMA_EPI(false, false, false, false, false, false, false, true);
+            break;
+        case kTmaHalfBiasR1:
+            if constexpr (!kLite) DAV2_TMA_EPI(false, true, false, false, false, true, false, false);
+            break;
+        case kTmaHalfBiasR1R2RC:
+            if constexpr (!kLite) DAV2_TMA_EPI(false, true, false, false, false, true, true, true);
+            break;
         case kTmaHalfBiasGelu:
-            if constexpr (kRows) DAV2_TMA_EPI(false, true, true, false, false, false, false, false);
+            if constexpr (kRows && !kLite) DAV2_TMA_EPI(false, true, true, false, false, false, false, false);
             break;
         case kTmaF32:
-            if constexpr (kRows) DAV2_TMA_EPI(true, false, false, false, false, false, false, false);
+            if constexpr (kRows && !kLite) DAV2_TMA_EPI(true, false, false, false, false, false, false, false);
             break;
         case kTmaF32Bias:
-            if constexpr (kRows) DAV2_TMA_EPI(true, true, false, false, false, false, false, false);
+            if constexpr (kRows && !kLite) DAV2_TMA_EPI(true, true, false, false, false, false, false, false);
             break;
         case kTmaF32BiasGelu:
-            if constexpr (kRows) DAV2_TMA_EPI(true, true, true, false, false, false, false, false);
+            if constexpr (kRows && !kLite) DAV2_TMA_EPI(true, true, true, false, false, false, false, false);
             break;
         default:
             if constexpr (kRows) DAV2_TMA_EPI(true, true, false, true, false, false, false, false);
@@ -1042,7 +1057,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
         if constexpr (BN == 32 && AMODE == kAModeConv3x3 && ELEM == kElemF16 && EPI == 8)
             epilogue_head_loop<BN>(p, tmem_base, tfull, tempty, abort_flag, warp, lane);
     } else if (p.tma_program != kTmaNone) {
-        if constexpr ((AMODE == kAModeRows && EPI == 16) || (AMODE == kAModeConv3x3 && ELEM == kElemF16 && EPI == 8))
+        if constexpr (AMODE == kAModeRows || (AMODE == kAModeConv3x3 && ELEM == kElemF16 && EPI == 8))
             epilogue_tma_dispatch<BN, EPI, AMODE, kInt8>(p, &em, tmem_base, tfull, tempty, rbars + 2u * (warp - 2u),
                                                          staging, abort_flag, warp, lane);
     } else if constexpr (EPI == 8) {
@@ -1210,9 +1225,9 @@ int run(const CUtensorMap& ma, const CUtensorMap& mb, const EpiMaps& em, GemmPar
 // 4-deep ring at BN = 256.
 template <int ELEM, int AMODE>
 int dispatch_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const EpiMaps& em, const GemmParamsDev& p,
-                uint32_t staging, int max_ctas, cudaStream_t st) {
+                uint32_t staging, int max_ctas, cudaStream_t st, bool epi8 = false) {
     if constexpr (AMODE == kAModeRows) {
-        if (p.tma_program != kTmaNone) {
+        if (p.tma_program != kTmaNone && !epi8) {
             switch (bn) {
                 case 256: return run<256, ELEM, AMODE, 16>(ma, mb, em, p, staging, max_ctas, st);
                 case 128: return run<128, ELEM, AMODE, 16>(ma, mb, em, p, staging, max_ctas, st);
@@ -1338,6 +1353,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     EpiMaps em;
     em.out = em.out2 = em.res1 = em.res2 = mb;  // placeholders when unused (never read)
     uint32_t staging = kSlabBytes;
+    bool epi8 = false;
     p.tma_program = kTmaNone;
     const bool conv = g.a_mode != kAModeRows;
     if (conv && g.elem == kElemF16 && bn == 32 && g.n == 32 && g.out_kind == kOutHeadF32 &&
@@ -1409,21 +1425,26 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
             p.tma_program = prog;
             // epilogue warps x 2 boxes (the 8-warp kernel's staging area is the
             // transposed-store slab, which is larger)
-            staging = conv ? kSlabBytes : 16u * 2u * kStageBufBytes;
+            // the LayerScale residual with a long K loop (fc2: 13 us of MMA per
+            // tile covers its epilogue) runs with 8 epilogue warps: half the
+            // staging boxes, one more ring stage at BN = 256 (measured: qkv's
+            // epilogue needs 16 warps)
+            epi8 = !conv && prog == kTmaF32BiasLS && g.k >= 2048;
+            staging = conv ? kSlabBytes : (epi8 ? 8u : 16u) * 2u * kStageBufBytes;
         }
     }
     const int mc = g.max_ctas;
     if (g.a_mode == kAModeRows) {
         switch (g.elem) {
-            case kElemS8: return dispatch_bn<kElemS8, kAModeRows>(bn, ma, mb, em, p, staging, mc, st);
-            case kElemF16: return dispatch_bn<kElemF16, kAModeRows>(bn, ma, mb, em, p, staging, mc, st);
-            default: return dispatch_bn<kElemBF16, kAModeRows>(bn, ma, mb, em, p, staging, mc, st);
+            case kElemS8: return dispatch_bn<kElemS8, kAModeRows>(bn, ma, mb, em, p, staging, mc, st, epi8);
+            case kElemF16: return dispatch_bn<kElemF16, kAModeRows>(bn, ma, mb, em, p, staging, mc, st, epi8);
+            default: return dispatch_bn<kElemBF16, kAModeRows>(bn, ma, mb, em, p, staging, mc, st, epi8);
         }
     }
     switch (g.elem) {
-        case kElemS8: return dispatch_bn<kElemS8, kAModeConv3x3>(bn, ma, mb, em, p, staging, mc, st);
-        case kElemF16: return dispatch_bn<kElemF16, kAModeConv3x3>(bn, ma, mb, em, p, staging, mc, st);
-        default: return dispatch_bn<kElemBF16, kAModeConv3x3>(bn, ma, mb, em, p, staging, mc, st);
+        case kElemS8: return dispatch_bn<kElemS8, kAModeConv3x3>(bn, ma, mb, em, p, staging, mc, st, epi8);
+        case kElemF16: return dispatch_bn<kElemF16, kAModeConv3x3>(bn, ma, mb, em, p, staging, mc, st, epi8);
+        default: return dispatch_bn<kElemBF16, kAModeConv3x3>(bn, ma, mb, em, p, staging, mc, st, epi8);
     }
 }
 

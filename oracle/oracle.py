@@ -520,16 +520,33 @@ def dpt_forward(sd, feats, pw, ph, encoder, precision="fp32", metric_max_depth=0
     return out.reshape(ph * 14, pw * 14)
 
 
-def infer_tensor(sd, image, encoder, precision="fp32", out_w=None, out_h=None):
+def infer_tensor(sd, image, encoder, precision="fp32", out_w=None, out_h=None, metric_max_depth=0.0):
     """dav2_infer_tensor_f32 / Executor::infer_resized on one planar image
     (src/vulkan_executor.cpp:572-636): graph, then align-corners bilinear to
-    the requested output size when it differs."""
+    the requested output size when it differs. metric_max_depth > 0 selects
+    the metric head (a model file with is_metric set)."""
     feats, pw, ph = encoder_forward(sd, image, encoder, precision)
-    depth = dpt_forward(sd, feats, pw, ph, encoder, precision)
+    depth = dpt_forward(sd, feats, pw, ph, encoder, precision, metric_max_depth)
     h, w = depth.shape
     if out_w is not None and (out_w != w or out_h != h):
         depth = bilinear_align_true(depth[None], out_w, out_h)[0]
     return depth
+
+
+def inferbridge_bgra8(sd, bgra, encoder, input_size=518, precision="fp32", metric_max_depth=0.0):
+    """dav2_inferbridge_bgra8_f32 (src/dav2.cpp:754-803): nearest resize to
+    the transposed network shape, graph, then host min/max normalization
+    (span max - min, or 25 - min for a metric model; all zeros when the span
+    is not positive)."""
+    h, w = bgra.shape[:2]
+    nw, nh = network_shape(w, h, input_size)
+    image = preprocess_inferbridge_bgra8(bgra, nh, nw)
+    depth = infer_tensor(sd, image, encoder, precision, metric_max_depth=metric_max_depth)
+    lo = np.float32(depth.min())
+    span = np.float32(25.0) - lo if metric_max_depth > 0 else np.float32(depth.max()) - lo
+    if not span > 0:
+        return np.zeros_like(depth)
+    return ((depth - lo) / span).astype(np.float32)
 
 
 def infer_bgr8(sd, bgr, encoder, input_size=518, precision="fp32"):

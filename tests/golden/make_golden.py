@@ -14,6 +14,9 @@ Contents:
                  (dav2file.random_state_dict(seed=0)) on seeded tensors;
   image_vits.npz infer_image (cv2 bicubic preprocessing + model + bilinear to
                  the source size) on a seeded BGR8 image;
+  model_vits_metric.npz  the metric-depth model (metric_depth/depth_anything_v2,
+                 sigmoid head x max_depth 20) with the base and strong weights on
+                 the model_vits inputs;
   image_vits_518.npz  the same at the benchmark's full size: a 518x518 BGR8
                  image (np.random.default_rng(0), the BASELINE CPU config's
                  image), input size 518, ViT-S with random_state_dict(seed=0);
@@ -119,6 +122,28 @@ def main(reference: str) -> None:
     tensor, (h, w) = model.image2tensor(bgr, 70)
     depth = model.infer_image(bgr, 70)
     np.savez_compressed(HERE / "image_vits.npz", bgr=bgr, tensor=tensor[0].numpy(), depth=depth.astype(np.float32))
+
+    # metric-depth model: same network, sigmoid head scaled by max_depth
+    import subprocess  # the metric package shares the relative package's name: run it in a child
+    code = (
+        "import sys, numpy as np, torch\n"
+        f"sys.path.insert(0, {str(Path(reference) / 'metric_depth')!r})\n"
+        "from depth_anything_v2.dpt import DepthAnythingV2\n"
+        f"sys.path.insert(0, {str(ROOT / 'depth-anything-v2_b200')!r})\n"
+        "from dav2_b200 import dav2file\n"
+        "res = {}\n"
+        f"fx = np.load({str(HERE / 'model_vits.npz')!r})\n"
+        "for tag, kw in (('base', dict(seed=0)), ('strong', dict(seed=1, std=0.05, bias_std=0.02))):\n"
+        "    sd = dav2file.random_state_dict('vits', **kw)\n"
+        "    m = DepthAnythingV2(encoder='vits', features=64, out_channels=[48, 96, 192, 384], max_depth=20.0).eval()\n"
+        "    m.load_state_dict({k: torch.from_numpy(v) for k, v in sd.items()})\n"
+        "    for shape in ('70x98', '126x126'):\n"
+        "        img = fx[f'{tag}_{shape}_in']\n"
+        "        with torch.no_grad():\n"
+        "            res[f'{tag}_{shape}_in'] = img\n"
+        "            res[f'{tag}_{shape}_out'] = m(torch.from_numpy(img)[None])[0].numpy()\n"
+        f"np.savez_compressed({str(HERE / 'model_vits_metric.npz')!r}, **res)\n")
+    subprocess.run([sys.executable, "-c", code], check=True)
 
     # full size: 518x518 source, input size 518 (1370 tokens)
     model = DepthAnythingV2(encoder="vits", features=64, out_channels=[48, 96, 192, 384]).eval()

@@ -178,3 +178,99 @@ def test_errors_and_counters(cuda, dav2lib, models):
         assert dav2lib.dav2_submit_d3d12(ctx, req, ctypes.byref(job)) == 8
     finally:
         dav2lib.dav2_destroy(ctx)
+
+
+@pytest.fixture(scope="module")
+def metric_models(tmp_path_factory, dav2lib):
+    d = tmp_path_factory.mktemp("metric")
+    out = {}
+    for tag, kw in (("base", dict(seed=0)), ("strong", dict(seed=1, std=0.05, bias_std=0.02))):
+        sd = dav2file.random_state_dict("vits", **kw)
+        path = d / f"vits_metric_{tag}.dav2"
+        dav2file.write_dav2(path, sd, "vits", metric_max_depth=20.0)
+        out[tag] = (path, sd)
+    return out
+
+
+@pytest.mark.parametrize("tag", ["base", "strong"])
+@pytest.mark.parametrize("shape", ["70x98", "126x126"])
+def test_metric_fp16_vs_reference_python(cuda, dav2lib, metric_models, tag, shape):
+    """A metric-depth .dav2 (is_metric, max depth 20: sigmoid head) through
+    dav2_infer_tensor_f32 against the reference's metric model."""
+    import ctypes
+
+    fx = np.load(G / "model_vits_metric.npz")
+    ctx = context(dav2lib, metric_models[tag][0], flags=capi.FLAGS["fp16"])
+    try:
+        info = capi.ModelInfo()
+        info.struct_size = ctypes.sizeof(info)
+        assert dav2lib.dav2_get_model_info(ctx, ctypes.byref(info)) == 0
+        assert info.is_metric == 1 and info.metric_max_depth == 20.0
+        got = infer_tensor(dav2lib, ctx, fx[f"{tag}_{shape}_in"])
+    finally:
+        dav2lib.dav2_destroy(ctx)
+    ref = fx[f"{tag}_{shape}_out"]
+    rel, rng_rel = errs(got, ref)
+    print(f"metric fp16 {tag} {shape}: rel {rel:.2e} range-rel {rng_rel:.2e}")
+    assert rel < 1e-2
+    if tag == "strong":
+        assert rng_rel < 1e-2  # measured 1.2e-3
+
+
+def test_metric_int8_vs_oracle_same_precision(cuda, dav2lib, metric_models):
+    fx = np.load(G / "model_vits_metric.npz")
+    img = fx["strong_126x126_in"]
+    ctx = context(dav2lib, metric_models["strong"][0], flags=capi.FLAGS["int8"])
+    try:
+        got = infer_tensor(dav2lib, ctx, img)
+    finally:
+        dav2lib.dav2_destroy(ctx)
+    want = oracle.infer_tensor(metric_models["strong"][1], img, "vits", precision="int8", metric_max_depth=20.0)
+    rel, rng_rel = errs(got, want)
+    floor, floor_rng = errs(want, fx["strong_126x126_out"])
+    print(f"metric int8: rel {rel:.2e} range-rel {rng_rel:.2e} (int8 floor {floor:.2e} / {floor_rng:.2e})")
+    assert rel < 1e-2
+    assert rng_rel < max(5e-2, 3 * floor_rng)
+
+
+@pytest.mark.parametrize("kind", ["relative", "metric"])
+@pytest.mark.parametrize("case", [0, 1, 3])
+def test_inferbridge_bgra8_vs_oracle(cuda, dav2lib, models, metric_models, kind, case):
+    """dav2_inferbridge_bgra8_f32 (src/dav2.cpp:754-803) on the padded-stride
+    BGRA8 sources of tests/golden/preprocess_ref.npz: the preprocessed tensor
+    is pinned to the reference's compiled code there; here the whole call
+    (nearest resize to the transposed shape, graph, host min/max normalization)
+    is compared with the oracle's fp32 restatement. The output lies in [0, 1];
+    the bound is absolute."""
+    import ctypes
+
+    f = np.load(G / "preprocess_ref.npz")
+    w, h, stride, dw, dh = f[f"bgra{case}_meta"].tolist()
+    src = np.ascontiguousarray(f[f"bgra{case}_src"])
+    size = {0: 70, 1: 140, 3: 70}[case]
+    path, sd = (models if kind == "relative" else metric_models)["strong"]
+    ctx = context(dav2lib, path, flags=capi.FLAGS["fp16"])
+    try:
+        out = np.full(dw * dh, -1.0, np.float32)
+        assert dav2lib.dav2_inferbridge_bgra8_f32(ctx, src.ctypes.data, w, h, stride, size, out.ctypes.data,
+                                                  out.size - 1) == 7  # BUFFER_TOO_SMALL
+        assert dav2lib.dav2_inferbridge_bgra8_f32(ctx, src.ctypes.data, w, h, w * 4 - 1, size, out.ctypes.data,
+                                                  out.size) == 1  # stride below width * 4
+        assert dav2lib.dav2_inferbridge_bgra8_f32(ctx, None, w, h, stride, size, out.ctypes.data, out.size) == 1
+        rc = dav2lib.dav2_inferbridge_bgra8_f32(ctx, src.ctypes.data, w, h, stride, size, out.ctypes.data, out.size)
+        assert rc == 0, dav2lib.dav2_last_error()
+    finally:
+        dav2lib.dav2_destroy(ctx)
+    metric = 20.0 if kind == "metric" else 0.0
+    tensor = f[f"bgra{case}_out"]
+    depth = oracle.infer_tensor(sd, tensor, "vits", metric_max_depth=metric)
+    lo = np.float32(depth.min())
+    span = (np.float32(25.0) if metric else np.float32(depth.max())) - lo
+    want = ((depth - lo) / span).reshape(-1)
+    bgra = src[:, :w * 4].reshape(h, w, 4)
+    assert np.array_equal(oracle.inferbridge_bgra8(sd, bgra, "vits", size, metric_max_depth=metric).reshape(-1), want)
+    err = np.abs(out - want).max()
+    print(f"inferbridge {kind} case {case} ({dw}x{dh}): max abs {err:.2e} (output range {want.min():.3f}..{want.max():.3f})")
+    assert out.min() >= 0.0 and (metric or out.max() == 1.0)
+    assert err < (1e-2 if kind == "relative" else 1e-3)  # measured 2.0e-3 / 1.4e-4
+

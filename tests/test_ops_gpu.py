@@ -167,6 +167,24 @@ def test_preprocess_bgr8(cuda, dav2lib, sw, sh, dw, dh):
         assert np.abs(got[i] - want).max() <= 1e-4 * np.abs(want).max()
 
 
+@pytest.mark.parametrize("case", range(5))
+def test_preprocess_bgr8_vs_reference_native(cuda, dav2lib, case):
+    """The device preprocess_bgr8 against the reference's own compiled
+    src/image.cpp (tests/golden/preprocess_ref.npz: padded row strides,
+    upscaling, a one-pixel-wide source)."""
+    from pathlib import Path
+
+    f = np.load(Path(__file__).resolve().parent / "golden" / "preprocess_ref.npz")
+    w, h, stride, dw, dh = f[f"bgr{case}_meta"].tolist()
+    src = np.ascontiguousarray(f[f"bgr{case}_src"])
+    want = f[f"bgr{case}_out"]
+    out = empty(cuda, (1, 3, dh, dw))
+    call(dav2lib, "dav2cuda_preprocess_bgr8", ptr(out), ptr(dev(cuda, src)), 1, w, h, stride, stride * h, dw, dh,
+         None)
+    finish(cuda, dav2lib)
+    assert np.abs(host(out)[0] - want).max() <= 1e-4 * np.abs(want).max()
+
+
 def test_preprocess_bgr8_bilinear(cuda, dav2lib):
     bgr = rng(9).integers(0, 256, (2, 108, 192, 3), dtype=np.uint8)
     out = empty(cuda, (2, 3, 98, 98))

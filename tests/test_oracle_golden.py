@@ -207,6 +207,51 @@ def test_full_graph_vs_reference_python(tag, shape):
     assert np.abs(got - ref).max() / (ref.max() - ref.min()) < 1e-3
 
 
+@pytest.mark.parametrize("tag", ["base", "strong"])
+@pytest.mark.parametrize("shape", ["70x98", "126x126"])
+def test_metric_graph_vs_reference_python(tag, shape):
+    """Metric-depth network (metric_depth/depth_anything_v2/dpt.py: sigmoid
+    head scaled by max_depth 20; src/dpt.cpp's sigmoid_scale) against the
+    reference's metric model. The base weights leave the output a ripple
+    around 20 * sigmoid(0); the strong ones spread it over ~1.6 m."""
+    from dav2_b200 import dav2file
+
+    fx = np.load(G / "model_vits_metric.npz")
+    sd = dav2file.random_state_dict("vits", seed=0) if tag == "base" else \
+        dav2file.random_state_dict("vits", seed=1, std=0.05, bias_std=0.02)
+    ref = fx[f"{tag}_{shape}_out"]
+    got = oracle.infer_tensor(sd, fx[f"{tag}_{shape}_in"], "vits", metric_max_depth=20.0)
+    assert max_rel(got, ref) < 1e-5
+    assert np.abs(got - ref).max() / (ref.max() - ref.min()) < 2e-3
+
+
+def test_network_shape_vs_reference_native():
+    """network_shape against the reference's own compiled src/image.cpp
+    (tests/golden/make_preprocess_golden.py), rejected sizes included."""
+    f = np.load(G / "preprocess_ref.npz")
+    for (w, h, s), rc, want in zip(f["shape_in"].tolist(), f["shape_rc"].tolist(), f["shape_out"].tolist()):
+        if rc:
+            with pytest.raises(ValueError):
+                oracle.network_shape(w, h, s)
+        else:
+            assert oracle.network_shape(w, h, s) == tuple(want)
+
+
+@pytest.mark.parametrize("tag,channels", [("bgr", 3), ("bgra", 4)])
+def test_preprocess_vs_reference_native(tag, channels):
+    """preprocess_bgr8 (bicubic, src/image.cpp:163-269) and
+    preprocess_inferbridge_bgra8 (nearest, src/image.cpp:289-339) against the
+    reference's compiled code on padded-stride, upscaling and one-pixel-wide
+    sources: bit-exact."""
+    f = np.load(G / "preprocess_ref.npz")
+    fn = oracle.preprocess_bgr8 if tag == "bgr" else oracle.preprocess_inferbridge_bgra8
+    for i in range(5):
+        w, h, stride, dw, dh = f[f"{tag}{i}_meta"].tolist()
+        src = f[f"{tag}{i}_src"][:, :w * channels].reshape(h, w, channels)
+        got = fn(src, dw, dh)
+        assert np.array_equal(got, f[f"{tag}{i}_out"]), (tag, i)
+
+
 def test_infer_image_vs_reference_python():
     from dav2_b200 import dav2file
 

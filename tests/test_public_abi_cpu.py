@@ -48,6 +48,23 @@ def test_network_shapes(dav2lib):
     assert (shape.width, shape.height) == (518, 686)
 
 
+def test_network_shapes_vs_reference_native(dav2lib):
+    """The shape table of tests/golden/preprocess_ref.npz, made by the
+    reference's own compiled network_shape (src/image.cpp), through both
+    public entry points; sizes the reference rejects answer INVALID_ARGUMENT."""
+    from pathlib import Path
+
+    f = np.load(Path(__file__).resolve().parent / "golden" / "preprocess_ref.npz")
+    shape = capi.ImageShape()
+    for (w, h, s), rc, (ow, oh) in zip(f["shape_in"].tolist(), f["shape_rc"].tolist(), f["shape_out"].tolist()):
+        assert dav2lib.dav2_get_network_shape(w, h, s, ctypes.byref(shape)) == rc
+        if rc == 0:
+            assert (shape.width, shape.height) == (ow, oh)
+        assert dav2lib.dav2_get_inferbridge_shape(w, h, s, ctypes.byref(shape)) == rc
+        if rc == 0:
+            assert (shape.width, shape.height) == (oh, ow)  # src/dav2.cpp:142-155 swaps the axes
+
+
 def test_create_validation(dav2lib, tmp_path):
     lib = dav2lib
     ctx = ctypes.c_void_p()

@@ -3,27 +3,34 @@
 // 1098-1209: QK^T*0.125 -> softmax_lastdim.glsl -> PV) without materialising
 // the [heads, T, T] scores.
 //
-// One CTA = one (image, head, 256-query block) = two 128-query tiles that
-// share every K/V block; 608 threads, one CTA per SM (a kernel that allocates
-// tensor memory is resident once per SM), all 512 TMEM columns: tile t uses
-// columns 256t + [0,128) for S and 256t + 128 + 64h for O_h, h = key half.
-//   warp 0       TMA: the Q tiles once, then K_j / V_j (128 keys x 64 dims
-//                each) into a 3-stage ring. The 3-D tensor map over qkv
-//                [B][T][3E] zero-fills rows past T.
+// Work unit = one (image, head, 256-query block) = two 128-query tiles that
+// share every K/V block. The kernel is persistent: one CTA per SM (a kernel
+// that allocates tensor memory is resident once per SM; all 512 TMEM columns)
+// walks units blockIdx.x, blockIdx.x + gridDim.x, ..., so that the next
+// unit's Q, first K/V blocks and first S overlap the current unit's last
+// blocks and output merge. Units whose second tile lies past T (one live
+// tile) are numbered after all two-tile units, which spreads them evenly over
+// the CTAs. Tile t uses TMEM columns 256t + [0,128) for S and 256t + 128 + 64h
+// for O_h, h = key half.
+//   warp 0       TMA: per unit the Q tiles (double-buffered per tile), then
+//                K_j / V_j (128 keys x 64 dims each) into a 3-stage ring that
+//                runs on across units. The 3-D tensor map over qkv [B][T][3E]
+//                zero-fills rows past T.
 //   warps 1, 18  MMA issuers, one per tile (so neither tile's pipeline waits
 //                on the other; a K/V stage is released once both have
-//                committed): S_{j+1} = Q K_{j+1}^T
-//                (M=128, N=128, K=64) as soon as the tile's softmax holds S_j in
-//                registers, so it is computed while that softmax works on block
-//                j; then, once P_j is published, O_h += P_j[:, 64h:64h+64]
-//                V_j[64h:64h+64, :] for both key halves (M=128, N=64, K=64; V
-//                read as an MN-major operand), accumulating in TMEM across key
-//                blocks.
+//                committed — the issuer of a tile with no rows in a unit
+//                releases each stage as soon as it is filled): S_{j+1} =
+//                Q K_{j+1}^T (M=128, N=128, K=64) as soon as the tile's softmax
+//                holds S_j in registers, so it is computed while that softmax
+//                works on block j; then, once P_j is published, O_h +=
+//                P_j[:, 64h:64h+64] V_j[64h:64h+64, :] for both key halves
+//                (M=128, N=64, K=64; V read as an MN-major operand),
+//                accumulating in TMEM across key blocks.
 //   warps 2..9   softmax of tile 0, warps 10..17 of tile 1: two warps per query
 //                row (TMEM lane), warp half h owning keys [64h, 64h+64) of every
 //                block with its own running maximum m_h, sum l_h and O_h — an
-//                independent online softmax per key half, merged once at the
-//                end. Per block: S loaded once into registers, row maximum,
+//                independent online softmax per key half, merged once per unit.
+//                Per block: S loaded once into registers, row maximum,
 //                P = exp2(s*c - m*c) (f16) into a 128-byte-swizzled shared tile,
 //                l_h += sum(P). The maximum used for P is only raised when the
 //                block maximum exceeds it by more than 8 (log2 units): P stays
@@ -31,8 +38,9 @@
 //                Full key blocks skip the key-range mask. The two tiles take
 //                turns for the exponentials (the issue- and MUFU-heavy phase), so each
 //                tile's other work overlaps the other tile's exp phase.
-// Ordering between the roles uses mbarriers; every wait is bounded and a
-// timeout sets the device error word instead of hanging.
+// Ordering between the roles uses mbarriers whose phases are counted across
+// units; every wait is bounded and a timeout sets the device error word
+// instead of hanging.
 #include "kernels.cuh"
 
 #include <cudaTypedefs.h>
@@ -45,13 +53,17 @@ namespace {
 
 struct AttnParams {
     uint32_t tokens, heads, num_kb;
+    uint32_t units;       // batch * heads * query blocks
+    uint32_t full_units;  // units with two live tiles, numbered first
+    uint32_t full_per_bh; // two-tile units per (image, head)
     uint64_t out_ld;
     __half* out;
     int* err;
 };
 
-constexpr uint32_t kQTiles = 2;       // 128-query tiles per CTA
-constexpr uint32_t kQ = 128 * kQTiles;  // queries per CTA
+constexpr uint32_t kQTiles = 2;       // 128-query tiles per unit
+constexpr uint32_t kQ = 128 * kQTiles;  // queries per unit
+constexpr uint32_t kQBufs = 2;        // Q buffers per tile (the next unit's Q loads early)
 constexpr uint32_t kKV = 128;         // keys per block
 // K/V ring depth and P buffers per tile (P_j in buffer j % kPBufs). Measured
 // on B200 (ViT-L, 64 images): 3 stages x 1 P buffer beats 2 x 2 (the only
@@ -61,9 +73,10 @@ constexpr uint32_t kPBufs = 1;
 constexpr uint32_t kTile = 128 * 128; // bytes of a 128 x 64 f16 tile
 constexpr uint32_t kThreads = 64 + 256 * kQTiles + 32;  // TMA, MMA(tile 0), softmax, MMA(tile 1)
 constexpr uint32_t kMma1Warp = 2 + 8 * kQTiles;
-// Q[tile], K[stage], V[stage], P[tile][buffer][key half], 1 KB barriers
-constexpr uint32_t kSmem = kTile * (kQTiles + 2 * kStages + 2 * kPBufs * kQTiles) + 1024;
-constexpr uint32_t kBarrierBytes = 8 * (2 * kStages + (7 + kPBufs) * kQTiles) + 8;
+// Q[tile][buffer], K[stage], V[stage], P[tile][buffer][key half], 1 KB barriers
+constexpr uint32_t kSmem = kTile * (kQBufs * kQTiles + 2 * kStages + 2 * kPBufs * kQTiles) + 1024;
+constexpr uint32_t kBarrierBytes = 8 * (2 * kStages + 2 * kQBufs * kQTiles + (6 + kPBufs) * kQTiles) + 8;
+static_assert(kQTiles == 2 && kQBufs == 2, "unit decoding and buffer parities assume two tiles, two Q buffers");
 static_assert(kBarrierBytes <= 1024, "barrier block overflows its 1 KB");
 static_assert(kSmem <= 232448, "shared memory above the per-block limit");
 
@@ -94,6 +107,30 @@ __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr) {
            (static_cast<uint64_t>(2) << 61);
 }
 
+struct Unit {
+    uint32_t img, head, q0, ntiles;
+};
+
+// Two-tile units first, (image, head)-major with the query block fastest
+// (the units of one (image, head) run side by side and share K/V in L2), then
+// the single-tile units (query block past T - 128), one per (image, head).
+__device__ __forceinline__ Unit unit_at(const AttnParams& p, uint32_t u) {
+    uint32_t bh, qb;
+    if (u < p.full_units) {
+        bh = u / p.full_per_bh;
+        qb = u - bh * p.full_per_bh;
+    } else {
+        bh = u - p.full_units;
+        qb = p.full_per_bh;
+    }
+    Unit w;
+    w.head = bh % p.heads;
+    w.img = bh / p.heads;
+    w.q0 = qb * kQ;
+    w.ntiles = p.tokens - w.q0 > 128u ? 2u : 1u;
+    return w;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
     extern __shared__ uint8_t smem[];
@@ -102,13 +139,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (threadIdx.x == 0) atomicExch(p.err, 2);
         return;
     }
-    uint8_t* sQ = smem;                                // [tile]
-    uint8_t* sK = smem + kQTiles * kTile;              // [stage]
+    uint8_t* sQ = smem;                                // [tile][buffer]
+    uint8_t* sK = smem + kQBufs * kQTiles * kTile;     // [stage]
     uint8_t* sV = sK + kStages * kTile;                // [stage]
     uint8_t* sP = sV + kStages * kTile;                // [tile][buffer][key half]
     uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBufs * kQTiles * kTile);
-    uint64_t* q_full = bars;                   // [tile]
-    uint64_t* kv_full = q_full + kQTiles;      // [stage]
+    uint64_t* q_full = bars;                           // [tile][buffer]
+    uint64_t* q_empty = q_full + kQBufs * kQTiles;     // [tile][buffer]
+    uint64_t* kv_full = q_empty + kQBufs * kQTiles;    // [stage]
     uint64_t* kv_empty = kv_full + kStages;    // [stage]
     uint64_t* s_full = kv_empty + kStages;     // [tile]
     uint64_t* s_empty = s_full + kQTiles;      // [tile]
@@ -120,14 +158,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + kQTiles);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-    const uint32_t q0 = blockIdx.x * kQ, head = blockIdx.y, img = blockIdx.z;
     const uint32_t E = p.heads * 64u;
-    const uint32_t ntiles = (p.tokens - q0 + 127u) / 128u >= kQTiles ? kQTiles : (p.tokens - q0 + 127u) / 128u;
 
     if (threadIdx.x == 0) {
         tma_prefetch_desc(&tm);
         for (uint32_t t = 0; t < kQTiles; ++t) {
-            mbar_init(&q_full[t], 1);
+            for (uint32_t b = 0; b < kQBufs; ++b) {
+                mbar_init(&q_full[kQBufs * t + b], 1);
+                mbar_init(&q_empty[kQBufs * t + b], 1);
+            }
             mbar_init(&s_full[t], 1);
             mbar_init(&p_full[t], 8);
             for (uint32_t b = 0; b < kPBufs; ++b) mbar_init(&p_empty[kPBufs * t + b], 1);
@@ -138,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (uint32_t st = 0; st < kStages; ++st) {
             mbar_init(&kv_full[st], 1);
-            mbar_init(&kv_empty[st], ntiles);  // released by every active tile's MMA issuer
+            mbar_init(&kv_empty[st], kQTiles);  // one release per tile issuer and block
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -153,72 +192,125 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            for (uint32_t t = 0; t < ntiles; ++t) {
-                mbar_arrive_expect_tx(&q_full[t], kTile);
-                tma_load_3d(sQ + t * kTile, &tm, &q_full[t], (int)(head * 64u), (int)(q0 + 128u * t), (int)img);
-            }
-            for (uint32_t j = 0; j < nkb && !*abort_flag; ++j) {
-                const uint32_t st = j % kStages;
-                if (!mbar_wait(&kv_empty[st], ((j / kStages) & 1u) ^ 1u, abort_flag, p.err)) break;
-                mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
-                tma_load_3d(sK + st * kTile, &tm, &kv_full[st], (int)(E + head * 64u), (int)(j * kKV), (int)img);
-                tma_load_3d(sV + st * kTile, &tm, &kv_full[st], (int)(2 * E + head * 64u), (int)(j * kKV), (int)img);
+            uint32_t g = 0;                        // K/V blocks loaded so far (all units)
+            uint32_t qn[kQTiles] = {0u, 0u};       // Q tiles loaded so far, per tile
+            bool ok = true;
+            for (uint32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+                const Unit w = unit_at(p, u);
+#pragma unroll
+                for (uint32_t t = 0; t < kQTiles; ++t) {
+                    if (t >= w.ntiles || !ok) break;
+                    const uint32_t b = qn[t] & 1u;
+                    // the buffer's previous Q (two units back) must be done
+                    if (qn[t] >= kQBufs &&
+                        !mbar_wait(&q_empty[kQBufs * t + b], ((qn[t] >> 1) - 1u) & 1u, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&q_full[kQBufs * t + b], kTile);
+                    tma_load_3d(sQ + (kQBufs * t + b) * kTile, &tm, &q_full[kQBufs * t + b], (int)(w.head * 64u),
+                                (int)(w.q0 + 128u * t), (int)w.img);
+                    ++qn[t];
+                }
+                for (uint32_t j = 0; ok && j < nkb; ++j, ++g) {
+                    const uint32_t st = g % kStages;
+                    if (*abort_flag || !mbar_wait(&kv_empty[st], ((g / kStages) & 1u) ^ 1u, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
+                    tma_load_3d(sK + st * kTile, &tm, &kv_full[st], (int)(E + w.head * 64u), (int)(j * kKV),
+                                (int)w.img);
+                    tma_load_3d(sV + st * kTile, &tm, &kv_full[st], (int)(2 * E + w.head * 64u), (int)(j * kKV),
+                                (int)w.img);
+                }
             }
         }
     } else if (warp == 1 || warp == kMma1Warp) {
         // one MMA issuer per tile, so that neither tile's pipeline waits on the other
         const uint32_t t = warp == 1 ? 0u : 1u;
-        if (lane == 0 && t < ntiles) {
+        if (lane == 0) {
             constexpr uint32_t idesc_s = make_idesc(1u, 0u, 128u, 128u);
             constexpr uint32_t idesc_o = make_idesc(1u, 0u, 128u, 64u) | (1u << 16);  // B (V) MN-major
-            const uint32_t q_addr = smem_addr(sQ + t * kTile);
-            auto issue_s = [&](uint32_t j) {
-                const uint32_t k_addr = smem_addr(sK + (j % kStages) * kTile);
-#pragma unroll
-                for (uint32_t kk = 0; kk < 4; ++kk)
-                    umma<false>(tmem + 256u * t, smem_desc_sw128(q_addr + 32u * kk), smem_desc_sw128(k_addr + 32u * kk),
-                                idesc_s, kk ? 1u : 0u);
-                umma_commit(&s_full[t]);
-            };
-            auto issue_o = [&](uint32_t j) {
-                const uint32_t v_addr = smem_addr(sV + (j % kStages) * kTile);
-#pragma unroll
-                for (uint32_t h = 0; h < 2; ++h) {
-                    const uint32_t p_addr = smem_addr(sP + ((kPBufs * t + j % kPBufs) * 2u + h) * kTile);
+            uint32_t g = 0;   // K/V blocks consumed (all units)
+            uint32_t gt = 0;  // blocks this tile has computed (its S/P/O barrier phases)
+            uint32_t qn = 0;  // units this tile has computed (its Q buffer phases)
+            bool ok = true;
+            for (uint32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+                const Unit w = unit_at(p, u);
+                if (t >= w.ntiles) {
+                    // no rows of this tile in the unit: release each K/V stage once
+                    // it is filled (the fill proves the stage's previous phase is over)
+                    for (uint32_t j = 0; j < nkb; ++j, ++g) {
+                        const uint32_t st = g % kStages;
+                        if (!mbar_wait(&kv_full[st], (g / kStages) & 1u, abort_flag, p.err)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive(&kv_empty[st]);
+                    }
+                    continue;
+                }
+                const uint32_t qbuf = kQBufs * t + (qn & 1u);
+                const uint32_t q_addr = smem_addr(sQ + qbuf * kTile);
+                auto issue_s = [&](uint32_t gg) {
+                    const uint32_t k_addr = smem_addr(sK + (gg % kStages) * kTile);
 #pragma unroll
                     for (uint32_t kk = 0; kk < 4; ++kk)
-                        umma<false>(tmem + 256u * t + 128u + 64u * h, smem_desc_sw128(p_addr + 32u * kk),
-                                    desc_mn_sw128(v_addr + (4u * h + kk) * 2048u), idesc_o, (j | kk) ? 1u : 0u);
-                }
-                umma_commit(&o_full[t]);
-                umma_commit(&p_empty[kPBufs * t + j % kPBufs]);
-                umma_commit(&kv_empty[j % kStages]);
-            };
-            bool ok = mbar_wait(&kv_full[0], 0, abort_flag, p.err) && mbar_wait(&q_full[t], 0, abort_flag, p.err);
-            if (ok) {
-                tc_fence_after();
-                issue_s(0);
-                mma_issued = true;
-            }
-            for (uint32_t j = 0; ok && j < nkb; ++j) {
-                // S_{j+1} as soon as the softmax holds S_j in registers (it is
-                // computed while that softmax works on block j) ...
-                if (j + 1 < nkb) {
-                    ok = mbar_wait(&kv_full[(j + 1) % kStages], ((j + 1) / kStages) & 1u, abort_flag, p.err) &&
-                         mbar_wait(&s_empty[t], j & 1u, abort_flag, p.err);
-                    if (!ok) break;
-                    tc_fence_after();
-                    issue_s(j + 1);
-                }
-                // ... and the O updates of block j once its P is published (the
-                // softmax has also rescaled O by then, if it had to)
-                ok = mbar_wait(&p_full[t], j & 1u, abort_flag, p.err);
+                        umma<false>(tmem + 256u * t, smem_desc_sw128(q_addr + 32u * kk),
+                                    smem_desc_sw128(k_addr + 32u * kk), idesc_s, kk ? 1u : 0u);
+                    umma_commit(&s_full[t]);
+                };
+                auto issue_o = [&](uint32_t gg, uint32_t j, uint32_t gtt) {
+                    const uint32_t v_addr = smem_addr(sV + (gg % kStages) * kTile);
+#pragma unroll
+                    for (uint32_t h = 0; h < 2; ++h) {
+                        const uint32_t p_addr = smem_addr(sP + ((kPBufs * t + gtt % kPBufs) * 2u + h) * kTile);
+#pragma unroll
+                        for (uint32_t kk = 0; kk < 4; ++kk)
+                            umma<false>(tmem + 256u * t + 128u + 64u * h, smem_desc_sw128(p_addr + 32u * kk),
+                                        desc_mn_sw128(v_addr + (4u * h + kk) * 2048u), idesc_o, (j | kk) ? 1u : 0u);
+                    }
+                    umma_commit(&o_full[t]);
+                    umma_commit(&p_empty[kPBufs * t + gtt % kPBufs]);
+                    umma_commit(&kv_empty[gg % kStages]);
+                };
+                // S_0 needs this unit's Q, K_0 and the S columns back from the
+                // softmax (it loaded the previous unit's last S)
+                ok = mbar_wait(&q_full[qbuf], (qn >> 1) & 1u, abort_flag, p.err) &&
+                     mbar_wait(&kv_full[g % kStages], (g / kStages) & 1u, abort_flag, p.err) &&
+                     (gt == 0 || mbar_wait(&s_empty[t], (gt - 1u) & 1u, abort_flag, p.err));
                 if (!ok) break;
                 tc_fence_after();
-                issue_o(j);
+                issue_s(g);
+                mma_issued = true;
+                if (nkb == 1) umma_commit(&q_empty[qbuf]);
+                for (uint32_t j = 0; j < nkb; ++j) {
+                    const uint32_t gg = g + j, gtt = gt + j;
+                    // S_{j+1} as soon as the softmax holds S_j in registers (it is
+                    // computed while that softmax works on block j) ...
+                    if (j + 1 < nkb) {
+                        ok = mbar_wait(&kv_full[(gg + 1) % kStages], ((gg + 1) / kStages) & 1u, abort_flag, p.err) &&
+                             mbar_wait(&s_empty[t], gtt & 1u, abort_flag, p.err);
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue_s(gg + 1);
+                        if (j + 2 == nkb) umma_commit(&q_empty[qbuf]);  // the unit's last read of Q
+                    }
+                    // ... and the O updates of block j once its P is published (the
+                    // softmax has also rescaled O, or read out the previous unit's
+                    // O, by then)
+                    ok = mbar_wait(&p_full[t], gtt & 1u, abort_flag, p.err);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_o(gg, j, gtt);
+                }
+                g += nkb;
+                gt += nkb;
+                ++qn;
             }
         }
-    } else if ((warp - 2u) / 8u < ntiles) {
+    } else {
         const uint32_t t = (warp - 2u) / 8u;
         const uint32_t quarter = warp & 3u;
         const uint32_t half = ((warp - 2u) >> 2) & 1u;
@@ -229,8 +321,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float c = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
         constexpr float kRaise = 8.0f;                 // raise the maximum only beyond 2^8
         uint8_t* atoms = sP + (kPBufs * t * 2u + half) * kTile + row * 128u;  // + 2*kTile per buffer
-        float m = -INFINITY, l = 0.f;
-        bool ok = true;
         // warp-uniform wait: on a timeout every lane leaves together, so the
         // warp-collective TMEM accesses and votes below never diverge
         auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
@@ -249,139 +339,160 @@ __global__ void __launch_bounds__(kThreads, 1)
                 default: asm volatile("bar.sync 8, 64;" ::: "memory"); break;
             }
         };
-        for (uint32_t j = 0; j < nkb; ++j) {
-            if (!warp_wait(&s_full[t], j & 1u)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            uint32_t sr[2][32];
-            tmem_ld_32x32b_x32(tS + 64u * half, sr[0]);
-            tmem_ld_32x32b_x32(tS + 64u * half + 32u, sr[1]);
-            tmem_ld_wait();
-            // S_j is in registers: its TMEM columns may take S_{j+1}
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[t]);
-            float s[64];
+        uint32_t gt = 0;  // blocks this tile has computed (its S/P/O barrier phases)
+        uint32_t b2 = 0;  // blocks of two-tile units (the turn phases)
+        bool ok = true;
+        for (uint32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+            const bool turns = unit_at(p, u).ntiles == 2;
+            if (t == 1 && !turns) continue;
+            float m = -INFINITY, l = 0.f;
+            for (uint32_t j = 0; j < nkb; ++j) {
+                const uint32_t gtt = gt + j, bt = b2 + j;
+                if (!warp_wait(&s_full[t], gtt & 1u)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                uint32_t sr[2][32];
+                tmem_ld_32x32b_x32(tS + 64u * half, sr[0]);
+                tmem_ld_32x32b_x32(tS + 64u * half + 32u, sr[1]);
+                tmem_ld_wait();
+                // S_j is in registers: its TMEM columns may take S_{j+1}
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_empty[t]);
+                float s[64];
 #pragma unroll
-            for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(sr[i >> 5][i & 31]);
-            const uint32_t kbase = j * kKV + 64u * half;
-            if (kbase + 64u > p.tokens) {  // tail block: keys >= T do not exist
+                for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(sr[i >> 5][i & 31]);
+                const uint32_t kbase = j * kKV + 64u * half;
+                if (kbase + 64u > p.tokens) {  // tail block: keys >= T do not exist
 #pragma unroll
-                for (int i = 0; i < 64; ++i)
-                    if (kbase + i >= p.tokens) s[i] = -INFINITY;
-            }
-            // row maximum by a tree (short dependency chains)
-            float mt[16];
+                    for (int i = 0; i < 64; ++i)
+                        if (kbase + i >= p.tokens) s[i] = -INFINITY;
+                }
+                // row maximum by a tree (short dependency chains)
+                float mt[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) mt[i] = fmaxf(fmaxf(s[i], s[i + 16]), fmaxf(s[i + 32], s[i + 48]));
+                for (int i = 0; i < 16; ++i) mt[i] = fmaxf(fmaxf(s[i], s[i + 16]), fmaxf(s[i + 32], s[i + 48]));
 #pragma unroll
-            for (int w = 8; w >= 1; w >>= 1)
+                for (int v = 8; v >= 1; v >>= 1)
 #pragma unroll
-                for (int i = 0; i < w; ++i) mt[i] = fmaxf(mt[i], mt[i + w]);
-            const float mx = fmaxf(m, mt[0]);
-            if (j == 0) {
-                m = mx;
-            } else {
-                const bool raise = (mx - m) * c > kRaise;  // false while both are -inf
-                if (__any_sync(0xffffffffu, raise)) {
-                    // O_h must hold blocks 0..j-1 before it is rescaled
-                    if (!warp_wait(&o_full[t], (j - 1) & 1u)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const float alpha = raise ? ex2_approx((m - mx) * c) : 1.0f;
+                    for (int i = 0; i < v; ++i) mt[i] = fmaxf(mt[i], mt[i + v]);
+                const float mx = fmaxf(m, mt[0]);
+                if (j == 0) {
+                    m = mx;
+                } else {
+                    const bool raise = (mx - m) * c > kRaise;  // false while both are -inf
+                    if (__any_sync(0xffffffffu, raise)) {
+                        // O_h must hold blocks 0..j-1 before it is rescaled
+                        if (!warp_wait(&o_full[t], (gtt - 1u) & 1u)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const float alpha = raise ? ex2_approx((m - mx) * c) : 1.0f;
 #pragma unroll 1
-                    for (uint32_t k = 0; k < 8; ++k) {
-                        uint32_t ov[8];
-                        tmem_ld_x8(tO + 8u * k, ov);
-                        tmem_ld_wait();
+                        for (uint32_t k = 0; k < 8; ++k) {
+                            uint32_t ov[8];
+                            tmem_ld_x8(tO + 8u * k, ov);
+                            tmem_ld_wait();
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-                        tmem_st_x8(tO + 8u * k, ov);
-                    }
-                    tmem_st_wait();
-                    if (raise) {
-                        l *= alpha;
-                        m = mx;
+                            for (int i = 0; i < 8; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+                            tmem_st_x8(tO + 8u * k, ov);
+                        }
+                        tmem_st_wait();
+                        if (raise) {
+                            l *= alpha;
+                            m = mx;
+                        }
                     }
                 }
-            }
-            const float mc = m == -INFINITY ? 0.f : m * c;  // a half with no key yet has P = 0
-            // the MMA that last read this P buffer (block j - kPBufs) must be done
-            if (!warp_wait(&p_empty[kPBufs * t + j % kPBufs], ((j / kPBufs) & 1u) ^ 1u)) {
-                ok = false;
-                break;
-            }
-            // ping-pong: with two tiles the exp phases alternate (tile 0 block j,
-            // tile 1 block j, tile 0 block j+1, ...), so that each tile's max,
-            // loads and waits overlap the other tile's exponentials
-            if (ntiles == 2 && (t == 1 || j > 0) && !warp_wait(&turn[t], (t == 0 ? j - 1 : j) & 1u)) {
-                ok = false;
-                break;
-            }
-            // all 64 exponentials first (independent, in place: the MUFU queue
-            // stays full), then four partial sums and the f16 P tile
+                const float mc = m == -INFINITY ? 0.f : m * c;  // a half with no key yet has P = 0
+                // the MMA that last read this P buffer (kPBufs blocks back) must be done
+                if (!warp_wait(&p_empty[kPBufs * t + gtt % kPBufs], ((gtt / kPBufs) & 1u) ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                // ping-pong: in two-tile units the exp phases alternate (tile 0
+                // block j, tile 1 block j, tile 0 block j+1, ...; counted across
+                // units), so that each tile's max, loads and waits overlap the
+                // other tile's exponentials
+                if (turns && (t == 1 || bt > 0) && !warp_wait(&turn[t], (t == 0 ? bt - 1u : bt) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                // all 64 exponentials first (independent, in place: the MUFU queue
+                // stays full), then four partial sums and the f16 P tile
 #pragma unroll
-            for (int i = 0; i < 64; ++i) s[i] = ex2_approx(fmaf(s[i], c, -mc));
+                for (int i = 0; i < 64; ++i) s[i] = ex2_approx(fmaf(s[i], c, -mc));
 
-            float ls[4] = {0.f, 0.f, 0.f, 0.f};
+                float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                uint32_t h[4];
+                for (int q = 0; q < 8; ++q) {
+                    uint32_t hv[4];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    ls[u] += s[8 * q + 2 * u] + s[8 * q + 2 * u + 1];
-                    __half2 hh = __floats2half2_rn(s[8 * q + 2 * u], s[8 * q + 2 * u + 1]);
-                    h[u] = *reinterpret_cast<uint32_t*>(&hh);
+                    for (int v = 0; v < 4; ++v) {
+                        ls[v] += s[8 * q + 2 * v] + s[8 * q + 2 * v + 1];
+                        __half2 hh = __floats2half2_rn(s[8 * q + 2 * v], s[8 * q + 2 * v + 1]);
+                        hv[v] = *reinterpret_cast<uint32_t*>(&hh);
+                    }
+                    *reinterpret_cast<uint4*>(atoms + (gtt % kPBufs) * 2u * kTile + (((uint32_t)q ^ (row & 7u)) << 4)) =
+                        make_uint4(hv[0], hv[1], hv[2], hv[3]);
                 }
-                *reinterpret_cast<uint4*>(atoms + (j % kPBufs) * 2u * kTile + (((uint32_t)q ^ (row & 7u)) << 4)) =
-                    make_uint4(h[0], h[1], h[2], h[3]);
+                l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+                tc_fence_before();
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&p_full[t]);
+                    if (turns) mbar_arrive(&turn[t ^ 1u]);
+                }
             }
-            l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+            gt += nkb;
+            if (turns) b2 += nkb;
+            // merge the two key halves: m = max(m0, m1), weights exp2((m_h - m) c).
+            // Both warps of a pair always reach both pair barriers (also after a
+            // timeout) and leave the unit loop together.
+            if (ok) ok = warp_wait(&o_full[t], (gt - 1u) & 1u);  // the unit's last O (and P read) is done
+            tc_fence_after();
+            // (m, l, ok) travel through this row's own P atoms, free until this
+            // warp writes the next unit's first P
+            *reinterpret_cast<float4*>(atoms) = make_float4(m, l, ok ? 1.f : 0.f, 0.f);
+            pair_sync();
+            const float4 other = *reinterpret_cast<const float4*>(half ? atoms - kTile : atoms + kTile);
+            pair_sync();  // the partner has read this row's values before they are overwritten
+            ok = ok && other.z != 0.f;
+            const float m_o = other.x, l_o = other.y;
+            const float mm = fmaxf(m, m_o);
+            const float f_own = ex2_approx((m - mm) * c), f_oth = ex2_approx((m_o - mm) * c);
+            const float inv = 1.0f / fmaxf(l * f_own + l_o * f_oth, 1.0e-30f);
+            // this warp writes output dims [32*half, 32*half+32): its own O_h and the
+            // partner's O_{1-h} for those dims
+            uint32_t oa[32], ob[32];
+            tmem_ld_32x32b_x32(tO + 32u * half, oa);
+            tmem_ld_32x32b_x32(tS + 128u + 64u * (half ^ 1u) + 32u * half, ob);
+            tmem_ld_wait();
+            // O is in registers: the next unit's first O MMA (ordered after this
+            // warp's next P publication) may overwrite it
             tc_fence_before();
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&p_full[t]);
-                if (ntiles == 2) mbar_arrive(&turn[t ^ 1u]);
-            }
-        }
-        // merge the two key halves: m = max(m0, m1), weights exp2((m_h - m) c)
-        if (ok && nkb > 0) ok = warp_wait(&o_full[t], (nkb - 1) & 1u);
-        tc_fence_after();
-        float* xch = reinterpret_cast<float*>(sP + kPBufs * t * 2u * kTile);  // free once the last O MMA completed
-        xch[half * 128u + row] = m;
-        xch[256u + half * 128u + row] = l;
-        pair_sync();
-        const float m_o = xch[(half ^ 1u) * 128u + row];
-        const float l_o = xch[256u + (half ^ 1u) * 128u + row];
-        const float mm = fmaxf(m, m_o);
-        const float f_own = ex2_approx((m - mm) * c), f_oth = ex2_approx((m_o - mm) * c);
-        const float inv = 1.0f / fmaxf(l * f_own + l_o * f_oth, 1.0e-30f);
-        // this warp writes output dims [32*half, 32*half+32): its own O_h and the
-        // partner's O_{1-h} for those dims
-        uint32_t oa[32], ob[32];
-        tmem_ld_32x32b_x32(tO + 32u * half, oa);
-        tmem_ld_32x32b_x32(tS + 128u + 64u * (half ^ 1u) + 32u * half, ob);
-        tmem_ld_wait();
-        const uint32_t qrow = q0 + 128u * t + row;
-        if (ok && qrow < p.tokens) {
-            const float wa = f_own * inv, wb = f_oth * inv;
-            __half* dst = p.out + ((uint64_t)img * p.tokens + qrow) * p.out_ld + head * 64u + half * 32u;
+            const Unit w = unit_at(p, u);
+            const uint32_t qrow = w.q0 + 128u * t + row;
+            if (ok && qrow < p.tokens) {
+                const float wa = f_own * inv, wb = f_oth * inv;
+                __half* dst = p.out + ((uint64_t)w.img * p.tokens + qrow) * p.out_ld + w.head * 64u + half * 32u;
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-                uint32_t w[4];
+                for (int i = 0; i < 32; i += 8) {
+                    uint32_t hv[4];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const float x0 = __uint_as_float(oa[i + 2 * u]) * wa + __uint_as_float(ob[i + 2 * u]) * wb;
-                    const float x1 = __uint_as_float(oa[i + 2 * u + 1]) * wa + __uint_as_float(ob[i + 2 * u + 1]) * wb;
-                    __half2 hh = __floats2half2_rn(x0, x1);
-                    w[u] = *reinterpret_cast<uint32_t*>(&hh);
+                    for (int v = 0; v < 4; ++v) {
+                        const float x0 = __uint_as_float(oa[i + 2 * v]) * wa + __uint_as_float(ob[i + 2 * v]) * wb;
+                        const float x1 =
+                            __uint_as_float(oa[i + 2 * v + 1]) * wa + __uint_as_float(ob[i + 2 * v + 1]) * wb;
+                        __half2 hh = __floats2half2_rn(x0, x1);
+                        hv[v] = *reinterpret_cast<uint32_t*>(&hh);
+                    }
+                    *reinterpret_cast<uint4*>(dst + i) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
                 }
-                *reinterpret_cast<uint4*>(dst + i) = make_uint4(w[0], w[1], w[2], w[3]);
             }
         }
     }
@@ -451,11 +562,23 @@ int launch_attention_tc(__half* out, const __half* qkv, uint32_t batch, uint32_t
     p.tokens = tokens;
     p.heads = heads;
     p.num_kb = (tokens + kKV - 1) / kKV;
+    const uint32_t nqb = (tokens + kQ - 1) / kQ;
+    const bool single_tail = tokens - (nqb - 1) * kQ <= 128u;  // the last query block has one live tile
+    const uint64_t bh = (uint64_t)batch * heads;
+    if (bh * nqb > 0xFFFFFFFFull) return set_error(DAV2CUDA_INVALID_ARGUMENT, "attention: too many work units");
+    p.units = (uint32_t)(bh * nqb);
+    p.full_per_bh = single_tail ? nqb - 1 : nqb;
+    p.full_units = (uint32_t)(bh * p.full_per_bh);
     p.out_ld = out_ld;
     p.out = out;
     p.err = device_error_word();
     if (!p.err) return set_error(DAV2CUDA_INTERNAL_ERROR, "attention: no device error word");
-    dim3 grid((tokens + kQ - 1) / kQ, heads, batch);
+    static int sms[64] = {0};
+    if (!sms[dev & 63] && cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return set_error(DAV2CUDA_LAUNCH_FAILED, "attention: cannot query the SM count");
+    // persistent: one CTA per SM (the TMEM allocation keeps it at one), each
+    // walking units blockIdx.x + k * gridDim.x
+    const uint32_t grid = p.units < (uint32_t)sms[dev & 63] ? p.units : (uint32_t)sms[dev & 63];
     attention_tc_kernel<<<grid, kThreads, kSmem, st>>>(tm, p);
     return check_launch("attention_tc");
 }

@@ -100,6 +100,32 @@ __device__ __forceinline__ float ex2_approx(float x) {
 }
 
 
+// Packed f32x2 arithmetic of sm_100 (two IEEE fp32 lanes per instruction,
+// each lane rounded exactly as the scalar operation) and the three-input
+// maximum: they halve the issue slots of the softmax's per-score work.
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+    return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+
+__device__ __forceinline__ void ffma2(float& x0, float& x1, uint64_t mul, uint64_t add) {
+    asm("{\n\t.reg .b64 a;\n\tmov.b64 a, {%0, %1};\n\tfma.rn.f32x2 a, a, %2, %3;\n\tmov.b64 {%0, %1}, a;\n\t}"
+        : "+f"(x0), "+f"(x1)
+        : "l"(mul), "l"(add));
+}
+
+__device__ __forceinline__ void fadd2(float& a0, float& a1, float x0, float x1) {
+    asm("{\n\t.reg .b64 a, b;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 b, {%2, %3};\n\tadd.rn.f32x2 a, a, b;\n\t"
+        "mov.b64 {%0, %1}, a;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(x0), "f"(x1));
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr) {
     // MN-major operand, 128-byte swizzle: 8-row (K) groups 1024 B apart.
     return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
@@ -370,15 +396,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int i = 0; i < 64; ++i)
                         if (kbase + i >= p.tokens) s[i] = -INFINITY;
                 }
-                // row maximum by a tree (short dependency chains)
-                float mt[16];
+                // row maximum by a tree of three-input maxima (32 operations, depth 4)
+                float ma[22], mb[8];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) mt[i] = fmaxf(fmaxf(s[i], s[i + 16]), fmaxf(s[i + 32], s[i + 48]));
+                for (int i = 0; i < 21; ++i) ma[i] = fmax3(s[3 * i], s[3 * i + 1], s[3 * i + 2]);
+                ma[21] = s[63];
 #pragma unroll
-                for (int v = 8; v >= 1; v >>= 1)
-#pragma unroll
-                    for (int i = 0; i < v; ++i) mt[i] = fmaxf(mt[i], mt[i + v]);
-                const float mx = fmaxf(m, mt[0]);
+                for (int i = 0; i < 7; ++i) mb[i] = fmax3(ma[3 * i], ma[3 * i + 1], ma[3 * i + 2]);
+                mb[7] = ma[21];
+                const float mx = fmax3(fmax3(mb[0], mb[1], mb[2]), fmax3(mb[3], mb[4], mb[5]), fmax3(mb[6], mb[7], m));
                 if (j == 0) {
                     m = mx;
                 } else {
@@ -422,24 +448,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 // all 64 exponentials first (independent, in place: the MUFU queue
-                // stays full), then four partial sums and the f16 P tile
+                // stays full; arguments s*c - m*c two at a time), then eight
+                // partial sums (pairwise) and the f16 P tile
+                const uint64_t mul2 = pack_f32x2(c, c), add2 = pack_f32x2(-mc, -mc);
 #pragma unroll
-                for (int i = 0; i < 64; ++i) s[i] = ex2_approx(fmaf(s[i], c, -mc));
+                for (int i = 0; i < 64; i += 2) ffma2(s[i], s[i + 1], mul2, add2);
+#pragma unroll
+                for (int i = 0; i < 64; ++i) s[i] = ex2_approx(s[i]);
 
-                float ls[4] = {0.f, 0.f, 0.f, 0.f};
+                float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
                     uint32_t hv[4];
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
-                        ls[v] += s[8 * q + 2 * v] + s[8 * q + 2 * v + 1];
+                        fadd2(ls[2 * v], ls[2 * v + 1], s[8 * q + 2 * v], s[8 * q + 2 * v + 1]);
                         __half2 hh = __floats2half2_rn(s[8 * q + 2 * v], s[8 * q + 2 * v + 1]);
                         hv[v] = *reinterpret_cast<uint32_t*>(&hh);
                     }
                     *reinterpret_cast<uint4*>(atoms + (gtt % kPBufs) * 2u * kTile + (((uint32_t)q ^ (row & 7u)) << 4)) =
                         make_uint4(hv[0], hv[1], hv[2], hv[3]);
                 }
-                l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+                l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
                 tc_fence_before();
                 fence_async_smem();
                 __syncwarp();

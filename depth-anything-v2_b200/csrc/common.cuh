@@ -294,6 +294,33 @@ __device__ __forceinline__ uint32_t q8(float v) {
     return static_cast<uint32_t>(__float2int_rn(v)) & 0xffu;
 }
 
+// ------------------------------------------------------- packed f32x2 math
+// sm_100 executes two IEEE fp32 lanes per instruction (fma/mul/add .rn .f32x2).
+// The assembler may contract a packed multiply and a following packed add
+// into one fused operation, so these serve approximations (GELU, softmax)
+// and not arithmetic that must reproduce separately rounded steps.
+__device__ __forceinline__ void f2_fma(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                       float c1) {
+    asm("{\n\t.reg .b64 a, b, c;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+        "fma.rn.f32x2 a, a, b, c;\n\tmov.b64 {%0, %1}, a;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+__device__ __forceinline__ void f2_mul(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 a, b;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+        "mul.rn.f32x2 a, a, b;\n\tmov.b64 {%0, %1}, a;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+__device__ __forceinline__ void f2_add(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 a, b;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+        "add.rn.f32x2 a, a, b;\n\tmov.b64 {%0, %1}, a;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // Exact-erf GELU (torch.nn.GELU) with erf from Abramowitz & Stegun 7.1.26
 // (|error| <= 1.5e-7): erf(z) = 1 - t(a1 + t(a2 + t(a3 + t(a4 + t a5)))) e^{-z^2},
 // t = 1/(1 + p z) for z >= 0, odd extension for z < 0. Used where GELU is
@@ -305,6 +332,26 @@ __device__ __forceinline__ float gelu_erf_as(float v) {
                                      -0.284496736f), 0.254829592f);
     const float e = 1.0f - poly * __expf(-z * z);
     return 0.5f * v * (1.0f + copysignf(e, v));
+}
+
+// gelu_erf_as on a pair, its fp32 multiply-adds issued as f32x2 (the same
+// operations and roundings per value, about half the instructions).
+__device__ __forceinline__ void gelu_erf_as2(float& v0, float& v1) {
+    float z0, z1, d0, d1, p0, p1, q0, q1, e0, e1, h0, h1;
+    f2_mul(z0, z1, fabsf(v0), fabsf(v1), 0.70710678118654752f, 0.70710678118654752f);
+    f2_fma(d0, d1, 0.3275911f, 0.3275911f, z0, z1, 1.0f, 1.0f);
+    const float t0 = __fdividef(1.0f, d0), t1 = __fdividef(1.0f, d1);
+    f2_fma(p0, p1, t0, t1, 1.061405429f, 1.061405429f, -1.453152027f, -1.453152027f);
+    f2_fma(p0, p1, t0, t1, p0, p1, 1.421413741f, 1.421413741f);
+    f2_fma(p0, p1, t0, t1, p0, p1, -0.284496736f, -0.284496736f);
+    f2_fma(p0, p1, t0, t1, p0, p1, 0.254829592f, 0.254829592f);
+    f2_mul(p0, p1, t0, t1, p0, p1);
+    f2_mul(q0, q1, -z0, -z1, z0, z1);
+    const float x0 = __expf(q0), x1 = __expf(q1);
+    f2_fma(e0, e1, -p0, -p1, x0, x1, 1.0f, 1.0f);
+    f2_add(e0, e1, 1.0f, 1.0f, copysignf(e0, v0), copysignf(e1, v1));
+    f2_mul(h0, h1, 0.5f, 0.5f, v0, v1);
+    f2_mul(v0, v1, h0, h1, e0, e1);
 }
 
 // Four bytes q8(x[k] / scale) (IEEE quotient) packed little-endian, for a

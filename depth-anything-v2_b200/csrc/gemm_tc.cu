@@ -115,7 +115,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParamsDev& p, const uin
     }
     if (f & kEpiGelu) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_erf_as(v[j]);
+        for (int j = 0; j < 32; j += 2) gelu_erf_as2(v[j], v[j + 1]);
     }
 
     // --- output-head dot product (one value per row)
@@ -363,7 +363,10 @@ __device__ __forceinline__ void epilogue_rows(const GemmParamsDev& p, const uint
             for (int k = 0; k < 4; ++k) {
                 if (kInt8) v[k] = __fmul_rn(v[k], sw[k]);
                 if (BIAS) v[k] = __fadd_rn(v[k], bs[k]);
-                if (GELU) v[k] = gelu_erf_as(v[k]);
+            }
+            if (GELU) {
+                gelu_erf_as2(v[0], v[1]);
+                gelu_erf_as2(v[2], v[3]);
             }
             const bool vec = cols_full && ((base[i] & 3u) == 0) && (!CT || (p.ct_cout & 3u) == 0);
             if (F32) {
@@ -503,13 +506,18 @@ __device__ __forceinline__ void dequant4(const uint32_t* acc, float si, const fl
     if (kInt8) w = ldg4(s_w + c);
     if (BIAS) b = ldg4(bias + c);
     const float ws[4] = {w.x, w.y, w.z, w.w}, bs[4] = {b.x, b.y, b.z, b.w};
+    // (acc * s_in) * s_w + b with the reference's separate roundings (scalar:
+    // bit-exact with the oracle), then GELU on pairs of columns
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         float t = kInt8 ? (float)(int32_t)acc[k] : __uint_as_float(acc[k]);
         if (kInt8) t = __fmul_rn(__fmul_rn(t, si), ws[k]);
         if (BIAS) t = __fadd_rn(t, bs[k]);
-        if (GELU) t = gelu_erf_as(t);
         v[k] = t;
+    }
+    if (GELU) {
+        gelu_erf_as2(v[0], v[1]);
+        gelu_erf_as2(v[2], v[3]);
     }
 }
 

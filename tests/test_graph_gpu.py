@@ -274,3 +274,20 @@ def test_inferbridge_bgra8_vs_oracle(cuda, dav2lib, models, metric_models, kind,
     assert out.min() >= 0.0 and (metric or out.max() == 1.0)
     assert err < (1e-2 if kind == "relative" else 1e-3)  # measured 2.0e-3 / 1.4e-4
 
+
+@pytest.mark.parametrize("prec", ["fp16", "int8"])
+def test_batch_matches_single_images(cuda, dav2lib, models, prec):
+    """Six 518x518 images in one batched call (8220 token rows) against the
+    same images one at a time: every operator of the graph is row- or
+    image-independent, so batching must not change a single value."""
+    imgs = np.random.default_rng(5).standard_normal((6, 3, 518, 518)).astype(np.float32)
+    ctx = context(dav2lib, models["strong"][0], flags=capi.FLAGS[prec])
+    try:
+        batched = infer_tensor_batch(dav2lib, ctx, imgs)
+        single = np.stack([infer_tensor(dav2lib, ctx, im) for im in imgs])
+    finally:
+        dav2lib.dav2_destroy(ctx)
+    rel, rng_rel = errs(batched, single.astype(np.float64))
+    print(f"batch vs single ({prec}): rel {rel:.2e} range-rel {rng_rel:.2e}")
+    assert rel < 1e-5
+

@@ -22,8 +22,10 @@ def rng(seed=0):
 
 
 # ---------------------------------------------------------------- row ops
-@pytest.mark.parametrize("rows,cols", [(4, 17), (37, 384), (129, 768), (300, 1024), (5, 1000)])
+@pytest.mark.parametrize("rows,cols", [(4, 17), (37, 384), (129, 768), (300, 1024), (5, 1000),
+                                       (8200, 1024), (9001, 768)])
 def test_layer_norm(cuda, dav2lib, rows, cols):
+    """Row counts from a handful to above the ViT-S batch-6 token count."""
     r = rng(rows)
     x = r.standard_normal((rows, cols)).astype(np.float32) * 3 + 0.5
     w = r.standard_normal(cols).astype(np.float32)

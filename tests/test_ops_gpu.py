@@ -382,7 +382,10 @@ def test_attention_reference_kat(cuda, dav2lib):
 
 
 @pytest.mark.parametrize("batch,tokens,heads", [(1, 1370, 6), (2, 130, 16), (1, 63, 2), (1, 5477, 1),
-                                                 (1, 1300, 2), (3, 384, 3)])
+                                                 (1, 1300, 2), (3, 384, 3),
+                                                 # more work units than SMs: each persistent CTA walks
+                                                 # several units (two-tile units, then single-tile tails)
+                                                 (4, 1370, 16), (3, 256, 64), (5, 100, 40), (2, 513, 50)])
 def test_attention(cuda, dav2lib, batch, tokens, heads):
     qkv = (rng(tokens).standard_normal((batch, tokens, 3 * heads * 64)) * 0.5).astype(np.float32)
     ws = dav2lib.dav2cuda_attention_head64_workspace_size(batch, tokens, heads)

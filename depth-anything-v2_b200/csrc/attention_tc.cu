@@ -12,8 +12,9 @@
 // tile) are numbered after all two-tile units, which spreads them evenly over
 // the CTAs. Tile t uses TMEM columns 256t + [0,128) for S and 256t + 128 + 64h
 // for O_h, h = key half.
-//   warp 0       TMA: per unit the Q tiles (double-buffered per tile), then
-//                K_j / V_j (128 keys x 64 dims each) into a 3-stage ring that
+//   warp 0       TMA: per unit the Q tiles (loaded as soon as the previous
+//                unit's last S is computed), then K_j / V_j (128 keys x 64
+//                dims each) into a 4-stage ring that
 //                runs on across units. The 3-D tensor map over qkv [B][T][3E]
 //                zero-fills rows past T.
 //   warps 1, 18  MMA issuers, one per tile (so neither tile's pipeline waits
@@ -63,12 +64,13 @@ struct AttnParams {
 
 constexpr uint32_t kQTiles = 2;       // 128-query tiles per unit
 constexpr uint32_t kQ = 128 * kQTiles;  // queries per unit
-constexpr uint32_t kQBufs = 2;        // Q buffers per tile (the next unit's Q loads early)
+constexpr uint32_t kQBufs = 1;        // Q buffers per tile
 constexpr uint32_t kKV = 128;         // keys per block
 // K/V ring depth and P buffers per tile (P_j in buffer j % kPBufs). Measured
-// on B200 (ViT-L, 64 images): 3 stages x 1 P buffer beats 2 x 2 (the only
-// double-buffered-P layout that fits), whose K/V ring runs dry.
-constexpr uint32_t kStages = 3;
+// on B200 (ViT-L, 64 images, one launch): 1 Q buffer x 4 stages x 1 P buffer
+// 0.839 ms, 2 x 3 x 1 0.846 ms, 1 x 2 x 2 (the only double-buffered-P layout
+// that fits) 1.006 ms: its K/V ring runs dry.
+constexpr uint32_t kStages = 4;
 constexpr uint32_t kPBufs = 1;
 constexpr uint32_t kTile = 128 * 128; // bytes of a 128 x 64 f16 tile
 constexpr uint32_t kThreads = 64 + 256 * kQTiles + 32;  // TMA, MMA(tile 0), softmax, MMA(tile 1)
@@ -76,7 +78,7 @@ constexpr uint32_t kMma1Warp = 2 + 8 * kQTiles;
 // Q[tile][buffer], K[stage], V[stage], P[tile][buffer][key half], 1 KB barriers
 constexpr uint32_t kSmem = kTile * (kQBufs * kQTiles + 2 * kStages + 2 * kPBufs * kQTiles) + 1024;
 constexpr uint32_t kBarrierBytes = 8 * (2 * kStages + 2 * kQBufs * kQTiles + (6 + kPBufs) * kQTiles) + 8;
-static_assert(kQTiles == 2 && kQBufs == 2, "unit decoding and buffer parities assume two tiles, two Q buffers");
+static_assert(kQTiles == 2, "unit decoding assumes two tiles per unit");
 static_assert(kBarrierBytes <= 1024, "barrier block overflows its 1 KB");
 static_assert(kSmem <= 232448, "shared memory above the per-block limit");
 
@@ -226,10 +228,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (uint32_t t = 0; t < kQTiles; ++t) {
                     if (t >= w.ntiles || !ok) break;
-                    const uint32_t b = qn[t] & 1u;
+                    const uint32_t b = qn[t] % kQBufs;
                     // the buffer's previous Q (two units back) must be done
                     if (qn[t] >= kQBufs &&
-                        !mbar_wait(&q_empty[kQBufs * t + b], ((qn[t] >> 1) - 1u) & 1u, abort_flag, p.err)) {
+                        !mbar_wait(&q_empty[kQBufs * t + b], ((qn[t] / kQBufs) - 1u) & 1u, abort_flag, p.err)) {
                         ok = false;
                         break;
                     }
@@ -277,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     continue;
                 }
-                const uint32_t qbuf = kQBufs * t + (qn & 1u);
+                const uint32_t qbuf = kQBufs * t + qn % kQBufs;
                 const uint32_t q_addr = smem_addr(sQ + qbuf * kTile);
                 auto issue_s = [&](uint32_t gg) {
                     const uint32_t k_addr = smem_addr(sK + (gg % kStages) * kTile);
@@ -303,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 };
                 // S_0 needs this unit's Q, K_0 and the S columns back from the
                 // softmax (it loaded the previous unit's last S)
-                ok = mbar_wait(&q_full[qbuf], (qn >> 1) & 1u, abort_flag, p.err) &&
+                ok = mbar_wait(&q_full[qbuf], (qn / kQBufs) & 1u, abort_flag, p.err) &&
                      mbar_wait(&kv_full[g % kStages], (g / kStages) & 1u, abort_flag, p.err) &&
                      (gt == 0 || mbar_wait(&s_empty[t], (gt - 1u) & 1u, abort_flag, p.err));
                 if (!ok) break;

@@ -694,15 +694,15 @@ int launch_layer_norm(void* out, float* out_scales, const float* in, const float
         layer_norm_generic_kernel<<<rows, 64, 0, st>>>(static_cast<float*>(out), in, w, b, cols, eps);
         return check_launch("layer_norm_generic");
     }
-    const unsigned grid = (unsigned)(((uint64_t)rows * 32 + 255) / 256);
+    const unsigned grid = (unsigned)(((uint64_t)rows * 32 + 127) / 128);  // 4 rows per block
     const int vpl = (int)((cols / 4 + 31) / 32);
 #define LN_CASE(V)                                                                                         \
     case V:                                                                                                \
         switch (out_kind) {                                                                                \
-            case kLnF32: layer_norm_warp_kernel<V, kLnF32><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break; \
-            case kLnF16: layer_norm_warp_kernel<V, kLnF16><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break; \
-            case kLnBF16: layer_norm_warp_kernel<V, kLnBF16><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break; \
-            default: layer_norm_warp_kernel<V, kLnS8><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break; \
+            case kLnF32: layer_norm_warp_kernel<V, kLnF32><<<grid, 128, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break; \
+            case kLnF16: layer_norm_warp_kernel<V, kLnF16><<<grid, 128, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break; \
+            case kLnBF16: layer_norm_warp_kernel<V, kLnBF16><<<grid, 128, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break; \
+            default: layer_norm_warp_kernel<V, kLnS8><<<grid, 128, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break; \
         }                                                                                                  \
         break;
     switch (vpl) {
@@ -715,10 +715,10 @@ int launch_layer_norm(void* out, float* out_scales, const float* in, const float
         case 5:
         case 7:
             switch (out_kind) {
-                case kLnF32: layer_norm_warp_kernel<8, kLnF32><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break;
-                case kLnF16: layer_norm_warp_kernel<8, kLnF16><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break;
-                case kLnBF16: layer_norm_warp_kernel<8, kLnBF16><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break;
-                default: layer_norm_warp_kernel<8, kLnS8><<<grid, 256, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break;
+                case kLnF32: layer_norm_warp_kernel<8, kLnF32><<<grid, 128, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break;
+                case kLnF16: layer_norm_warp_kernel<8, kLnF16><<<grid, 128, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break;
+                case kLnBF16: layer_norm_warp_kernel<8, kLnBF16><<<grid, 128, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break;
+                default: layer_norm_warp_kernel<8, kLnS8><<<grid, 128, 0, st>>>(out, out_scales, in, w, b, rows, cols, eps, out_group, in_group, in_offset); break;
             }
             break;
         default: return set_error(DAV2CUDA_INVALID_ARGUMENT, "layer_norm: unsupported width");

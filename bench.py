@@ -8,23 +8,35 @@ GPU, images/s on N B200s of one node.
 One step = one batch of `--batch` random-u8 518x518 BGR8 images (seeded per
 image) through the whole network (GPU preprocessing -> encoder -> DPT head),
 one replica per GPU, no collectives on the data path (images are
-independent; "scaling": "weak").
+independent; "scaling": "weak"). The process group (gloo, host side) only
+carries the timing barrier and the max-over-ranks reduction.
 
   value    images/s with the images already in HBM: dav2_infer_device_bgr8_batch
            on a CUDA stream, timed with CUDA events (max over ranks);
   e2e      the same through dav2_infer_bgr8_batch with pinned host buffers:
            host->device copy of the BGR8 batch and device->host copy of the
            depth maps inside the timed region (host clock, max over ranks);
+  check    outside the timed region: image 0 of the device-path and of the
+           host-path batch against a single-image dav2_infer_bgr8 call (max
+           relative difference; every operation is per row or per image, so
+           it is 0 unless a kernel's arithmetic depends on the batch);
   roofline the dominant operation of one step (largest share of the
            executor's live per-operation event timing, dav2_profile_operations)
-           with its algorithmic tensor work per launch, against the tensor peak
+           with its algorithmic tensor work per launch against the tensor peak
            of its operand type: int8 = cuBLAS int8 GEMM measured in this run
-           (torch._int_mm, 8192^3); f16 = MEASURED_PEAKS.json's sustained bf16
-           figure, else the pool's stated fallback (1.4 PFLOP/s sustained);
-           `ops` lists the same for every GEMM-family operation;
-  cpu_baseline (rank 0, N=1) the reference's CPU path — its PyTorch-CPU fp32
-           forward, restated in oracle/torch_graph.py — on one image, all
-           host cores.
+           (torch._int_mm, 8192^3, burst); f16 = MEASURED_PEAKS.json's
+           sustained bf16 figure, else the pool's stated fallback. `ops` lists
+           every GEMM-family operation with its algorithmic bytes too and the
+           fraction of max(bytes / HBM, work / peak) it reaches; `hbm_ops`
+           the bandwidth-bound operations of the graph against both the
+           measured copy bandwidth and the 8 TB/s nominal;
+  op_microbench (rank 0, N=1) BASELINE configuration 2: the stand-alone
+           LayerNorm, erf-GELU, row softmax and int8 3x3-conv + 2x upsample
+           kernels at their BASELINE shapes, achieved GB/s of algorithmic bytes;
+  cpu_baseline (rank 0, N=1) the reference's CPU path — OpenCV-exact bicubic
+           BGR8 preprocessing (the oracle's bit-exact restatement of
+           src/image.cpp) and the PyTorch-CPU fp32 forward (oracle/torch_graph.py)
+           — on one image, all host cores, median of 5 after one warm-up.
 --impl reference times only that CPU path (rank 0), one image per step.
 """
 from __future__ import annotations
@@ -45,9 +57,10 @@ sys.path[:0] = [str(ROOT / "depth-anything-v2_b200"), str(ROOT / "oracle")]
 
 METRIC = "ViT-L 518^2 images/s (full graph, int8 path)"
 GFLOP_PER_IMAGE = 1304.2  # ViT-L @518 (torch.utils.flop_counter on the reference model)
+NOMINAL_HBM_GBS = 8000.0  # B200 HBM3e nominal (DGX figure) named by the BASELINE metric
 
 
-def parse():
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=8)
@@ -58,12 +71,30 @@ def parse():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--precision", choices=["int8", "fp16"], default="int8")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-microbench", action="store_true")
     ap.add_argument("--profile-only", action="store_true", help="print the per-operation profile and exit")
-    return ap.parse_args()
+    return ap.parse_args(argv)
 
 
 def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def shard_seeds(rank: int, batch: int) -> range:
+    """Image seeds of one rank: a contiguous, disjoint block of `batch` seeds
+    per rank (rank r generates images r*batch ... r*batch + batch - 1)."""
+    return range(rank * batch, (rank + 1) * batch)
+
+
+def max_over_ranks(value: float, dist=None) -> float:
+    """Max of a host-side float over all ranks (gloo all-reduce on the CPU)."""
+    if dist is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 def model_path(encoder: str, rank: int, world: int) -> Path:
@@ -79,11 +110,10 @@ def model_path(encoder: str, rank: int, world: int) -> Path:
     return path
 
 
-def images(n, size, seed0):
+def images(seeds, size):
     import numpy as np
 
-    return np.stack([np.random.default_rng(seed0 + i).integers(0, 256, (size, size, 3), dtype=np.uint8)
-                     for i in range(n)])
+    return np.stack([np.random.default_rng(s).integers(0, 256, (size, size, 3), dtype=np.uint8) for s in seeds])
 
 
 class ClockSampler:
@@ -154,52 +184,56 @@ def int8_peak_tops(torch):
     return 2 * n ** 3 / (best * 1e-3) / 1e12
 
 
+def _peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        try:
+            return json.loads(f.read_text())
+        except (ValueError, OSError):
+            pass
+    return {}
+
+
 def f16_peak_tflops():
     """Dense 16-bit tensor peak for an operation timed inside a long step:
     MEASURED_PEAKS.json (driver-written) sustained bf16 figure, else the
     pool's stated fallback."""
-    f = ROOT / "MEASURED_PEAKS.json"
-    if f.exists():
-        try:
-            d = json.loads(f.read_text())
-            for k in ("bf16_tflops_sustained", "bf16_tflops"):
-                if d.get(k):
-                    return float(d[k]), f"MEASURED_PEAKS.json {k} (of measured)"
-        except (ValueError, OSError):
-            pass
+    d = _peaks()
+    for k in ("bf16_tflops_sustained", "bf16_tflops"):
+        if d.get(k):
+            return float(d[k]), f"MEASURED_PEAKS.json {k} (of measured)"
     return 1400.0, "fallback 1.4 PFLOP/s sustained bf16 (of fallback; MEASURED_PEAKS.json absent)"
 
 
 def hbm_peak_gbs():
     """HBM copy bandwidth: MEASURED_PEAKS.json (driver-written) else the pool's
     stated fallback."""
-    f = ROOT / "MEASURED_PEAKS.json"
-    if f.exists():
-        try:
-            d = json.loads(f.read_text())
-            if d.get("hbm_gbs"):
-                return float(d["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (of measured)"
-        except (ValueError, OSError):
-            pass
+    d = _peaks()
+    if d.get("hbm_gbs"):
+        return float(d["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (of measured)"
     return 6650.0, "fallback 6.65 TB/s (of fallback; MEASURED_PEAKS.json absent)"
+
+
+def graph_shapes(encoder, batch, size):
+    from dav2_b200.dav2file import ARCH
+
+    d, heads, blocks, _, f, oc = ARCH[encoder]
+    p = size // 14
+    return d, heads, f, p, batch * (p * p + 1)
 
 
 def op_bytes(encoder, batch, size, int8):
     """Algorithmic HBM bytes per launch of the bandwidth-bound operations the
     executor profiles by name: every tensor read once and written once."""
-    from dav2_b200.dav2file import ARCH
-
-    d, heads, blocks, _, f, oc = ARCH[encoder]
-    p = size // 14
-    r = batch * (p * p + 1)
+    d, heads, f, p, r = graph_shapes(encoder, batch, size)
     code = 1 if int8 else 2  # int8 codes (+ f32 row scale) or f16 values
     out = {
         "ln1": r * d * 4 + r * d * code + (r * 4 if int8 else 0),
         "ln2": r * d * 4 + r * d * code + (r * 4 if int8 else 0),
     }
-    if int8:
-        out["quantize hidden"] = r * 4 * d * 2 + r * 4 * d + r * 4
-        out["quantize attention"] = r * d * 2 + r * d + r * 4
+    if int8:  # f32 quantizer inputs (the reference's precision), int8 codes + f32 row scales out
+        out["quantize hidden"] = r * 4 * d * 4 + r * 4 * d + r * 4
+        out["quantize attention"] = r * d * 4 + r * d + r * 4
     # align-corners bilinear on channels-last f16 maps (channels padded to 64)
     fp = -(-f // 64) * 64
     l4 = (p + 2 - 3) // 2 + 1
@@ -210,81 +244,170 @@ def op_bytes(encoder, batch, size, int8):
     return out
 
 
-def op_work(encoder, batch, size):
-    """Algorithmic tensor ops per launch of each GEMM-family operation name
-    (2*M*N*K), for the operations the executor profiles by name."""
-    from dav2_b200.dav2file import ARCH
-
-    d, heads, blocks, _, f, oc = ARCH[encoder]
-    p = size // 14
-    t = p * p + 1
-    r = batch * t
+def op_work(encoder, batch, size, int8):
+    """Algorithmic tensor ops (2*M*N*K) and HBM bytes (operands, outputs and
+    residuals once each) per launch of each GEMM-family operation name."""
+    d, heads, f, p, r = graph_shapes(encoder, batch, size)
+    a = 1 if int8 else 2          # A operand bytes per element
+    s = r * 4 if int8 else 0      # f32 row scales
+    w = 1 if int8 else 2          # weight bytes per element
+    hid = 4 if int8 else 2        # fc1 output: f32 hidden (int8 path) or f16
+    att = 4 if int8 else 2        # attention output: f32 (int8 path) or f16
     return {
-        "qkv": 2 * r * 3 * d * d, "proj": 2 * r * d * d, "fc1": 2 * r * 4 * d * d, "fc2": 2 * r * 4 * d * d,
-        "attention": batch * heads * 4 * t * t * 64,
+        "qkv": (2 * r * 3 * d * d, r * d * a + s + 3 * d * d * w + r * 3 * d * 2),
+        "proj": (2 * r * d * d, r * d * a + s + d * d * w + 2 * r * d * 4),
+        "fc1": (2 * r * 4 * d * d, r * d * a + s + 4 * d * d * w + r * 4 * d * hid),
+        "fc2": (2 * r * 4 * d * d, r * 4 * d * a + s + 4 * d * d * w + 2 * r * d * 4),
+        "attention": (batch * heads * 4 * (p * p + 1) ** 2 * 64, r * 3 * d * 2 + r * d * att),
     }
 
 
-def cpu_baseline(encoder, size, seconds_cap=40.0):
-    """The reference's CPU path (PyTorch CPU fp32 forward, oracle/torch_graph.py)
-    on one image with all host threads."""
+def cpu_forward_fn(encoder, size, threads):
+    """The reference's CPU path for one 518x518 BGR8 image: the oracle's
+    bit-exact restatement of src/image.cpp (network shape, OpenCV bicubic,
+    ImageNet normalization) then the PyTorch-CPU fp32 forward."""
     import numpy as np
     import torch
 
+    import oracle
     import torch_graph
     from dav2_b200 import dav2file
 
-    threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     w = torch_graph.to_torch(dav2file.random_state_dict(encoder, seed=0))
-    x = np.random.default_rng(0).standard_normal((1, 3, size, size)).astype(np.float32)
-    t0 = time.perf_counter()
-    torch_graph.forward(w, x, encoder)
-    first = time.perf_counter() - t0
-    best = first
-    if first * 2 < seconds_cap:
+    bgr = np.random.default_rng(0).integers(0, 256, (size, size, 3), dtype=np.uint8)
+
+    def run():
+        nw, nh = oracle.network_shape(size, size, size)
+        x = oracle.preprocess_bgr8(bgr, nw, nh)[None]
+        return torch_graph.forward(w, x, encoder, out_size=(size, size))
+
+    return run
+
+
+def cpu_baseline(encoder, size, runs=5):
+    threads = os.cpu_count() or 1
+    run = cpu_forward_fn(encoder, size, threads)
+    run()  # warm-up
+    times = []
+    for _ in range(runs):
         t0 = time.perf_counter()
-        torch_graph.forward(w, x, encoder)
-        best = min(best, time.perf_counter() - t0)
-    return {"value": round(1.0 / best, 4), "unit": "images/s", "cores": threads, "kind": "port",
-            "sample": f"1 image {encoder} {size}x{size}, fp32 PyTorch-CPU restatement of the reference forward "
-                      f"(oracle/torch_graph.py), best of {1 if first * 2 >= seconds_cap else 2} runs"}
+        run()
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": round(1.0 / med, 4), "unit": "images/s", "cores": threads, "kind": "port",
+            "sample": f"1 image {encoder} {size}x{size} BGR8 per run (bicubic preprocessing + fp32 PyTorch-CPU "
+                      f"forward restating the reference, oracle/), median of {runs} after 1 warm-up"}
 
 
 def run_reference(args):
     rank, _, world = dist_env()
     if rank != 0:
         return
-    import numpy as np
-    import torch
-
-    import torch_graph
-    from dav2_b200 import dav2file
-
     threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    w = torch_graph.to_torch(dav2file.random_state_dict(args.encoder, seed=0))
-    x = np.random.default_rng(0).standard_normal((1, 3, args.size, args.size)).astype(np.float32)
+    run = cpu_forward_fn(args.encoder, args.size, threads)
     for _ in range(args.warmup):
-        torch_graph.forward(w, x, args.encoder)
+        run()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        torch_graph.forward(w, x, args.encoder)
+        run()
     dt = time.perf_counter() - t0
     value = args.steps / dt
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "images/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.encoder} {args.size}x{args.size} full graph, 1 image per step (bounded "
-                               f"sample of the 64-image batch)", "precision": "fp32 (the reference CPU path)",
+        "config": {"workload": f"{args.encoder} {args.size}x{args.size} full graph from a BGR8 image, 1 image per "
+                               f"step (bounded sample of the 64-image batch)", "precision": "fp32 (the reference CPU path)",
                    "parallelism": "host threads"},
         "cpu_baseline": {"value": round(value, 4), "unit": "images/s", "cores": threads, "kind": "port",
-                         "sample": "1 image per step, PyTorch-CPU fp32 restatement of the reference forward "
-                                   "(oracle/torch_graph.py)"},
+                         "sample": "1 image per step: bicubic BGR8 preprocessing + PyTorch-CPU fp32 forward "
+                                   "restating the reference (oracle/)"},
         "e2e": {"value": round(value, 4), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def _time_kernel(torch, fn, flush, iters=10, warmup=3):
+    """Median device time (ms) of fn() over `iters` launches, each bracketed by
+    CUDA events on the current stream with an L2 flush (256 MiB write) before it."""
+    for _ in range(warmup):
+        fn()
+    times = []
+    for _ in range(iters):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    return statistics.median(times)
+
+
+def op_microbench(lib, torch, hbm_pk):
+    """BASELINE configuration 2 through the operator C ABI (include/dav2cuda.h):
+    seeded N(0,1) inputs, the kernels the ABI runs, algorithmic bytes (every
+    tensor read once and written once) over the median event-timed launch."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    out = {}
+
+    def rec(name, ms, nbytes, shape, kernel, extra=None):
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"shape": shape, "kernel": kernel, "ms": round(ms, 4), "bytes": int(nbytes),
+                     "achieved_gbs": round(gbs, 1), "frac_measured": round(gbs / hbm_pk, 3),
+                     "frac_nominal_8tbs": round(gbs / NOMINAL_HBM_GBS, 3), **(extra or {})}
+
+    def check(rc, name):
+        if rc != 0:
+            raise RuntimeError(f"{name}: {lib.dav2cuda_last_error().decode()}")
+
+    # (a) LayerNorm eps 1e-6, f32 [10960, 1024]
+    r, c = 10960, 1024
+    x = torch.randn((r, c), generator=g, device="cuda")
+    w = torch.randn(c, generator=g, device="cuda")
+    b = torch.randn(c, generator=g, device="cuda")
+    y = torch.empty_like(x)
+    ms = _time_kernel(torch, lambda: check(lib.dav2cuda_layer_norm(y.data_ptr(), x.data_ptr(), w.data_ptr(),
+                                                                  b.data_ptr(), r, c, 1e-6, None), "ln"), flush)
+    rec("layer_norm", ms, 2 * r * c * 4, [r, c], "layer_norm_warp_kernel")
+    del x, y
+    # (b) erf-GELU f32 [10960, 4096]
+    n = 10960 * 4096
+    x = torch.randn(n, generator=g, device="cuda")
+    y = torch.empty_like(x)
+    ms = _time_kernel(torch, lambda: check(lib.dav2cuda_gelu(y.data_ptr(), x.data_ptr(), n, None), "gelu"), flush)
+    rec("gelu", ms, 2 * n * 4, [10960, 4096], "gelu_kernel")
+    del x, y
+    # (c) row softmax over [8, 16, 1370, 1370] scores, scaled by 1/8
+    rows, cols = 8 * 16 * 1370, 1370
+    x = torch.randn((rows, cols), generator=g, device="cuda")
+    y = torch.empty_like(x)
+    ms = _time_kernel(torch, lambda: check(lib.dav2cuda_softmax_rows(y.data_ptr(), x.data_ptr(), rows, cols, 0.125,
+                                                                    None), "softmax"), flush)
+    rec("softmax", ms, 2 * rows * cols * 4, [8, 16, 1370, 1370], "softmax_warp_kernel")
+    del x, y
+    # (d) int8 3x3 pad-1 conv [8,256,148,148] (per-row im2col quantize, s8 GEMM,
+    #     dequant) then 2x align-corners upsample -> [8,256,296,296]
+    B, C, H, W, Co = 8, 256, 148, 148, 256
+    x = torch.randn((B, C, H, W), generator=g, device="cuda")
+    wq = torch.randint(-127, 128, (Co, C * 9), generator=g, device="cuda", dtype=torch.int8)
+    sw = torch.rand(Co, generator=g, device="cuda") * 1e-3 + 1e-4
+    bias = torch.randn(Co, generator=g, device="cuda")
+    y = torch.empty((B, Co, 2 * H, 2 * W), device="cuda")
+    wsz = lib.dav2cuda_conv3x3_int8_up2_workspace_size(B, W, H, C, Co)
+    ws = torch.empty(wsz, dtype=torch.uint8, device="cuda")
+    ms = _time_kernel(torch, lambda: check(lib.dav2cuda_conv3x3_int8_up2(
+        y.data_ptr(), x.data_ptr(), wq.data_ptr(), sw.data_ptr(), bias.data_ptr(), B, W, H, C, Co, ws.data_ptr(),
+        wsz, None), "conv3x3_int8_up2"), flush)
+    ops = 2 * B * H * W * Co * C * 9
+    rec("conv3x3_int8_up2", ms, B * C * H * W * 4 + Co * C * 9 + B * Co * 4 * H * W * 4, [B, C, H, W],
+        "im2col quantize + gemm_tc kind::i8 + bilinear_align",
+        {"tops": round(ops / (ms * 1e-3) / 1e12, 1), "int_ops": ops})
+    del x, y, ws
+    torch.cuda.empty_cache()
+    return out
 
 
 def main():
@@ -306,18 +429,12 @@ def main():
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+        # host-side group: barrier + max-over-ranks only; nothing on the data path
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
 
     def barrier():
         if dist is not None:
             dist.barrier()
-
-    def max_over_ranks(v):
-        if dist is None:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
     lib = dav2_b200.load()
     path = model_path(args.encoder, rank, world)
@@ -330,7 +447,7 @@ def main():
         raise RuntimeError(f"dav2_create: {lib.dav2_last_error().decode()}")
 
     B, S = args.batch, args.size
-    host = images(B, S, seed0=rank * B)
+    host = images(shard_seeds(rank, B), S)
     pinned_in = torch.from_numpy(host).pin_memory()
     dev_in = pinned_in.cuda()
     pinned_out = torch.empty((B, S, S), dtype=torch.float32).pin_memory()
@@ -365,6 +482,9 @@ def main():
             for name, (n, ms) in sorted(agg.items(), key=lambda kv: -kv[1][1]):
                 print(f"{name:28s} {n:4d} {ms:9.3f} ms {100 * ms / prof['total_ms']:5.1f}%")
             print("total", prof["total_ms"])
+        lib.dav2_destroy(ctx)
+        if dist is not None:
+            dist.destroy_process_group()
         return
 
     with torch.cuda.stream(stream):
@@ -384,9 +504,11 @@ def main():
             end.record(stream)
             torch.cuda.synchronize()
         barrier()
-        dev_ms = max_over_ranks(start.elapsed_time(end))
+        dev_ms = max_over_ranks(start.elapsed_time(end), dist)
         launches1 = ctypes.c_uint64()
         lib.dav2_get_kernel_launch_count(ctx, ctypes.byref(launches1))
+        if lib.dav2_synchronize(ctx) != 0:
+            raise RuntimeError(f"device path: {lib.dav2_last_error().decode()}")
         # end to end through the host-buffer entry point
         host_step()
         barrier()
@@ -394,17 +516,28 @@ def main():
         t0 = time.perf_counter()
         for _ in range(args.steps):
             host_step()
-        e2e_s = max_over_ranks(time.perf_counter() - t0)
+        e2e_s = max_over_ranks(time.perf_counter() - t0, dist)
         barrier()
     out = pinned_out.numpy()
     assert np.isfinite(out).all()
+    # outside the timed region: the batched device path against one image
+    # through the single-image public entry point
+    single = np.zeros((S, S), np.float32)
+    if lib.dav2_infer_bgr8(ctx, host[0].ctypes.data, S, S, S * 3, S, single.ctypes.data, single.size) != 0:
+        raise RuntimeError(lib.dav2_last_error().decode())
+    dev0 = dev_out[0].cpu().numpy()
+    scale = max(float(np.abs(single).max()), 1e-30)
+    check = {"image0_device_batch_vs_single_max_rel": float(np.abs(dev0 - single).max()) / scale,
+             "image0_host_batch_vs_single_max_rel": float(np.abs(out[0] - single).max()) / scale}
+    if max(check.values()) > 1e-5:
+        print(f"warning: batched and single-image depth differ: {check}", file=sys.stderr)
 
     value = B * world * args.steps / (dev_ms * 1e-3)
     e2e = B * world * args.steps / e2e_s
-    line = None
     if rank == 0:
-        peak = int8_peak_tops(torch) if args.precision == "int8" else None
-        work = op_work(args.encoder, B, S)
+        int8 = args.precision == "int8"
+        peak = int8_peak_tops(torch) if int8 else None
+        work = op_work(args.encoder, B, S, int8)
         agg = {}
         for o in prof["ops"]:
             a = agg.setdefault(o["name"], [0, 0.0])
@@ -412,6 +545,7 @@ def main():
             a[1] += o["ms"]
         shares = {k: round(v[1] / prof["total_ms"], 4) for k, v in sorted(agg.items(), key=lambda kv: -kv[1][1])}
         f16_peak, f16_src = f16_peak_tflops()
+        hbm_pk, hbm_src = hbm_peak_gbs()
         traffic_by_op = {}
         tfile = ROOT / "profiles" / "traffic.txt"
         if tfile.exists():
@@ -421,34 +555,43 @@ def main():
 
         def roofline_of(name):
             per_launch_ms = agg[name][1] / agg[name][0]
-            achieved = work[name] / (per_launch_ms * 1e-3) / 1e12
-            int8 = args.precision == "int8" and name != "attention"
-            pk = peak if int8 else f16_peak
+            ops, nbytes = work[name]
+            achieved = ops / (per_launch_ms * 1e-3) / 1e12
+            i8 = int8 and name != "attention"
+            pk = peak if i8 else f16_peak
+            t_tensor = ops / (pk * 1e12) * 1e3 if pk else 0.0
+            t_hbm = nbytes / (hbm_pk * 1e9) * 1e3
             return {"bound": "tensor",
                     "kernel": f"attention_tc f16 ({name})" if name == "attention" else
-                              f"gemm_tc {'int8' if int8 else 'f16'} ({name})",
+                              f"gemm_tc {'int8' if i8 else 'f16'} ({name})",
                     "achieved": round(achieved, 1), "peak": round(pk, 1) if pk else None, "unit": "TFLOP/s",
                     "frac": round(achieved / pk, 3) if pk else None, "traffic": traffic_by_op.get(name),
                     "peak_source": ("cuBLAS int8 GEMM (torch._int_mm 8192^3, burst) measured in this run; "
-                                    "MEASURED_PEAKS.json has no int8 figure") if int8 else f16_src,
-                    "per_launch_ms": round(per_launch_ms, 4), "launches_per_step": agg[name][0]}
+                                    "MEASURED_PEAKS.json has no int8 figure") if i8 else f16_src,
+                    "per_launch_ms": round(per_launch_ms, 4), "launches_per_step": agg[name][0],
+                    "algorithmic_bytes": int(nbytes),
+                    "ideal_bound": "hbm" if t_hbm > t_tensor else "tensor",
+                    "frac_of_ideal": round(max(t_hbm, t_tensor) / per_launch_ms, 3)}
 
-        hbm_pk, hbm_src = hbm_peak_gbs()
-        mem = op_bytes(args.encoder, B, S, args.precision == "int8")
+        mem = op_bytes(args.encoder, B, S, int8)
         hbm_ops = {}
         for k, nbytes in mem.items():
             if k in agg:
                 gbs = nbytes / (agg[k][1] / agg[k][0] * 1e-3) / 1e9
                 hbm_ops[k] = {"achieved": round(gbs, 1), "peak": hbm_pk, "unit": "GB/s", "frac": round(gbs / hbm_pk, 3),
-                              "bytes_per_launch": int(nbytes)}
+                              "frac_nominal_8tbs": round(gbs / NOMINAL_HBM_GBS, 3), "bytes_per_launch": int(nbytes)}
         known = [k for k in shares if k in work]
         dom = max(known, key=lambda k: agg[k][1])
         roof = roofline_of(dom)
-        roof["ops"] = {k: {kk: v for kk, v in roofline_of(k).items() if kk in ("achieved", "peak", "frac")}
+        roof["ops"] = {k: {kk: v for kk, v in roofline_of(k).items()
+                           if kk in ("achieved", "peak", "frac", "algorithmic_bytes", "ideal_bound", "frac_of_ideal")}
                        for k in known}
         roof["hbm_ops"] = hbm_ops
         roof["hbm_peak_source"] = hbm_src
         roof["op_shares"] = shares
+        micro = None
+        if world == 1 and not args.no_microbench:
+            micro = op_microbench(lib, torch, hbm_pk)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(args.encoder, S)
@@ -456,20 +599,22 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8" if args.precision == "int8" else "f16",
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8" if int8 else "f16",
             "data": "synthetic (random u8 BGR8 images, seeded per image; random-init N(0,0.02) weights)",
             "config": {"workload": f"{args.encoder} {S}x{S} full graph (GPU preprocessing + encoder + DPT head), "
                                    f"{B} images per GPU per step",
                        "encoder": args.encoder, "image": f"{S}x{S}", "batch_per_gpu": B,
-                       "precision": f"{args.precision} (int8 linears/projections/resize layers, f16 attention "
-                                    f"and refinement convolutions, f32/s32 accumulation)" if args.precision == "int8"
-                       else "fp16",
+                       "precision": f"{args.precision} (int8 linears/projections/resize layers with f32 quantizer "
+                                    f"inputs, f16 attention and refinement convolutions, f32/s32 accumulation)"
+                       if int8 else "fp16",
                        "parallelism": f"replicas x{world} (independent images, no collectives)",
                        "l2": "256 MiB buffer written between timed steps (inside the timed region); per-step "
                              "working set ~15 GB"},
             "e2e": {"value": round(e2e, 2), "unit": "images/s", "h2d_bytes_per_step": int(B * S * S * 3),
                     "d2h_bytes_per_step": int(B * S * S * 4)},
+            "check": check,
             "roofline": roof,
+            "op_microbench": micro,
             "cpu_baseline": cpu,
             "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
             "gpu_launches": int(launches1.value - launches0.value),

@@ -257,11 +257,10 @@ template <typename H>
 int launch_attention(H* out, const H* qkv, uint32_t batch, uint32_t tokens, uint32_t heads, uint64_t qkv_ld,
                      uint64_t out_ld, cudaStream_t st) {
     if (tokens == 0 || heads == 0 || batch == 0) return set_error(DAV2CUDA_INVALID_ARGUMENT, "attention: empty");
-    // f16 with the interleaved QKV layout runs on the tcgen05 kernel (attention_tc.cu)
-    if constexpr (std::is_same<H, __half>::value) {
-        if (qkv_ld == 3ull * heads * 64 && out_ld % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0)
-            return launch_attention_tc(out, qkv, batch, tokens, heads, qkv_ld, out_ld, st);
-    }
+    // the interleaved QKV layout runs on the tcgen05 kernel (attention_tc.cu)
+    if (qkv_ld == 3ull * heads * 64 && out_ld % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0)
+        return launch_attention_tc(out, false, qkv, std::is_same<H, __nv_bfloat16>::value, batch, tokens, heads,
+                                   qkv_ld, out_ld, st);
     if ((qkv_ld * sizeof(H)) % 16 || (out_ld * sizeof(H)) % 4 || reinterpret_cast<uintptr_t>(qkv) % 16)
         return set_error(DAV2CUDA_INVALID_ARGUMENT, "attention: misaligned rows");
     dim3 grid((tokens + kBM - 1) / kBM, heads, batch);

@@ -1,5 +1,5 @@
-// Flash attention on tcgen05 tensor cores (head dim 64, f16 operands, f32
-// accumulation) — attention_head64 of the reference (src/operators.cpp:
+// Flash attention on tcgen05 tensor cores (head dim 64, f16 or bf16
+// operands, f32 accumulation; output f16/bf16 or f32) — attention_head64 of the reference (src/operators.cpp:
 // 1098-1209: QK^T*0.125 -> softmax_lastdim.glsl -> PV) without materialising
 // the [heads, T, T] scores.
 //
@@ -58,7 +58,8 @@ struct AttnParams {
     uint32_t full_units;  // units with two live tiles, numbered first
     uint32_t full_per_bh; // two-tile units per (image, head)
     uint64_t out_ld;
-    __half* out;
+    void* out;        // [B*T][out_ld]: the operand type, or f32 when out_f32
+    uint32_t out_f32;
     int* err;
 };
 
@@ -159,6 +160,19 @@ __device__ __forceinline__ Unit unit_at(const AttnParams& p, uint32_t u) {
     return w;
 }
 
+// Two f32 values as a packed f16x2 or bf16x2 word (round to nearest even).
+template <bool kBF16>
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    if constexpr (kBF16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    } else {
+        __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+}
+
+template <bool kBF16>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
     extern __shared__ uint8_t smem[];
@@ -258,8 +272,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // one MMA issuer per tile, so that neither tile's pipeline waits on the other
         const uint32_t t = warp == 1 ? 0u : 1u;
         if (lane == 0) {
-            constexpr uint32_t idesc_s = make_idesc(1u, 0u, 128u, 128u);
-            constexpr uint32_t idesc_o = make_idesc(1u, 0u, 128u, 64u) | (1u << 16);  // B (V) MN-major
+            constexpr uint32_t ab = kBF16 ? 1u : 0u;  // kind::f16 operand format: 0 f16, 1 bf16
+            constexpr uint32_t idesc_s = make_idesc(1u, ab, 128u, 128u);
+            constexpr uint32_t idesc_o = make_idesc(1u, ab, 128u, 64u) | (1u << 16);  // B (V) MN-major
             uint32_t g = 0;   // K/V blocks consumed (all units)
             uint32_t gt = 0;  // blocks this tile has computed (its S/P/O barrier phases)
             uint32_t qn = 0;  // units this tile has computed (its Q buffer phases)
@@ -465,8 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
                         fadd2(ls[2 * v], ls[2 * v + 1], s[8 * q + 2 * v], s[8 * q + 2 * v + 1]);
-                        __half2 hh = __floats2half2_rn(s[8 * q + 2 * v], s[8 * q + 2 * v + 1]);
-                        hv[v] = *reinterpret_cast<uint32_t*>(&hh);
+                        hv[v] = pack_h2<kBF16>(s[8 * q + 2 * v], s[8 * q + 2 * v + 1]);
                     }
                     *reinterpret_cast<uint4*>(atoms + (gtt % kPBufs) * 2u * kTile + (((uint32_t)q ^ (row & 7u)) << 4)) =
                         make_uint4(hv[0], hv[1], hv[2], hv[3]);
@@ -511,19 +525,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t qrow = w.q0 + 128u * t + row;
             if (ok && qrow < p.tokens) {
                 const float wa = f_own * inv, wb = f_oth * inv;
-                __half* dst = p.out + ((uint64_t)w.img * p.tokens + qrow) * p.out_ld + w.head * 64u + half * 32u;
+                const uint64_t at = ((uint64_t)w.img * p.tokens + qrow) * p.out_ld + w.head * 64u + half * 32u;
 #pragma unroll
                 for (int i = 0; i < 32; i += 8) {
-                    uint32_t hv[4];
+                    float x[8];
 #pragma unroll
-                    for (int v = 0; v < 4; ++v) {
-                        const float x0 = __uint_as_float(oa[i + 2 * v]) * wa + __uint_as_float(ob[i + 2 * v]) * wb;
-                        const float x1 =
-                            __uint_as_float(oa[i + 2 * v + 1]) * wa + __uint_as_float(ob[i + 2 * v + 1]) * wb;
-                        __half2 hh = __floats2half2_rn(x0, x1);
-                        hv[v] = *reinterpret_cast<uint32_t*>(&hh);
+                    for (int v = 0; v < 8; ++v)
+                        x[v] = __uint_as_float(oa[i + v]) * wa + __uint_as_float(ob[i + v]) * wb;
+                    if (p.out_f32) {
+                        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + at + i);
+                        dst[0] = make_float4(x[0], x[1], x[2], x[3]);
+                        dst[1] = make_float4(x[4], x[5], x[6], x[7]);
+                    } else {
+                        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + at + i) =
+                            make_uint4(pack_h2<kBF16>(x[0], x[1]), pack_h2<kBF16>(x[2], x[3]),
+                                       pack_h2<kBF16>(x[4], x[5]), pack_h2<kBF16>(x[6], x[7]));
                     }
-                    *reinterpret_cast<uint4*>(dst + i) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
                 }
             }
         }
@@ -556,8 +573,8 @@ std::once_flag g_enc_once;
 
 }  // namespace
 
-int launch_attention_tc(__half* out, const __half* qkv, uint32_t batch, uint32_t tokens, uint32_t heads,
-                        uint64_t qkv_ld, uint64_t out_ld, cudaStream_t st) {
+int launch_attention_tc(void* out, bool out_f32, const void* qkv, bool bf16, uint32_t batch, uint32_t tokens,
+                        uint32_t heads, uint64_t qkv_ld, uint64_t out_ld, cudaStream_t st) {
     if (!tokens || !heads || !batch) return set_error(DAV2CUDA_INVALID_ARGUMENT, "attention: empty");
     if (qkv_ld != 3ull * heads * 64 || (qkv_ld * 2) % 16 || reinterpret_cast<uintptr_t>(qkv) % 16 || out_ld % 8 ||
         reinterpret_cast<uintptr_t>(out) % 16)
@@ -575,20 +592,21 @@ int launch_attention_tc(__half* out, const __half* qkv, uint32_t batch, uint32_t
     const cuuint64_t strides[2] = {qkv_ld * 2, (cuuint64_t)tokens * qkv_ld * 2};
     const cuuint32_t box[3] = {64, 128, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
-    const CUresult rc = g_enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(qkv), dims, strides, box,
-                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult rc = g_enc(&tm, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                              const_cast<void*>(qkv), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (rc != CUDA_SUCCESS) return set_error(DAV2CUDA_INVALID_ARGUMENT, "attention: tensor map encoding failed");
-    static uint64_t configured = 0;
+    auto kernel = bf16 ? attention_tc_kernel<true> : attention_tc_kernel<false>;
+    static std::atomic<uint64_t> configured[2];  // one bit per device ordinal, per operand type
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!(configured >> (dev & 63) & 1ull)) {
-        if (cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem) !=
-                cudaSuccess ||
-            cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+    if (!configured_on(configured[bf16], dev)) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem) != cudaSuccess ||
+            cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return set_error(DAV2CUDA_LAUNCH_FAILED, "attention: cannot set shared memory size");
-        configured |= 1ull << (dev & 63);
+        mark_configured(configured[bf16], dev);
     }
     AttnParams p;
     p.tokens = tokens;
@@ -603,15 +621,15 @@ int launch_attention_tc(__half* out, const __half* qkv, uint32_t batch, uint32_t
     p.full_units = (uint32_t)(bh * p.full_per_bh);
     p.out_ld = out_ld;
     p.out = out;
+    p.out_f32 = out_f32 ? 1u : 0u;
     p.err = device_error_word();
     if (!p.err) return set_error(DAV2CUDA_INTERNAL_ERROR, "attention: no device error word");
-    static int sms[64] = {0};
-    if (!sms[dev & 63] && cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-        return set_error(DAV2CUDA_LAUNCH_FAILED, "attention: cannot query the SM count");
+    const int sms = sm_count(dev);
+    if (sms <= 0) return set_error(DAV2CUDA_LAUNCH_FAILED, "attention: cannot query the SM count");
     // persistent: one CTA per SM (the TMEM allocation keeps it at one), each
     // walking units blockIdx.x + k * gridDim.x
-    const uint32_t grid = p.units < (uint32_t)sms[dev & 63] ? p.units : (uint32_t)sms[dev & 63];
-    attention_tc_kernel<<<grid, kThreads, kSmem, st>>>(tm, p);
+    const uint32_t grid = p.units < (uint32_t)sms ? p.units : (uint32_t)sms;
+    kernel<<<grid, kThreads, kSmem, st>>>(tm, p);
     return check_launch("attention_tc");
 }
 

@@ -76,10 +76,11 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity
 }
 
 // Waits for the phase with the given parity to complete. Gives up after
-// kWaitTimeoutNs, or as soon as *abort is set by another role of the CTA;
-// on a timeout it records error 1 and sets *abort. Returns false when the
-// wait did not complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+// limit_ns, or as soon as *abort is set by another role of the CTA; on a
+// timeout it records error 1 and sets *abort. Returns false when the wait
+// did not complete.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
+                                              unsigned long long limit_ns) {
     const uint32_t a = smem_addr(bar);
     if (mbar_try_wait(a, parity)) return true;
     const unsigned long long start = globaltimer();
@@ -87,13 +88,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         if (mbar_try_wait_hint(a, parity, 20000u)) return true;
         if ((spin & 15u) == 0) {
             if (*abort) return false;
-            if (globaltimer() - start > kWaitTimeoutNs) {
+            if (globaltimer() - start > limit_ns) {
                 *abort = 1;
                 atomicExch(err, 1);
                 return false;
             }
         }
     }
+}
+
+// The pipelines' wait: limit kWaitTimeoutNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+    return mbar_wait_for(bar, parity, abort, err, kWaitTimeoutNs);
 }
 
 // ----------------------------------------------------------------------- TMA

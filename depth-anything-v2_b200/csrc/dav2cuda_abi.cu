@@ -15,18 +15,32 @@ namespace {
 thread_local std::string t_last_error;
 std::atomic<uint64_t> g_launches{0};
 __device__ int g_device_error = 0;
-int* g_error_word[64] = {};
+std::atomic<int*> g_error_word[64];
 }  // namespace
 
+// Device address of the error word on the current device, resolved once per
+// device with cudaGetSymbolAddress (a cudaDeviceReset invalidates it, as it
+// invalidates every device allocation this library and its contexts hold).
 int* device_error_word() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    if (!g_error_word[dev]) {
+    int* cached = g_error_word[dev].load(std::memory_order_acquire);
+    if (!cached) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
-        g_error_word[dev] = static_cast<int*>(p);
+        cached = static_cast<int*>(p);
+        g_error_word[dev].store(cached, std::memory_order_release);
     }
-    return g_error_word[dev];
+    return cached;
+}
+
+int sm_count(int dev) {
+    static std::atomic<int> cache[64];
+    if (dev < 0 || dev >= 64) return 0;
+    int n = cache[dev].load(std::memory_order_relaxed);
+    if (n == 0 && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+        cache[dev].store(n, std::memory_order_relaxed);
+    return n > 0 ? n : 0;
 }
 
 int set_error(int status, const char* message) {
@@ -62,6 +76,23 @@ __global__ void f16_to_f32_kernel(float* __restrict__ out, const __half* __restr
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
         out[i] = __half2float(in[i]);
+}
+
+// One 32-thread block: thread 0 waits on an mbarrier phase that completes
+// only when `arrive` is set, through the pipelines' bounded wait.
+__global__ void wait_probe_kernel(unsigned long long limit_ns, uint32_t arrive, int* err) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (arrive) mbar_arrive(&bar);
+        mbar_wait_for(&bar, 0, &abort_flag, err, limit_ns);
+    }
 }
 
 int pad_byte_rows(uint8_t* out, const void* in, uint64_t rows, uint32_t in_bytes, uint32_t out_bytes,
@@ -120,6 +151,14 @@ int dav2cuda_device_error(void) {
     if (cudaMemcpyFromSymbol(&value, g_device_error, sizeof(int)) != cudaSuccess) return -1;
     cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
     return value;
+}
+
+int dav2cuda_wait_probe(uint64_t limit_ns, uint32_t arrive, void* stream) {
+    REQUIRE(limit_ns > 0 && limit_ns <= 1000000000ull, "wait probe: limit must be in (0, 1 s]");
+    int* err = device_error_word();
+    if (!err) return set_error(DAV2CUDA_INTERNAL_ERROR, "wait probe: no device error word");
+    wait_probe_kernel<<<1, 32, 0, as_stream(stream)>>>(limit_ns, arrive, err);
+    return check_launch("wait_probe");
 }
 
 uint64_t dav2cuda_launch_count(int reset) {
@@ -232,6 +271,21 @@ int dav2cuda_quantize_rows_s8(uint32_t* packed, float* scales, const float* inpu
                                        (uint64_t)rows * columns, columns, columns / 4, as_stream(stream));
 }
 
+int dav2cuda_pack_weight_s8(uint8_t* codes, float* scales, const float* weight, uint32_t layout, uint32_t rows,
+                            uint32_t columns, uint32_t padded_columns, uint32_t output_channels, uint32_t kernel,
+                            uint32_t input_channels, void* stream) {
+    REQUIRE(rows && columns && padded_columns >= columns && layout <= 2, "invalid weight packing dimensions");
+    REQUIRE(layout != 1 || (output_channels && kernel && input_channels == columns &&
+                            rows == kernel * kernel * output_channels),
+            "weight packing: conv-transpose shape mismatch");
+    REQUIRE(layout != 2 || (output_channels == rows && kernel && input_channels &&
+                            columns == kernel * kernel * input_channels),
+            "weight packing: convolution shape mismatch");
+    REQUIRE(!null_any(codes, scales, weight), "weight packing: null buffer");
+    return launch_pack_weight_s8(codes, scales, weight, (int)layout, rows, columns, padded_columns, output_channels,
+                                 kernel, input_channels, as_stream(stream));
+}
+
 int dav2cuda_im2col_quantize_s8(uint32_t* packed, float* scales, const float* input, uint32_t iw, uint32_t ih,
                                 uint32_t ic, uint32_t ow, uint32_t oh, uint32_t kernel, uint32_t stride,
                                 int32_t padding, void* stream) {
@@ -280,7 +334,7 @@ int dav2cuda_linear_s8_packed(float* output, const uint32_t* packed_input, const
 }
 
 uint64_t dav2cuda_linear_int8_workspace_size(uint32_t rows, uint32_t input_columns, uint32_t output_columns) {
-    const uint32_t kp = round_up(input_columns, 16);
+    const uint64_t kp = ((uint64_t)input_columns + 15) / 16 * 16;  // 64-bit: no wrap near UINT32_MAX
     return align256((uint64_t)rows * kp) + align256((uint64_t)rows * 4) +
            (kp != input_columns ? align256((uint64_t)output_columns * kp) : 0) + 256;
 }
@@ -289,6 +343,7 @@ int dav2cuda_linear_int8(float* output, const float* input, const uint32_t* int8
                          const float* bias, uint32_t rows, uint32_t input_columns, uint32_t output_columns,
                          uint32_t gelu, void* workspace, uint64_t workspace_bytes, void* stream) {
     REQUIRE(rows && input_columns && output_columns && input_columns % 4 == 0, "invalid INT8 linear dimensions");
+    REQUIRE(input_columns <= 0xFFFFFFF0u, "INT8 linear: input_columns too large");
     REQUIRE(!null_any(output, input, int8_weight, weight_scales, bias, workspace), "INT8 linear: null buffer");
     REQUIRE(workspace_bytes >= dav2cuda_linear_int8_workspace_size(rows, input_columns, output_columns),
             "INT8 linear: workspace is too small");

@@ -19,6 +19,8 @@ template <>
 __device__ __forceinline__ float tof<__half>(__half v) { return __half2float(v); }
 template <>
 __device__ __forceinline__ float tof<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float tof<float>(float v) { return v; }
 
 unsigned gcap(uint64_t n) {
     const uint64_t g = (n + 255) / 256;
@@ -197,9 +199,26 @@ __global__ void __launch_bounds__(256) im2col_quantize_nhwc_kernel(uint8_t* __re
         out[r * kp + col] = col < cols ? (uint8_t)q8(__fmul_rn(value(col), inv)) : 0;
 }
 
+// Eight consecutive channels as floats: one 16-byte load for half maps, two
+// for f32 maps.
+template <typename H>
+__device__ __forceinline__ void load8(const H* p, float (&f)[8]) {
+    const uint4 q = *reinterpret_cast<const uint4*>(p);
+    const H* hv = reinterpret_cast<const H*>(&q);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = tof(hv[j]);
+}
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&f)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *(reinterpret_cast<const float4*>(p) + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
 // Vectorised form of the same for 8-aligned channels: each thread holds up to
-// VEC 16-byte groups of 8 channels of one tap in registers, so the row is
-// gathered once; codes and padding as above.
+// VEC groups of 8 channels of one tap in registers, so the row is gathered
+// once; codes and padding as above.
 template <typename H, int VEC>
 __global__ void __launch_bounds__(256) im2col_quantize_nhwc_vec_kernel(uint8_t* __restrict__ out,
                                                                        float* __restrict__ scales,
@@ -213,20 +232,19 @@ __global__ void __launch_bounds__(256) im2col_quantize_nhwc_vec_kernel(uint8_t* 
     const uint32_t pp = (uint32_t)(r % ((uint64_t)oh * ow));
     const uint32_t oy = pp / ow, ox = pp % ow;
     const uint32_t cg = c / 8, groups = k * k * cg;
-    uint4 v[VEC];
+    float v[VEC][8];
     float m = 0.f;
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
         const uint32_t g = threadIdx.x + 256u * i;
-        v[i] = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
         if (g < groups) {
             const uint32_t tap = g / cg, ch = (g % cg) * 8;
             const int iy = (int)(oy * s + tap / k) - (int)pad, ix = (int)(ox * s + tap % k) - (int)pad;
-            if (iy >= 0 && ix >= 0 && iy < (int)h && ix < (int)w)
-                v[i] = *reinterpret_cast<const uint4*>(in + ((b * h + iy) * w + ix) * ldc + ch);
-            const H* hv = reinterpret_cast<const H*>(&v[i]);
+            if (iy >= 0 && ix >= 0 && iy < (int)h && ix < (int)w) load8(in + ((b * h + iy) * w + ix) * ldc + ch, v[i]);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(tof(hv[j])));
+            for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[i][j]));
         }
     }
     m = warp_max(m);
@@ -242,10 +260,9 @@ __global__ void __launch_bounds__(256) im2col_quantize_nhwc_vec_kernel(uint8_t* 
     for (int i = 0; i < VEC; ++i) {
         const uint32_t g = threadIdx.x + 256u * i;
         if (g < groups) {
-            const H* hv = reinterpret_cast<const H*>(&v[i]);
             uint32_t q[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) q[j] = q8(__fmul_rn(tof(hv[j]), inv));
+            for (int j = 0; j < 8; ++j) q[j] = q8(__fmul_rn(v[i][j], inv));
             *reinterpret_cast<uint2*>(out + r * kp + 8ull * g) =
                 make_uint2(q[0] | (q[1] << 8) | (q[2] << 16) | (q[3] << 24), q[4] | (q[5] << 8) | (q[6] << 16) | (q[7] << 24));
         }
@@ -318,7 +335,14 @@ __global__ void expand_bias_kernel(float* __restrict__ out, const float* __restr
     if (i < co * reps) out[i] = bias[i % co];
 }
 
+__global__ void store_pointer_kernel(void** slot, void* value) { *slot = value; }
+
 }  // namespace
+
+int launch_store_pointer(void** slot, void* value, cudaStream_t st) {
+    store_pointer_kernel<<<1, 1, 0, st>>>(slot, value);
+    return check_launch("store_pointer");
+}
 
 template <typename H>
 int launch_patch_im2col(H* out, const float* img, uint32_t batch, uint32_t h, uint32_t w, uint32_t kp,
@@ -417,5 +441,8 @@ int launch_expand_bias(float* out, const float* bias, uint32_t co, uint32_t reps
 DAV2_INST(__half)
 DAV2_INST(__nv_bfloat16)
 #undef DAV2_INST
+template int launch_im2col_quantize_nhwc<float>(uint8_t*, float*, const float*, uint32_t, uint32_t, uint32_t,
+                                                uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t,
+                                                uint32_t, uint32_t, cudaStream_t);
 
 }  // namespace dav2cuda

@@ -557,30 +557,48 @@ __global__ void __launch_bounds__(128) quantize_rows_kernel(uint32_t* __restrict
     }
 }
 
-// Register-resident form of the same quantizer for half rows whose width
-// is a multiple of 1024: each of the 128 threads holds VEC x 8 values
-// (16-byte loads), so the row is read from HBM once and written once.
-template <int VEC>
-__global__ void __launch_bounds__(128) quantize_rows_half_vec_kernel(uint32_t* __restrict__ packed,
-                                                                     float* __restrict__ scales,
-                                                                     const __half* __restrict__ in, uint32_t cols,
-                                                                     uint32_t row_stride, uint32_t out_words) {
+// Eight consecutive row elements (one 16-byte load for half rows, two for
+// f32 rows) as floats; streaming loads (each row is read once).
+template <typename T>
+__device__ __forceinline__ void load8_cs(const T* p, float (&f)[8]);
+template <>
+__device__ __forceinline__ void load8_cs<__half>(const __half* p, float (&f)[8]) {
+    const uint4 q = __ldcs(reinterpret_cast<const uint4*>(p));
+    const __half2* h = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float2 t = __half22float2(h[j]);
+        f[2 * j] = t.x;
+        f[2 * j + 1] = t.y;
+    }
+}
+template <>
+__device__ __forceinline__ void load8_cs<float>(const float* p, float (&f)[8]) {
+    const float4 a = __ldcs(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldcs(reinterpret_cast<const float4*>(p) + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+// Register-resident form of the same quantizer for f16 or f32 rows whose
+// width is a multiple of 1024: each of the 128 threads holds VEC groups of 8
+// values (16- or 32-byte loads), so the row is read from HBM once and its
+// codes written once.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(128) quantize_rows_vec_kernel(uint32_t* __restrict__ packed,
+                                                                float* __restrict__ scales,
+                                                                const T* __restrict__ in, uint32_t cols,
+                                                                uint32_t row_stride, uint32_t out_words) {
     __shared__ float red[4];
     const uint64_t row = blockIdx.x;
-    const uint4* x = reinterpret_cast<const uint4*>(in + row * (uint64_t)row_stride);
+    const T* x = in + row * (uint64_t)row_stride;
     float v[VEC][8];
     float m = 0.f;
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
-        const uint4 q = __ldcs(x + threadIdx.x + 128 * i);
-        const __half2* h = reinterpret_cast<const __half2*>(&q);
+        load8_cs<T>(x + 8u * (threadIdx.x + 128u * i), v[i]);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float2 f = __half22float2(h[j]);
-            v[i][2 * j] = f.x;
-            v[i][2 * j + 1] = f.y;
-            m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
-        }
+        for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[i][j]));
     }
     m = block_max_128(m, red);
     const float scale = fmaxf(m / 127.0f, 1.0e-8f);
@@ -596,31 +614,25 @@ __global__ void __launch_bounds__(128) quantize_rows_half_vec_kernel(uint32_t* _
     }
 }
 
-// Warp-per-row form for half rows of 256*VPL columns (VPL <= 8): each lane
-// holds VPL 16-byte groups, the row maximum is a shuffle reduction, and a
-// 128-thread block quantizes four rows (no block barrier).
-template <int VPL>
-__global__ void __launch_bounds__(128) quantize_rows_half_warp_kernel(uint32_t* __restrict__ packed,
-                                                                      float* __restrict__ scales,
-                                                                      const __half* __restrict__ in, uint64_t rows,
-                                                                      uint32_t row_stride, uint32_t out_words) {
+// Warp-per-row form for f16 / f32 rows of 256*VPL columns (VPL <= 8): each
+// lane holds VPL groups of 8 values, the row maximum is a shuffle reduction,
+// and a 128-thread block quantizes four rows (no block barrier).
+template <typename T, int VPL>
+__global__ void __launch_bounds__(128) quantize_rows_warp_kernel(uint32_t* __restrict__ packed,
+                                                                 float* __restrict__ scales,
+                                                                 const T* __restrict__ in, uint64_t rows,
+                                                                 uint32_t row_stride, uint32_t out_words) {
     const uint64_t row = (uint64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
     const uint32_t lane = threadIdx.x & 31;
     if (row >= rows) return;
-    const uint4* x = reinterpret_cast<const uint4*>(in + row * (uint64_t)row_stride);
+    const T* x = in + row * (uint64_t)row_stride;
     float v[VPL][8];
     float m = 0.f;
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
-        const uint4 q = __ldcs(x + lane + 32 * i);
-        const __half2* h = reinterpret_cast<const __half2*>(&q);
+        load8_cs<T>(x + 8u * (lane + 32u * i), v[i]);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float2 f = __half22float2(h[j]);
-            v[i][2 * j] = f.x;
-            v[i][2 * j + 1] = f.y;
-            m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
-        }
+        for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[i][j]));
     }
     m = warp_max(m);
     const float scale = fmaxf(m / 127.0f, 1.0e-8f);
@@ -813,35 +825,36 @@ int launch_quantize_rows(uint32_t* packed, float* scales, const T* in, uint64_t 
                          uint64_t offset, uint32_t group, uint64_t group_stride, uint32_t row_stride,
                          uint32_t out_words, cudaStream_t st) {
     if (rows == 0) return DAV2CUDA_OK;
-    if constexpr (std::is_same<T, __half>::value) {
+    if constexpr (std::is_same<T, __half>::value || std::is_same<T, float>::value) {
+        constexpr uint32_t kAlign = 8;  // 8-element groups start on 16-byte boundaries
         const bool plain = offset == 0 && (group == rows || group_stride == (uint64_t)group * row_stride);
-        const bool aligned = (reinterpret_cast<uintptr_t>(in) % 16 == 0) && (row_stride % 8 == 0) &&
+        const bool aligned = (reinterpret_cast<uintptr_t>(in) % 16 == 0) && (row_stride % kAlign == 0) &&
                              (reinterpret_cast<uintptr_t>(packed) % 8 == 0) && out_words == cols / 4;
         if (plain && aligned && cols % 256 == 0 && cols <= 2048) {
             const unsigned grid = (unsigned)((rows + 3) / 4);
+#define DAV2_QWARP(V)                                                                                        \
+    case V:                                                                                                  \
+        quantize_rows_warp_kernel<T, V><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); \
+        break;
             switch (cols / 256) {
-                case 1: quantize_rows_half_warp_kernel<1><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
-                case 2: quantize_rows_half_warp_kernel<2><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
-                case 3: quantize_rows_half_warp_kernel<3><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
-                case 4: quantize_rows_half_warp_kernel<4><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
-                case 5: quantize_rows_half_warp_kernel<5><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
-                case 6: quantize_rows_half_warp_kernel<6><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
-                case 7: quantize_rows_half_warp_kernel<7><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
-                default: quantize_rows_half_warp_kernel<8><<<grid, 128, 0, st>>>(packed, scales, in, rows, row_stride, out_words); break;
+                DAV2_QWARP(1) DAV2_QWARP(2) DAV2_QWARP(3) DAV2_QWARP(4) DAV2_QWARP(5) DAV2_QWARP(6) DAV2_QWARP(7)
+                default: DAV2_QWARP(8)
             }
-            return check_launch("quantize_rows_half_warp");
+#undef DAV2_QWARP
+            return check_launch("quantize_rows_warp");
         }
         if (plain && aligned && cols % 1024 == 0 && cols <= 8192) {
+#define DAV2_QVEC(V)                                                                                          \
+    case V:                                                                                                   \
+        quantize_rows_vec_kernel<T, V><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, row_stride,  \
+                                                                       out_words);                            \
+        break;
             switch (cols / 1024) {
-                case 1: quantize_rows_half_vec_kernel<1><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, row_stride, out_words); break;
-                case 2: quantize_rows_half_vec_kernel<2><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, row_stride, out_words); break;
-                case 3: quantize_rows_half_vec_kernel<3><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, row_stride, out_words); break;
-                case 4: quantize_rows_half_vec_kernel<4><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, row_stride, out_words); break;
-                case 6: quantize_rows_half_vec_kernel<6><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, row_stride, out_words); break;
-                case 8: quantize_rows_half_vec_kernel<8><<<(unsigned)rows, 128, 0, st>>>(packed, scales, in, cols, row_stride, out_words); break;
+                DAV2_QVEC(1) DAV2_QVEC(2) DAV2_QVEC(3) DAV2_QVEC(4) DAV2_QVEC(6) DAV2_QVEC(8)
                 default: goto generic;
             }
-            return check_launch("quantize_rows_half_vec");
+#undef DAV2_QVEC
+            return check_launch("quantize_rows_vec");
         }
     }
 generic:

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "dav2cuda.h"
 
 namespace dav2cuda {
@@ -15,6 +17,19 @@ int set_error(int status, const char* message);
 int check_launch(const char* what);
 int* device_error_word();
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Per-device one-time kernel set-up (cudaFuncSetAttribute): one bit per
+// device ordinal, set atomically once the attributes are applied. Threads
+// driving different devices (or the same one) may both apply them, which is
+// idempotent; none can skip them.
+inline bool configured_on(const std::atomic<uint64_t>& mask, int dev) {
+    return (mask.load(std::memory_order_acquire) >> (dev & 63)) & 1ull;
+}
+inline void mark_configured(std::atomic<uint64_t>& mask, int dev) {
+    mask.fetch_or(1ull << (dev & 63), std::memory_order_release);
+}
+// Multiprocessor count of a device (cached per ordinal; 0 when the query fails).
+int sm_count(int dev);
 
 
 // ------------------------------------------------------------ memory-bound
@@ -71,6 +86,10 @@ int launch_conv_weight_to_half(H* out, const float* w, uint32_t co, uint32_t ci,
                                cudaStream_t st);
 
 // ------------------------------------------------------------ graph pieces
+// Stream-ordered store of one device pointer into a device-side slot (the
+// graph's final convolution reads its destination from such a slot, so a
+// captured graph can write straight into each call's output buffer).
+int launch_store_pointer(void** slot, void* value, cudaStream_t st);
 template <typename H>
 int launch_patch_im2col(H* out, const float* img, uint32_t batch, uint32_t h, uint32_t w, uint32_t kp,
                         cudaStream_t st);
@@ -95,8 +114,11 @@ int launch_half_weight(H* out, const float* w, int kind, uint64_t rows, uint32_t
 int launch_expand_bias(float* out, const float* bias, uint32_t co, uint32_t reps, cudaStream_t st);
 
 // ------------------------------------------------------------- attention
-int launch_attention_tc(__half* out, const __half* qkv, uint32_t batch, uint32_t tokens, uint32_t heads,
-                        uint64_t qkv_ld, uint64_t out_ld, cudaStream_t st);
+// tcgen05 flash attention over interleaved qkv [B*T][3*heads*64] of f16 (or
+// bf16 when bf16) values; out [B*T][out_ld] of the same type, or f32 when
+// out_f32.
+int launch_attention_tc(void* out, bool out_f32, const void* qkv, bool bf16, uint32_t batch, uint32_t tokens,
+                        uint32_t heads, uint64_t qkv_ld, uint64_t out_ld, cudaStream_t st);
 template <typename H>
 int launch_attention(H* out, const H* qkv, uint32_t batch, uint32_t tokens, uint32_t heads, uint64_t qkv_ld,
                      uint64_t out_ld, cudaStream_t st);
@@ -150,6 +172,7 @@ struct GemmArgs {
     const void* res1 = nullptr;     // residual tensors: same layout and type as out
     const void* res2 = nullptr;
     const float* head_w = nullptr;  // kEpiHeadDot
+    float* const* out_slot = nullptr;  // kOutHeadF32: destination read from this device slot when set
     float head_b = 0.f;
     float head_max_depth = 0.f;
     // row remap: out_row = (r / rows_per_img) * out_rows_per_img + row_offset + r % rows_per_img

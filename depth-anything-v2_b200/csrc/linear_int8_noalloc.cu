@@ -15,7 +15,9 @@
 //    DAV2CUDA_INVALID_ARGUMENT before anything is launched;
 //  - the first call on a device resolves the array's device address with
 //    cudaGetSymbolAddress while that device is current; make that first call
-//    before any stream capture;
+//    before any stream capture. The address is kept for the life of the
+//    process: after a cudaDeviceReset (which also frees every buffer the
+//    caller passes in) the process must not call this entry point again;
 //  - every call on a device shares the one array: calls that overlap on the
 //    GPU (different streams, no ordering between them) race on it;
 //  - each call overwrites every scratch byte it later reads, so the contents
@@ -62,7 +64,8 @@ extern "C" DAV2CUDA_API int dav2cuda_linear_int8_noalloc(float* output, const fl
                                             const float* weight_scales, const float* bias, uint32_t rows,
                                             uint32_t input_columns, uint32_t output_columns, uint32_t gelu,
                                             void* stream) {
-    if (rows == 0 || input_columns == 0 || output_columns == 0 || input_columns % 4 != 0)
+    if (rows == 0 || input_columns == 0 || output_columns == 0 || input_columns % 4 != 0 ||
+        input_columns > 0xFFFFFFF0u)
         return dav2cuda::set_error(DAV2CUDA_INVALID_ARGUMENT, "invalid INT8 linear dimensions");
     const uint64_t need = dav2cuda_linear_int8_workspace_size(rows, input_columns, output_columns);
     if (need > kNoAllocScratchBytes)

@@ -32,6 +32,7 @@
 #include "image.h"
 #include "launch.h"
 #include "model_file.h"
+#include "status_error.h"
 
 namespace dav2 {
 namespace {
@@ -130,12 +131,15 @@ public:
     CudaExecutor(const std::string& path, dav2_encoder encoder, int device, uint32_t flags)
         : model_(path, encoder), encoder_(encoder), device_(device), arch_(arch_for(encoder)) {
         int count = 0;
-        if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0)
-            throw std::runtime_error("no CUDA device is available");
+        if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0) throw_no_device("no CUDA device is available");
         if (device < 0 || device >= count) throw std::invalid_argument("CUDA device index out of range");
         int8_ = (flags & DAV2_CREATE_FORCE_INT8) != 0;
         cuda_check(cudaSetDevice(device_), "cudaSetDevice");
         cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+        cuda_check(cudaEventCreateWithFlags(&done_, cudaEventDisableTiming), "cudaEventCreate");
+        cuda_check(cudaEventCreateWithFlags(&err_event_, cudaEventDisableTiming), "cudaEventCreate");
+        cuda_check(cudaMallocHost(&err_host_, sizeof(int)), "cudaMallocHost");
+        *err_host_ = 0;
         model_.verify_crc();
         load_weights();
     }
@@ -148,6 +152,9 @@ public:
         if (staging_) cudaFree(staging_);
         if (host_in_) cudaFreeHost(host_in_);
         if (host_out_) cudaFreeHost(host_out_);
+        if (err_host_) cudaFreeHost(err_host_);
+        if (done_) cudaEventDestroy(done_);
+        if (err_event_) cudaEventDestroy(err_event_);
         if (stream_) cudaStreamDestroy(stream_);
     }
 
@@ -177,8 +184,10 @@ public:
         const ImageShape s = network_shape(w, h, input_size);
         std::lock_guard<std::mutex> lock(mutex_);
         cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+        poll_device_error();
         Plan& p = plan(batch, s.width, s.height);
         cudaStream_t st = user_stream ? static_cast<cudaStream_t>(user_stream) : stream_;
+        order_after_previous_call(st);
         const uint64_t img_bytes = uint64_t(image_stride > 0 ? image_stride : row_stride * h);
         const uint64_t in_bytes = img_bytes * (batch - 1) + uint64_t(row_stride) * (h - 1) + uint64_t(w) * 3;
         const uint8_t* dbgr = bgr;
@@ -196,40 +205,98 @@ public:
             upload_bytes_ += in_bytes;
             dbgr = staging_;
         }
+        const bool resize = w != s.width || h != s.height;
+        // The graph's last convolution writes where the plan's slot points:
+        // straight into the caller's device buffer when no resize follows.
+        float* graph_out = device_memory && !resize ? depth : p.depth;
+        op(launch_store_pointer(reinterpret_cast<void**>(p.depth_slot), graph_out, st), "store_pointer");
         op(launch_preprocess_bgr8(p.image, dbgr, batch, w, h, row_stride, img_bytes, s.width, s.height, 0, st),
            "preprocess_bgr8");
-        ++launches_;
+        launches_ += 2;
         launch_plan(p, st);
-        float* result = p.depth;
-        if (w != s.width || h != s.height) {
-            float* resized = resized_buffer(uint64_t(batch) * w * h);
-            op(launch_bilinear_align<float, float>(resized, p.depth, s.width, s.height, w, h, batch, st),
+        float* result = graph_out;
+        if (resize) {
+            float* target = device_memory ? depth : resized_buffer(uint64_t(batch) * w * h);
+            op(launch_bilinear_align<float, float>(target, p.depth, s.width, s.height, w, h, batch, st),
                "resize depth");
             ++launches_;
-            result = resized;
+            result = target;
         }
         const uint64_t out_bytes = uint64_t(batch) * w * h * 4;
-        if (device_memory) {
-            cuda_check(cudaMemcpyAsync(depth, result, out_bytes, cudaMemcpyDeviceToDevice, st), "D2D");
-            if (!user_stream) cuda_check(cudaStreamSynchronize(st), "sync");
-        } else {
+        if (!device_memory) {
             cuda_check(cudaMemcpyAsync(pinned_out ? static_cast<void*>(depth) : host_out_, result, out_bytes,
                                        cudaMemcpyDeviceToHost, st),
                        "D2H");
-            cuda_check(cudaStreamSynchronize(st), "sync");
-            if (!pinned_out) std::memcpy(depth, host_out_, out_bytes);
             download_bytes_ += out_bytes;
         }
-        check_device_error();
+        queue_error_read(st);
+        finish_call(st);
+        if (device_memory && user_stream) return;  // asynchronous: checked at the next call or dav2_synchronize
+        cuda_check(cudaStreamSynchronize(st), "sync");
+        if (!device_memory && !pinned_out) std::memcpy(depth, host_out_, out_bytes);
+        raise_device_error();
+    }
+
+    void probe_block(int batch, int w, int h, int block, const float* x_in, float* x_out, int8_t* codes,
+                     float* scales) override {
+        if (!x_in || !x_out || batch <= 0) throw std::invalid_argument("null probe argument");
+        if (block < 0 || block >= int(arch_.blocks)) throw std::invalid_argument("block index out of range");
+        if ((codes || scales) && !int8_)
+            throw std::invalid_argument("LayerNorm codes exist only at int8 precision");
+        std::lock_guard<std::mutex> lock(mutex_);
+        cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+        poll_device_error();
+        Plan& p = plan(batch, w, h);
+        order_after_previous_call(stream_);
+        const uint64_t rows = uint64_t(batch) * p.T, D = arch_.d;
+        cuda_check(cudaMemcpyAsync(p.x, x_in, rows * D * 4, cudaMemcpyHostToDevice, stream_), "H2D");
+        if (codes || scales) {
+            enqueue_ln1(p, uint32_t(block), stream_);
+            if (codes) cuda_check(cudaMemcpyAsync(codes, p.xn, rows * D, cudaMemcpyDeviceToHost, stream_), "D2H");
+            if (scales) cuda_check(cudaMemcpyAsync(scales, p.xn_s, rows * 4, cudaMemcpyDeviceToHost, stream_), "D2H");
+        }
+        enqueue_block(p, uint32_t(block), stream_);
+        cuda_check(cudaMemcpyAsync(x_out, p.x, rows * D * 4, cudaMemcpyDeviceToHost, stream_), "D2H");
+        queue_error_read(stream_);
+        finish_call(stream_);
+        cuda_check(cudaStreamSynchronize(stream_), "sync");
+        raise_device_error();
+    }
+
+    void probe_head(int batch, int w, int h, const float* tap_x, float* depth) override {
+        if (!tap_x || !depth || batch <= 0) throw std::invalid_argument("null probe argument");
+        std::lock_guard<std::mutex> lock(mutex_);
+        cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+        poll_device_error();
+        Plan& p = plan(batch, w, h);
+        order_after_previous_call(stream_);
+        const uint64_t rows = uint64_t(batch) * p.T, D = arch_.d;
+        for (int k = 0; k < 4; ++k) {
+            cuda_check(cudaMemcpyAsync(p.x, tap_x + k * rows * D, rows * D * 4, cudaMemcpyHostToDevice, stream_),
+                       "H2D");
+            enqueue_tap(p, k, stream_);
+        }
+        op(launch_store_pointer(reinterpret_cast<void**>(p.depth_slot), p.depth, stream_), "store_pointer");
+        enqueue_head(p, stream_);
+        cuda_check(cudaMemcpyAsync(depth, p.depth, uint64_t(batch) * w * h * 4, cudaMemcpyDeviceToHost, stream_),
+                   "D2H");
+        queue_error_read(stream_);
+        finish_call(stream_);
+        cuda_check(cudaStreamSynchronize(stream_), "sync");
+        raise_device_error();
     }
 
     uint64_t kernel_launches() const override { return launches_; }
     std::string profile_json(int batch, int w, int h) override { return profile(batch, w, h); }
 
     void synchronize() override {
+        std::lock_guard<std::mutex> lock(mutex_);
         cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+        // everything queued by this context, on any stream, precedes done_
+        cuda_check(cudaStreamWaitEvent(stream_, done_, 0), "wait");
+        queue_error_read(stream_);
         cuda_check(cudaStreamSynchronize(stream_), "sync");
-        check_device_error();
+        raise_device_error();
     }
 
     GpuCapabilities gpu_capabilities() const override {
@@ -388,6 +455,7 @@ private:
         std::unique_ptr<Arena> arena;
         float* image = nullptr;   // [B][3][H][W]
         float* depth = nullptr;   // [B][H][W]
+        float** depth_slot = nullptr;  // destination of the graph's last convolution
         float* pos = nullptr;     // [hw][D]
         void* patch_a = nullptr;  // int8 [B*hw][592] or f16
         float* patch_s = nullptr;
@@ -395,15 +463,16 @@ private:
         void* xn = nullptr;
         float* xn_s = nullptr;
         __half* qkv = nullptr;
-        __half* att = nullptr;
+        void* att = nullptr;      // attention output: f32 (int8 path, the quantizer's input) or f16
         void* att_q = nullptr;
         float* att_s = nullptr;
-        __half* hid = nullptr;
+        void* hid = nullptr;      // GELU(fc1) output: f32 (int8 path) or f16
         void* hid_q = nullptr;
         float* hid_s = nullptr;
         void* taps[4] = {};
         float* taps_s[4] = {};
-        __half* proj[4] = {};
+        __half* proj[4] = {};     // f16 channels-last projections (those the f16 convolutions read)
+        float* projf[4] = {};     // int8 path: f32 projections that are quantized next (0, 1, 3)
         void* ct_q[2] = {};
         float* ct_s[2] = {};
         __half* layer[4] = {};
@@ -424,6 +493,7 @@ private:
         const bool q = int8_;
         p.image = A.take<float>(B * 3 * p.H * p.W * 4);
         p.depth = A.take<float>(B * p.H * p.W * 4);
+        p.depth_slot = A.take<float*>(sizeof(float*));
         p.pos = A.take<float>(uint64_t(p.hw) * D * 4);
         p.patch_a = A.take<uint8_t>(PH * 592 * (q ? 1 : 2));
         if (q) p.patch_s = A.take<float>(PH * 4);
@@ -431,12 +501,12 @@ private:
         p.xn = A.take<uint8_t>(R * D * (q ? 1 : 2));
         if (q) p.xn_s = A.take<float>(R * 4);
         p.qkv = A.take<__half>(R * 3 * D * 2);
-        p.att = A.take<__half>(R * D * 2);
+        p.att = A.take<uint8_t>(R * D * (q ? 4 : 2));
         if (q) {
             p.att_q = A.take<uint8_t>(R * D);
             p.att_s = A.take<float>(R * 4);
         }
-        p.hid = A.take<__half>(R * 4 * D * 2);
+        p.hid = A.take<uint8_t>(R * 4 * D * (q ? 4 : 2));
         if (q) {
             p.hid_q = A.take<uint8_t>(R * 4 * D);
             p.hid_s = A.take<float>(R * 4);
@@ -444,7 +514,10 @@ private:
         for (int i = 0; i < 4; ++i) {
             p.taps[i] = A.take<uint8_t>(PH * D * (q ? 1 : 2));
             if (q) p.taps_s[i] = A.take<float>(PH * 4);
-            p.proj[i] = A.take<__half>(PH * cp_[i] * 2);
+            if (q && i != 2)
+                p.projf[i] = A.take<float>(PH * a.oc[i] * 4);
+            else
+                p.proj[i] = A.take<__half>(PH * cp_[i] * 2);
         }
         for (int i = 0; i < 2; ++i) {
             const uint32_t k = i == 0 ? 4 : 2;
@@ -507,9 +580,12 @@ private:
         alloc(p, *p.arena);
         op(launch_position_bicubic(p.pos, pos_, arch_.d, p.pw, p.ph, stream_), "position_bicubic");
         // warm-up run (sets kernel attributes), then capture
+        cuda_check(cudaStreamWaitEvent(stream_, done_, 0), "wait");
+        op(launch_store_pointer(reinterpret_cast<void**>(p.depth_slot), p.depth, stream_), "store_pointer");
         enqueue(p, stream_);
+        queue_error_read(stream_);
         cuda_check(cudaStreamSynchronize(stream_), "warm-up");
-        check_device_error();
+        raise_device_error();
         cudaGraph_t g = nullptr;
         cuda_check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "capture");
         try {
@@ -549,6 +625,8 @@ public:
         cudaEvent_t start;
         cuda_check(cudaEventCreate(&start), "event");
         marks_.clear();
+        cuda_check(cudaStreamWaitEvent(stream_, done_, 0), "wait");
+        op(launch_store_pointer(reinterpret_cast<void**>(p.depth_slot), p.depth, stream_), "store_pointer");
         cuda_check(cudaStreamSynchronize(stream_), "sync");
         cuda_check(cudaEventRecord(start, stream_), "event record");
         profiling_ = true;
@@ -559,8 +637,9 @@ public:
             throw;
         }
         profiling_ = false;
+        queue_error_read(stream_);
         cuda_check(cudaStreamSynchronize(stream_), "sync");
-        check_device_error();
+        raise_device_error();
         std::string out = "{\"batch\": " + std::to_string(batch) + ", \"width\": " + std::to_string(w) +
                           ", \"height\": " + std::to_string(h) + ", \"ops\": [";
         cudaEvent_t prev = start;
@@ -619,13 +698,24 @@ private:
         return g;
     }
 
+    // The whole graph: embedding, blocks (with the tap LayerNorms), head.
+    // The stage functions below are also what the stage probes run, so a
+    // probe exercises exactly the launches of the captured graph.
     void enqueue(Plan& p, cudaStream_t st) {
+        enqueue_embed(p, st);
+        int tap = 0;
+        for (uint32_t i = 0; i < arch_.blocks; ++i) {
+            enqueue_block(p, i, st);
+            if (tap < 4 && i == arch_.taps[tap]) enqueue_tap(p, tap++, st);
+        }
+        enqueue_head(p, st);
+    }
+
+    // ---- patch embedding + cls + positions (src/operators.cpp:1211-1406)
+    void enqueue_embed(Plan& p, cudaStream_t st) {
         const Arch& a = arch_;
         const bool q = int8_;
-        const uint32_t B = p.B, D = a.d, F = a.f;
-        const uint32_t R = B * p.T, PH = B * p.hw;
-
-        // ---- patch embedding + cls + positions (src/operators.cpp:1211-1406)
+        const uint32_t B = p.B, D = a.d, PH = B * p.hw;
         step(st, launch_fill_tokens(p.x, cls_, pos_, p.pos, D, p.T, B, st), "fill_tokens");
         if (q)
             step(st, launch_im2col_quantize(static_cast<uint32_t*>(p.patch_a), p.patch_s, p.image, B, p.W, p.H, 3, p.pw,
@@ -634,98 +724,125 @@ private:
         else
             step(st, launch_patch_im2col<__half>(static_cast<__half*>(p.patch_a), p.image, B, p.H, p.W, 592, st),
                "patch im2col");
+        GemmArgs g = gemm(patch_, p.patch_a, 592, PH, q);
+        g.s_in = p.patch_s;
+        g.flags |= kEpiResidual1;
+        g.res1 = p.x;
+        g.out = p.x;
+        g.out_kind = kOutF32Rows;
+        g.ldo = D;
+        g.rows_per_img = p.hw;
+        g.out_rows_per_img = p.T;
+        g.row_offset = 1;
+        step(st, launch_gemm(g, st), "patch gemm");
+    }
+
+    // block i's first LayerNorm: residual p.x -> p.xn (int8 codes + p.xn_s, or f16)
+    void enqueue_ln1(Plan& p, uint32_t i, cudaStream_t st) {
+        const Block& b = blocks_[i];
+        step(st, launch_layer_norm(p.xn, p.xn_s, p.x, b.ln1_w, b.ln1_b, p.B * p.T, arch_.d, 1e-6f,
+                                   int8_ ? kLnOutS8 : kLnOutF16, 1, 1, 0, st),
+             "ln1");
+    }
+
+    // ---- transformer block i (src/encoder.cpp:426-591), p.x updated in place
+    void enqueue_block(Plan& p, uint32_t i, cudaStream_t st) {
+        const Arch& a = arch_;
+        const bool q = int8_;
+        const uint32_t B = p.B, D = a.d;
+        const uint32_t R = B * p.T;
+        const Block& b = blocks_[i];
+        enqueue_ln1(p, i, st);
         {
-            GemmArgs g = gemm(patch_, p.patch_a, 592, PH, q);
-            g.s_in = p.patch_s;
-            g.flags |= kEpiResidual1;
+            GemmArgs g = gemm(b.qkv, p.xn, D, R, q);
+            g.s_in = p.xn_s;
+            g.out = p.qkv;
+            g.out_kind = kOutHalfRows;
+            g.ldo = 3 * D;
+            step(st, launch_gemm(g, st), "qkv");
+        }
+        // int8 path: attention output and GELU hidden stay f32 up to their
+        // quantizers, as the reference's int8 mode keeps them
+        // (src/operators.cpp:1098-1209 writes f32; src/encoder.cpp:526-528)
+        step(st, launch_attention_tc(p.att, q, p.qkv, false, B, p.T, a.heads, 3 * D, D, st), "attention");
+        const void* att_in = p.att;
+        if (q) {
+            step(st, launch_quantize_rows<float>(static_cast<uint32_t*>(p.att_q), p.att_s,
+                                                 static_cast<const float*>(p.att), R, D, 0, R, 0, D, D / 4, st),
+               "quantize attention");
+            att_in = p.att_q;
+        }
+        {
+            GemmArgs g = gemm(b.proj, att_in, D, R, q);
+            g.s_in = p.att_s;
+            g.flags |= kEpiLayerScale;
+            g.gamma = b.ls1;
             g.res1 = p.x;
             g.out = p.x;
             g.out_kind = kOutF32Rows;
             g.ldo = D;
-            g.rows_per_img = p.hw;
-            g.out_rows_per_img = p.T;
-            g.row_offset = 1;
-            step(st, launch_gemm(g, st), "patch gemm");
+            step(st, launch_gemm(g, st), "proj");
         }
-        // ---- transformer blocks (src/encoder.cpp:426-591)
-        int tap = 0;
-        for (uint32_t i = 0; i < a.blocks; ++i) {
-            const Block& b = blocks_[i];
-            step(st, launch_layer_norm(p.xn, p.xn_s, p.x, b.ln1_w, b.ln1_b, R, D, 1e-6f, q ? kLnOutS8 : kLnOutF16, 1, 1, 0,
-                                 st),
-               "ln1");
-            {
-                GemmArgs g = gemm(b.qkv, p.xn, D, R, q);
-                g.s_in = p.xn_s;
-                g.out = p.qkv;
-                g.out_kind = kOutHalfRows;
-                g.ldo = 3 * D;
-                step(st, launch_gemm(g, st), "qkv");
-            }
-            step(st, launch_attention<__half>(p.att, p.qkv, B, p.T, a.heads, 3 * D, D, st), "attention");
-            const void* att_in = p.att;
-            if (q) {
-                step(st, launch_quantize_rows<__half>(static_cast<uint32_t*>(p.att_q), p.att_s, p.att, R, D, 0, R, 0, D,
-                                                D / 4, st),
-                   "quantize attention");
-                att_in = p.att_q;
-            }
-            {
-                GemmArgs g = gemm(b.proj, att_in, D, R, q);
-                g.s_in = p.att_s;
-                g.flags |= kEpiLayerScale;
-                g.gamma = b.ls1;
-                g.res1 = p.x;
-                g.out = p.x;
-                g.out_kind = kOutF32Rows;
-                g.ldo = D;
-                step(st, launch_gemm(g, st), "proj");
-            }
-            step(st, launch_layer_norm(p.xn, p.xn_s, p.x, b.ln2_w, b.ln2_b, R, D, 1e-6f, q ? kLnOutS8 : kLnOutF16, 1, 1, 0,
-                                 st),
-               "ln2");
-            {
-                GemmArgs g = gemm(b.fc1, p.xn, D, R, q);
-                g.s_in = p.xn_s;
-                g.flags |= kEpiGelu;
-                g.out = p.hid;
-                g.out_kind = kOutHalfRows;
-                g.ldo = 4 * D;
-                step(st, launch_gemm(g, st), "fc1");
-            }
-            const void* hid_in = p.hid;
-            if (q) {
-                step(st, launch_quantize_rows<__half>(static_cast<uint32_t*>(p.hid_q), p.hid_s, p.hid, R, 4 * D, 0, R, 0,
-                                                4 * D, D, st),
-                   "quantize hidden");
-                hid_in = p.hid_q;
-            }
-            {
-                GemmArgs g = gemm(b.fc2, hid_in, 4 * D, R, q);
-                g.s_in = p.hid_s;
-                g.flags |= kEpiLayerScale;
-                g.gamma = b.ls2;
-                g.res1 = p.x;
-                g.out = p.x;
-                g.out_kind = kOutF32Rows;
-                g.ldo = D;
-                step(st, launch_gemm(g, st), "fc2");
-            }
-            if (tap < 4 && i == a.taps[tap]) {
-                // pretrained.norm on the patch rows only (cls dropped)
-                step(st, launch_layer_norm(p.taps[tap], p.taps_s[tap], p.x, norm_w_, norm_b_, PH, D, 1e-6f,
-                                     q ? kLnOutS8 : kLnOutF16, p.hw, p.T, 1, st),
-                   "tap norm");
-                ++tap;
-            }
+        step(st, launch_layer_norm(p.xn, p.xn_s, p.x, b.ln2_w, b.ln2_b, R, D, 1e-6f, q ? kLnOutS8 : kLnOutF16, 1, 1, 0,
+                             st),
+           "ln2");
+        {
+            GemmArgs g = gemm(b.fc1, p.xn, D, R, q);
+            g.s_in = p.xn_s;
+            g.flags |= kEpiGelu;
+            g.out = p.hid;
+            g.out_kind = q ? kOutF32Rows : kOutHalfRows;
+            g.ldo = 4 * D;
+            step(st, launch_gemm(g, st), "fc1");
         }
+        const void* hid_in = p.hid;
+        if (q) {
+            step(st, launch_quantize_rows<float>(static_cast<uint32_t*>(p.hid_q), p.hid_s,
+                                                 static_cast<const float*>(p.hid), R, 4 * D, 0, R, 0, 4 * D, D, st),
+               "quantize hidden");
+            hid_in = p.hid_q;
+        }
+        {
+            GemmArgs g = gemm(b.fc2, hid_in, 4 * D, R, q);
+            g.s_in = p.hid_s;
+            g.flags |= kEpiLayerScale;
+            g.gamma = b.ls2;
+            g.res1 = p.x;
+            g.out = p.x;
+            g.out_kind = kOutF32Rows;
+            g.ldo = D;
+            step(st, launch_gemm(g, st), "fc2");
+        }
+    }
+
+    // pretrained.norm of tap k on the patch rows only (cls dropped)
+    void enqueue_tap(Plan& p, int k, cudaStream_t st) {
+        step(st, launch_layer_norm(p.taps[k], p.taps_s[k], p.x, norm_w_, norm_b_, p.B * p.hw, arch_.d, 1e-6f,
+                                   int8_ ? kLnOutS8 : kLnOutF16, p.hw, p.T, 1, st),
+             "tap norm");
+    }
+
+    // ---- DPT head (src/dpt.cpp:628-863): taps -> depth (through p.depth_slot)
+    void enqueue_head(Plan& p, cudaStream_t st) {
+        const Arch& a = arch_;
+        const bool q = int8_;
+        const uint32_t B = p.B, D = a.d, F = a.f;
+        const uint32_t PH = B * p.hw;
         // ---- DPT projections and resize layers (src/dpt.cpp:641-731)
+        // int8 path: the projections that are quantized next (0, 1, 3) are
+        // written f32, the reference's FeatureMap precision (src/dpt.cpp:494-499)
         for (int i = 0; i < 4; ++i) {
             GemmArgs g = gemm(projects_[i], p.taps[i], D, PH, q);
             g.s_in = p.taps_s[i];
-            g.out = p.proj[i];
-            g.out_kind = kOutHalfRows;
-            g.ldo = cp_[i];
+            if (p.projf[i]) {
+                g.out = p.projf[i];
+                g.out_kind = kOutF32Rows;
+                g.ldo = a.oc[i];
+            } else {
+                g.out = p.proj[i];
+                g.out_kind = kOutHalfRows;
+                g.ldo = cp_[i];
+            }
             step(st, launch_gemm(g, st), "project");
         }
         for (int i = 0; i < 2; ++i) {
@@ -733,8 +850,10 @@ private:
             GemmArgs g;
             if (q) {
                 const uint32_t kp = up(oc, 16);
-                step(st, launch_quantize_rows<__half>(static_cast<uint32_t*>(p.ct_q[i]), p.ct_s[i], p.proj[i], PH, oc, 0,
-                                                PH, 0, cp_[i], kp / 4, st),
+                // per-pixel channel quantization with the im2col rule x * (1/scale),
+                // as conv_transpose_nonoverlap_int8 does (src/operators.cpp:1952-1955)
+                step(st, launch_im2col_quantize_nhwc<float>(static_cast<uint8_t*>(p.ct_q[i]), p.ct_s[i], p.projf[i], B,
+                                                            p.ph, p.pw, oc, oc, 1, 1, 0, p.ph, p.pw, kp, st),
                    "quantize convT input");
                 g = gemm(resize_[i], p.ct_q[i], kp, PH, true);
                 g.s_in = p.ct_s[i];
@@ -754,8 +873,8 @@ private:
             const uint32_t oc = a.oc[3], rows = B * p.lh[3] * p.lw[3];
             GemmArgs g;
             if (q) {
-                step(st, launch_im2col_quantize_nhwc<__half>(static_cast<uint8_t*>(p.r3_col), p.r3_s, p.proj[3], B, p.ph,
-                                                       p.pw, oc, cp_[3], 3, 2, 1, p.lh[3], p.lw[3], 9 * oc, st),
+                step(st, launch_im2col_quantize_nhwc<float>(static_cast<uint8_t*>(p.r3_col), p.r3_s, p.projf[3], B,
+                                                            p.ph, p.pw, oc, oc, 3, 2, 1, p.lh[3], p.lw[3], 9 * oc, st),
                    "resize3 im2col_quantize");
                 g = gemm(resize_[3], p.r3_col, 9 * oc, rows, true);
                 g.s_in = p.r3_s;
@@ -849,6 +968,7 @@ private:
             g.head_b = head_b_;
             g.head_max_depth = model_.metric_max_depth();
             g.out = p.depth;
+            g.out_slot = p.depth_slot;
             g.out_kind = kOutHeadF32;
             step(st, launch_gemm(g, st), "output_conv2");
         }
@@ -858,13 +978,17 @@ private:
         if (!chw || !depth || batch <= 0) throw std::invalid_argument("null inference argument");
         std::lock_guard<std::mutex> lock(mutex_);
         cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+        poll_device_error();
         Plan& p = plan(batch, w, h);
+        order_after_previous_call(stream_);
         const uint64_t in_bytes = uint64_t(batch) * 3 * w * h * 4;
         const uint64_t out_bytes = uint64_t(batch) * ow * oh * 4;
         ensure_host(in_bytes, out_bytes);
         std::memcpy(host_in_, chw, in_bytes);
         cuda_check(cudaMemcpyAsync(p.image, host_in_, in_bytes, cudaMemcpyHostToDevice, stream_), "H2D");
         upload_bytes_ += in_bytes;
+        op(launch_store_pointer(reinterpret_cast<void**>(p.depth_slot), p.depth, stream_), "store_pointer");
+        ++launches_;
         launch_plan(p, stream_);
         float* result = p.depth;
         if (ow != w || oh != h) {
@@ -874,10 +998,12 @@ private:
             result = resized;
         }
         cuda_check(cudaMemcpyAsync(host_out_, result, out_bytes, cudaMemcpyDeviceToHost, stream_), "D2H");
+        queue_error_read(stream_);
+        finish_call(stream_);
         cuda_check(cudaStreamSynchronize(stream_), "sync");
         std::memcpy(depth, host_out_, out_bytes);
         download_bytes_ += out_bytes;
-        check_device_error();
+        raise_device_error();
     }
 
     void ensure_host(uint64_t in, uint64_t out) {
@@ -912,14 +1038,48 @@ private:
         return resized_ptr_;
     }
 
-    void check_device_error() {
+    // Device-side failures (a bounded pipeline wait that gave up) set the
+    // device error word, which stays set until the host clears it. Every
+    // call queues an asynchronous read of the word into pinned host memory
+    // behind its own work: a synchronous call checks it after its stream
+    // synchronisation; after an asynchronous call (a caller stream) it is
+    // checked by the next call of this context once that read has completed,
+    // or by synchronize(), which waits for it.
+    void queue_error_read(cudaStream_t st) {
         int* word = device_error_word();
-        int value = 0;
-        if (word && cudaMemcpy(&value, word, sizeof value, cudaMemcpyDeviceToHost) == cudaSuccess && value != 0) {
-            const int zero = 0;
-            cudaMemcpy(word, &zero, sizeof zero, cudaMemcpyHostToDevice);
-            throw std::runtime_error("a kernel pipeline wait timed out on the device");
+        if (!word) throw std::runtime_error("the device error word is unavailable");
+        cuda_check(cudaMemcpyAsync(err_host_, word, sizeof(int), cudaMemcpyDeviceToHost, st), "error word read");
+        cuda_check(cudaEventRecord(err_event_, st), "event record");
+        err_pending_ = true;
+    }
+
+    // Throws (DAV2_STATUS_INFERENCE_FAILED) when the last completed read saw
+    // the word set, after clearing it on the device.
+    void raise_device_error() {
+        if (!err_pending_) return;
+        err_pending_ = false;
+        if (*err_host_ == 0) return;
+        *err_host_ = 0;
+        if (int* word = device_error_word()) {
+            cuda_check(cudaMemsetAsync(word, 0, sizeof(int), stream_), "error word clear");
+            cuda_check(cudaStreamSynchronize(stream_), "sync");
         }
+        throw_inference_failed("a kernel pipeline wait timed out on the device");
+    }
+
+    void poll_device_error() {
+        if (err_pending_ && cudaEventQuery(err_event_) == cudaSuccess) raise_device_error();
+    }
+
+    // A context's plans and buffers are shared by all its calls: a call on
+    // another stream than the previous call's starts after that call's work.
+    void order_after_previous_call(cudaStream_t st) {
+        if (last_stream_ != nullptr && last_stream_ != st) cuda_check(cudaStreamWaitEvent(st, done_, 0), "wait");
+    }
+
+    void finish_call(cudaStream_t st) {
+        cuda_check(cudaEventRecord(done_, st), "event record");
+        last_stream_ = st;
     }
 
     ModelFile model_;
@@ -928,6 +1088,11 @@ private:
     Arch arch_;
     bool int8_ = false;
     cudaStream_t stream_ = nullptr;
+    cudaEvent_t done_ = nullptr;       // end of the last call's work (on last_stream_)
+    cudaStream_t last_stream_ = nullptr;
+    cudaEvent_t err_event_ = nullptr;  // completion of the last queued error-word read
+    int* err_host_ = nullptr;          // pinned copy of the device error word
+    bool err_pending_ = false;
     std::mutex mutex_;
 
     Arena wa_;
@@ -964,6 +1129,13 @@ std::unique_ptr<Executor> create_executor(const std::string& model_path, dav2_en
     (void)cache_path;
     if ((flags & DAV2_CREATE_FORCE_METAL) && (flags & DAV2_CREATE_FORCE_VULKAN))
         throw std::invalid_argument("Metal and Vulkan cannot both be forced");
+    // The reference keeps fp32 weights and scores for these requests
+    // (src/vulkan_executor.cpp:505-518, src/encoder.cpp:389-396). This
+    // executor has no fp32-exact tensor path, so it refuses them instead of
+    // running a lower precision under an fp32 request.
+    if (flags & (DAV2_CREATE_FORCE_FP32 | DAV2_CREATE_FORCE_FP32_WEIGHTS | DAV2_CREATE_FORCE_FP32_ATTENTION))
+        throw_unsupported("fp32 execution is not available in the CUDA executor (use the default / FORCE_FP16 "
+                          "or FORCE_INT8 precision)");
     return std::make_unique<CudaExecutor>(model_path, encoder, device_index, flags);
 }
 

@@ -1,6 +1,9 @@
 // The public C ABI (include/depth_anything_v2.h) over the CUDA executor.
 // Argument checks, their order, the status mapping of exceptions and the
-// thread-local last-error string follow src/dav2.cpp:71-90 and 96-668.
+// thread-local last-error string follow src/dav2.cpp:71-90 and 96-668. The
+// runtime throws dav2::StatusError where the public status is fixed at the
+// throw site (model I/O / format, no device, device-side failure,
+// unsupported precision); protect() maps the class, never the message.
 #include <algorithm>
 #include <cstddef>
 #include <cstring>
@@ -13,6 +16,7 @@
 #include "depth_anything_v2.h"
 #include "executor.h"
 #include "image.h"
+#include "status_error.h"
 
 struct dav2_context {
     std::shared_ptr<dav2::Executor> executor;
@@ -45,6 +49,8 @@ dav2_status protect(F&& f) {
         last_error.clear();
         return DAV2_STATUS_OK;
     } catch (const ApiError& e) {
+        return fail(e.status(), e.what());
+    } catch (const dav2::StatusError& e) {
         return fail(e.status(), e.what());
     } catch (const std::bad_alloc&) {
         return fail(DAV2_STATUS_OUT_OF_MEMORY, "out of memory");
@@ -130,22 +136,8 @@ DAV2_API dav2_status DAV2_CALL dav2_create(const char* path, const dav2_create_o
         const std::string cache = options->struct_size >= sizeof(dav2_create_options) && options->cache_path_utf8
                                       ? options->cache_path_utf8
                                       : "";
-        try {
-            ctx->executor = std::shared_ptr<dav2::Executor>(
-                dav2::create_executor(path, options->encoder, options->vulkan_device_index, options->flags, cache));
-        } catch (const std::runtime_error& e) {
-            const std::string m = e.what();
-            if (m.find("open model") != std::string::npos || m.find("query model") != std::string::npos ||
-                m.find("map model") != std::string::npos)
-                throw ApiError(DAV2_STATUS_MODEL_IO, e.what());
-            if (m.find("DAV2") != std::string::npos || m.find("CRC") != std::string::npos ||
-                m.find("truncated") != std::string::npos || m.find("encoder does not match") != std::string::npos ||
-                m.find("missing tensor") != std::string::npos)
-                throw ApiError(DAV2_STATUS_MODEL_FORMAT, e.what());
-            if (m.find("no CUDA device") != std::string::npos)
-                throw ApiError(DAV2_STATUS_VULKAN_UNAVAILABLE, e.what());
-            throw;
-        }
+        ctx->executor = std::shared_ptr<dav2::Executor>(
+            dav2::create_executor(path, options->encoder, options->vulkan_device_index, options->flags, cache));
         *context = ctx.release();
     });
 }
@@ -321,6 +313,25 @@ DAV2_API dav2_status DAV2_CALL dav2_profile_operations(dav2_context* context, ui
         if (s.size() + 1 > capacity) throw ApiError(DAV2_STATUS_BUFFER_TOO_SMALL, "profile buffer is too small");
         std::memcpy(json, s.c_str(), s.size() + 1);
     });
+}
+
+DAV2_API dav2_status DAV2_CALL dav2_probe_encoder_block(dav2_context* context, uint32_t batch, int32_t w, int32_t h,
+                                                        uint32_t block, const float* x_in, float* x_out,
+                                                        int8_t* ln1_codes, float* ln1_scales) {
+    if (!context || !x_in || !x_out || batch == 0) return fail(DAV2_STATUS_INVALID_ARGUMENT, "null probe argument");
+    if (w <= 0 || h <= 0 || w % 14 != 0 || h % 14 != 0)
+        return fail(DAV2_STATUS_INVALID_ARGUMENT, "network dimensions must be positive multiples of 14");
+    return protect([&] {
+        context->executor->probe_block(int(batch), w, h, int(block), x_in, x_out, ln1_codes, ln1_scales);
+    });
+}
+
+DAV2_API dav2_status DAV2_CALL dav2_probe_head(dav2_context* context, uint32_t batch, int32_t w, int32_t h,
+                                               const float* tap_x, float* depth) {
+    if (!context || !tap_x || !depth || batch == 0) return fail(DAV2_STATUS_INVALID_ARGUMENT, "null probe argument");
+    if (w <= 0 || h <= 0 || w % 14 != 0 || h % 14 != 0)
+        return fail(DAV2_STATUS_INVALID_ARGUMENT, "network dimensions must be positive multiples of 14");
+    return protect([&] { context->executor->probe_head(int(batch), w, h, tap_x, depth); });
 }
 
 DAV2_API dav2_status DAV2_CALL dav2_synchronize(dav2_context* context) {

@@ -48,6 +48,19 @@ public:
     // Runs the (batch, width, height) graph once without graph capture,
     // timing every launch with events on its stream; returns JSON.
     virtual std::string profile_json(int batch, int width, int height) = 0;
+    // Stage probes (the analogue of the reference's tools/dav2_encoder_probe.cpp
+    // stage dumps): run one stage of the (batch, width, height) graph — the
+    // same launches the captured graph makes — on host inputs.
+    //   probe_block: transformer block `block` on residual rows x_in
+    //     ([batch*tokens][embedding] f32) -> x_out; at int8 precision
+    //     ln1_codes / ln1_scales (nullable) receive the block's first
+    //     LayerNorm as the int8 codes and f32 row scales its GEMM reads.
+    //   probe_head: the tap LayerNorms and the DPT head from the four tapped
+    //     residual streams ([4][batch*tokens][embedding]) -> depth
+    //     [batch][height][width].
+    virtual void probe_block(int batch, int width, int height, int block, const float* x_in, float* x_out,
+                             std::int8_t* ln1_codes, float* ln1_scales) = 0;
+    virtual void probe_head(int batch, int width, int height, const float* tap_x, float* depth) = 0;
 };
 
 // src/executor_factory.cpp:7-42: FORCE_METAL / FORCE_VULKAN both set is an

@@ -9,6 +9,8 @@
 #include <limits>
 #include <stdexcept>
 
+#include "status_error.h"
+
 namespace dav2 {
 namespace {
 
@@ -64,49 +66,49 @@ ModelFile::ModelFile(const std::string& path, dav2_encoder expected) {
     if (path.empty()) throw std::invalid_argument("model path is empty");
     try {
         fd_ = ::open(path.c_str(), O_RDONLY | O_CLOEXEC);
-        if (fd_ < 0) throw std::runtime_error("failed to open model file");
+        if (fd_ < 0) throw_model_io("failed to open model file");
         struct stat st {};
-        if (fstat(fd_, &st) != 0 || st.st_size < 0) throw std::runtime_error("failed to query model file size");
+        if (fstat(fd_, &st) != 0 || st.st_size < 0) throw_model_io("failed to query model file size");
         size_ = static_cast<std::uint64_t>(st.st_size);
-        if (size_ < sizeof(Header)) throw std::runtime_error("model file is truncated or too large");
+        if (size_ < sizeof(Header)) throw_model_format("model file is truncated or too large");
         void* m = mmap(nullptr, size_, PROT_READ, MAP_PRIVATE, fd_, 0);
-        if (m == MAP_FAILED) throw std::runtime_error("failed to map model file");
+        if (m == MAP_FAILED) throw_model_io("failed to map model file");
         view_ = static_cast<const unsigned char*>(m);
 
         Header h;
         std::memcpy(&h, view_, sizeof h);
         if (std::memcmp(h.magic, "DAV2MOD\0", 8) != 0 || h.version != 1 || h.endian != 0x01020304u)
-            throw std::runtime_error("invalid DAV2 model header");
+            throw_model_format("invalid DAV2 model header");
         if (h.encoder != static_cast<std::uint32_t>(expected))
-            throw std::runtime_error("model encoder does not match create options");
+            throw_model_format("model encoder does not match create options");
         if (h.tensor_count == 0 || h.tensor_count > 2048 || h.file_bytes != size_)
-            throw std::runtime_error("invalid DAV2 model bounds");
+            throw_model_format("invalid DAV2 model bounds");
         if (h.directory_bytes != std::uint64_t(h.tensor_count) * sizeof(Record) ||
             !in_bounds(h.directory_offset, h.directory_bytes, size_) || h.data_offset % 64 != 0 ||
             h.data_offset < h.directory_offset + h.directory_bytes || h.data_offset > size_)
-            throw std::runtime_error("invalid DAV2 tensor directory");
+            throw_model_format("invalid DAV2 tensor directory");
         if (h.metadata_offset != 0) {
             if (h.metadata_offset != h.directory_offset + h.directory_bytes ||
                 !in_bounds(h.metadata_offset, sizeof(Metadata), h.data_offset))
-                throw std::runtime_error("invalid DAV2 derivation metadata bounds");
+                throw_model_format("invalid DAV2 derivation metadata bounds");
             Metadata md;
             std::memcpy(&md, view_ + h.metadata_offset, sizeof md);
             if (std::memcmp(md.magic, "DAV2META", 8) != 0 || md.version != 1 || md.bytes != sizeof(Metadata) ||
                 md.model_format_version != 1 || md.encoder != h.encoder || (md.flags & ~1u) != 0 ||
                 std::memchr(md.converter, '\0', sizeof md.converter) == nullptr)
-                throw std::runtime_error("invalid DAV2 derivation metadata");
+                throw_model_format("invalid DAV2 derivation metadata");
             const std::string converter(md.converter);
             if (md.flags & 1u) {
                 float depth;
                 std::memcpy(&depth, &md.max_depth_bits, sizeof depth);
                 if (converter != "dav2-export-pytorch-metric-v1")
-                    throw std::runtime_error("invalid DAV2 metric converter identity");
-                if (depth != 20.0f && depth != 80.0f) throw std::runtime_error("invalid DAV2 metric maximum depth");
+                    throw_model_format("invalid DAV2 metric converter identity");
+                if (depth != 20.0f && depth != 80.0f) throw_model_format("invalid DAV2 metric maximum depth");
                 metric_max_depth_ = depth;
             } else if (md.max_depth_bits != 0) {
-                throw std::runtime_error("invalid DAV2 relative derivation metadata");
+                throw_model_format("invalid DAV2 relative derivation metadata");
             } else if (converter != "dav2-export-pytorch-v1") {
-                throw std::runtime_error("invalid DAV2 relative converter identity");
+                throw_model_format("invalid DAV2 relative converter identity");
             }
         }
         tensors_.reserve(h.tensor_count);
@@ -118,19 +120,19 @@ ModelFile::ModelFile(const std::string& path, dav2_encoder expected) {
             if (!end || r.name[0] == '\0' || r.dtype != 1 || r.rank == 0 || r.rank > 4 || r.flags != 0 ||
                 r.reserved != 0 || r.data_offset < h.data_offset || r.data_offset % 64 != 0 ||
                 !in_bounds(r.data_offset, r.data_bytes, size_))
-                throw std::runtime_error("invalid DAV2 tensor record");
+                throw_model_format("invalid DAV2 tensor record");
             std::uint64_t elements = 1;
             for (std::uint32_t d = 0; d < 4; ++d) {
                 if (d < r.rank) {
                     if (r.dims[d] == 0 || elements > std::numeric_limits<std::uint64_t>::max() / r.dims[d])
-                        throw std::runtime_error("invalid DAV2 tensor dimensions");
+                        throw_model_format("invalid DAV2 tensor dimensions");
                     elements *= r.dims[d];
                 } else if (r.dims[d] != 0) {
-                    throw std::runtime_error("invalid DAV2 unused dimension");
+                    throw_model_format("invalid DAV2 unused dimension");
                 }
             }
             if (elements != r.element_count || elements * 4 != r.data_bytes)
-                throw std::runtime_error("invalid DAV2 tensor byte count");
+                throw_model_format("invalid DAV2 tensor byte count");
             const char* name = reinterpret_cast<const char*>(view_ + h.directory_offset + std::uint64_t(i) * sizeof(Record));
             std::string_view key(name, static_cast<const char*>(end) - name);
             TensorView tv;
@@ -139,7 +141,7 @@ ModelFile::ModelFile(const std::string& path, dav2_encoder expected) {
             tv.rank = r.rank;
             tv.elements = r.element_count;
             tv.crc32 = r.crc32;
-            if (!tensors_.emplace(key, tv).second) throw std::runtime_error("duplicate DAV2 tensor name");
+            if (!tensors_.emplace(key, tv).second) throw_model_format("duplicate DAV2 tensor name");
             names_.push_back(key);
         }
     } catch (...) {
@@ -161,14 +163,14 @@ void ModelFile::unmap() noexcept {
 
 const TensorView& ModelFile::tensor(std::string_view name) const {
     auto it = tensors_.find(name);
-    if (it == tensors_.end()) throw std::runtime_error("model is missing tensor: " + std::string(name));
+    if (it == tensors_.end()) throw_model_format("model is missing tensor: " + std::string(name));
     return it->second;
 }
 
 void ModelFile::verify_crc() const {
     for (const auto& [name, t] : tensors_)
         if (crc32(t.data, t.elements * 4) != t.crc32)
-            throw std::runtime_error("CRC-32 mismatch for tensor " + std::string(name));
+            throw_model_format("CRC-32 mismatch for tensor " + std::string(name));
 }
 
 }  // namespace dav2

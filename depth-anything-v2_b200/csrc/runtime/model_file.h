@@ -34,7 +34,9 @@ public:
     bool contains(std::string_view name) const { return tensors_.count(name) != 0; }
     const std::vector<std::string_view>& names() const { return names_; }
     float metric_max_depth() const { return metric_max_depth_; }
-    // Verifies every tensor's CRC-32; throws std::runtime_error on mismatch.
+    // Verifies every tensor's CRC-32; a mismatch throws StatusError
+    // (DAV2_STATUS_MODEL_FORMAT), as do all format violations of the
+    // constructor; open/stat/mmap failures are DAV2_STATUS_MODEL_IO.
     void verify_crc() const;
 
 private:

@@ -27,6 +27,7 @@ DAV2CUDA = {
     "dav2cuda_build_info": (ctypes.c_char_p, []),
     "dav2cuda_device_error": (ctypes.c_int, []),
     "dav2cuda_launch_count": (u64, [ctypes.c_int]),
+    "dav2cuda_wait_probe": (ctypes.c_int, [u64, u32, vp]),
     "dav2cuda_layer_norm": (ctypes.c_int, [vp, vp, vp, vp, u32, u32, f32, vp]),
     "dav2cuda_gelu": (ctypes.c_int, [vp, vp, u64, vp]),
     "dav2cuda_softmax_rows": (ctypes.c_int, [vp, vp, u64, u32, f32, vp]),
@@ -42,6 +43,7 @@ DAV2CUDA = {
     "dav2cuda_preprocess_bgr8": (ctypes.c_int, [vp, vp, u32, u32, u32, u64, u64, u32, u32, vp]),
     "dav2cuda_preprocess_bgr8_bilinear": (ctypes.c_int, [vp, vp, u32, u32, u32, u64, u64, u32, u32, vp]),
     "dav2cuda_quantize_rows_s8": (ctypes.c_int, [vp, vp, vp, u32, u32, u64, vp]),
+    "dav2cuda_pack_weight_s8": (ctypes.c_int, [vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp]),
     "dav2cuda_im2col_quantize_s8": (ctypes.c_int, [vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, i32, vp]),
     "dav2cuda_linear_s8_packed": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp]),
     "dav2cuda_linear_int8_workspace_size": (u64, [u32, u32, u32]),

@@ -73,6 +73,8 @@ PUBLIC = {
     "dav2_infer_device_bgr8_batch": (ctypes.c_int, [vp, vp, u32, i32, i32, ctypes.c_ssize_t, ctypes.c_ssize_t, i32,
                                                     vp, vp]),
     "dav2_synchronize": (ctypes.c_int, [vp]),
+    "dav2_probe_encoder_block": (ctypes.c_int, [vp, u32, i32, i32, u32, vp, vp, vp, vp]),
+    "dav2_probe_head": (ctypes.c_int, [vp, u32, i32, i32, vp, vp]),
     "dav2_get_kernel_launch_count": (ctypes.c_int, [vp, ctypes.POINTER(u64)]),
     "dav2_profile_operations": (ctypes.c_int, [vp, u32, i32, i32, ctypes.c_char_p, ctypes.c_size_t]),
 }

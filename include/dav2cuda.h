@@ -53,6 +53,15 @@ DAV2CUDA_API const char* dav2cuda_build_info(void);
 DAV2CUDA_API int dav2cuda_device_error(void);
 /* Number of kernels this library launched since the last reset. */
 DAV2CUDA_API uint64_t dav2cuda_launch_count(int reset);
+/* Failure-detection check of the bounded device waits (no counterpart in
+ * the reference, whose Vulkan fences have host-side timeouts): one 32-thread
+ * block waits on an mbarrier phase through the same bounded wait the
+ * pipeline kernels use, with a limit of limit_ns (at most 1 s). With
+ * arrive != 0 the phase completes at once; with arrive == 0 nothing
+ * completes it, the wait gives up after limit_ns, sets the device error
+ * word to 1 exactly as a timed-out pipeline wait does, and the kernel
+ * returns. Asynchronous on the stream. */
+DAV2CUDA_API int dav2cuda_wait_probe(uint64_t limit_ns, uint32_t arrive, void* stream);
 
 /* --------------------------------------------------------------- row ops */
 
@@ -144,6 +153,19 @@ DAV2CUDA_API int dav2cuda_quantize_rows_s8(uint32_t* packed, float* scales, cons
                                            uint32_t rows, uint32_t columns,
                                            uint64_t input_offset, void* stream);
 
+/* The executor's on-device int8 weight packing (GpuModel's per-output-row
+ * symmetric quantization, src/gpu_model.cpp:207-284: scale = max(absmax/127,
+ * 1e-8), code = nearbyint(clamp(w/scale))): codes [rows][padded_columns]
+ * (int8, zero beyond `columns`) + f32 scales [rows]. layout 0: weight is
+ * [rows][columns]; 1: a conv-transpose [Ci][Co][k][k] packed as rows
+ * (ky*k+kx)*Co+co over Ci (rows = k*k*Co, columns = Ci); 2: a convolution
+ * [Co][Ci][k][k] with columns in (ky, kx, ci) order (rows = Co, columns =
+ * k*k*Ci). output_channels / kernel / input_channels describe layouts 1, 2. */
+DAV2CUDA_API int dav2cuda_pack_weight_s8(uint8_t* codes, float* scales, const float* weight, uint32_t layout,
+                                         uint32_t rows, uint32_t columns, uint32_t padded_columns,
+                                         uint32_t output_channels, uint32_t kernel, uint32_t input_channels,
+                                         void* stream);
+
 /* im2col_quantize_int8.glsl dispatch (src/operators.cpp:1787-1801) on a
  * planar [C,H,W] input: rows = output pixels, padded to ceil(C*k*k/4) words
  * (the reference layout). */
@@ -198,8 +220,9 @@ DAV2CUDA_API int dav2cuda_linear_int8(float* output, const float* input, const u
  * loads the library (dav2cuda_linear_int8_noalloc_scratch_limit()), held
  * until exit; larger problems return DAV2CUDA_INVALID_ARGUMENT. The first
  * call on a device resolves the array's address (make it before any stream
- * capture). All calls share the array: calls that overlap on the GPU race.
- * Allocates nothing. */
+ * capture); the address is kept for the life of the process, so no call may
+ * follow a cudaDeviceReset. All calls share the array: calls that overlap on
+ * the GPU race. Allocates nothing. */
 DAV2CUDA_API uint64_t dav2cuda_linear_int8_noalloc_scratch_limit(void);
 DAV2CUDA_API int dav2cuda_linear_int8_noalloc(float* output, const float* input,
                                               const uint32_t* int8_weight, const float* weight_scales,

@@ -338,9 +338,13 @@ DAV2_API dav2_status DAV2_CALL dav2_infer_bgr8_batch(dav2_context* context, cons
 
 /* EXTENSION: the headless device-resident submit path (the CUDA analogue
  * of the reference's GPU submit path without graphics interop): device BGR8
- * images in, device depth out (batch * image_width * image_height floats),
- * asynchronous on the given cudaStream_t (NULL = the context's stream; the
- * call then returns once the work is queued). */
+ * images in, device depth out (batch * image_width * image_height floats).
+ * stream NULL = the context's own stream, and the call waits for the work to
+ * finish. A non-NULL cudaStream_t makes the call return as soon as the work
+ * is queued on that stream; a device-side failure of that work is reported
+ * by the context's next call or by dav2_synchronize. Calls of one context on
+ * different streams run one after another on the device (each waits for the
+ * previous call's work), because they share the context's buffers. */
 DAV2_API dav2_status DAV2_CALL dav2_infer_device_bgr8_batch(dav2_context* context, const uint8_t* device_bgr,
                                                             uint32_t batch, int32_t image_width,
                                                             int32_t image_height, ptrdiff_t row_stride_bytes,
@@ -359,7 +363,29 @@ DAV2_API dav2_status DAV2_CALL dav2_get_kernel_launch_count(const dav2_context* 
 DAV2_API dav2_status DAV2_CALL dav2_profile_operations(dav2_context* context, uint32_t batch, int32_t network_width,
                                                        int32_t network_height, char* json, size_t capacity);
 
-/* EXTENSION: waits for all work the context queued. */
+/* EXTENSION (stage probes; the analogue of the reference's
+ * tools/dav2_encoder_probe.cpp stage dumps, used by the block- and head-level
+ * parity tests): run one stage of the context's (batch, network_width,
+ * network_height) graph — the same kernels in the same order as the
+ * captured graph — on host inputs, synchronously. tokens = 1 +
+ * (network_width/14)(network_height/14).
+ * dav2_probe_encoder_block: transformer block `block` on residual-stream
+ *   rows x_in ([batch*tokens][embedding] f32) -> x_out (same shape). At int8
+ *   precision, ln1_codes ([batch*tokens][embedding]) and ln1_scales
+ *   ([batch*tokens]) may be non-NULL and receive the block's first LayerNorm
+ *   as the int8 codes and f32 row scales that its QKV GEMM reads.
+ * dav2_probe_head: the four tap LayerNorms and the DPT head from the tapped
+ *   residual streams tap_x ([4][batch*tokens][embedding] f32) -> depth
+ *   ([batch][network_height][network_width]). */
+DAV2_API dav2_status DAV2_CALL dav2_probe_encoder_block(dav2_context* context, uint32_t batch, int32_t network_width,
+                                                        int32_t network_height, uint32_t block, const float* x_in,
+                                                        float* x_out, int8_t* ln1_codes, float* ln1_scales);
+DAV2_API dav2_status DAV2_CALL dav2_probe_head(dav2_context* context, uint32_t batch, int32_t network_width,
+                                               int32_t network_height, const float* tap_x, float* depth);
+
+/* EXTENSION: waits for all work the context queued, on any stream; returns
+ * DAV2_STATUS_INFERENCE_FAILED when that work hit a device-side failure (a
+ * bounded pipeline wait that gave up). */
 DAV2_API dav2_status DAV2_CALL dav2_synchronize(dav2_context* context);
 
 #ifdef __cplusplus

@@ -396,19 +396,53 @@ def _linear(sd, q8, x, name, precision):
     return linear_f32(x, w, b)
 
 
-def encoder_forward(sd, image, encoder, precision="fp32"):
-    """DINOv2 forward of src/encoder.cpp:322-597 on one planar [3,H,W] image.
+def ln1_codes(sd, x, block):
+    """Block `block`'s first LayerNorm (f32) and, at int8 precision, the
+    per-row codes and scales its QKV GEMM reads (quantize_rows_int8_fused:
+    x / scale): returns (normalized f32, packed codes u32, scales)."""
+    p = f"pretrained.blocks.{block}"
+    n = layer_norm(x, sd[p + ".norm1.weight"], sd[p + ".norm1.bias"])
+    rows, cols = n.shape
+    px, sx = quantize_rows_s8(n, rows, cols)
+    return n, px, sx
 
-    precision "fp32" restates the FP32 executor; "int8" restates the INT8
-    routing (src/encoder.cpp:285-297, src/operators.cpp:770-845 and the int8
-    patch embedding of src/operators.cpp:1270-1308) with fp32 attention.
-    Returns the four tapped, normalized token matrices [1+hw, D] and (pw, ph).
-    """
-    emb, heads, blocks, taps, _, _ = ENCODERS[encoder]
+
+def encoder_block(sd, x, block, encoder, precision="fp32", q8=None, tokens=None):
+    """One DINOv2 block of src/encoder.cpp:426-591 on residual rows x
+    ([images*tokens, D], images stacked; tokens = rows of one image).
+
+    precision "int8" restates the reference's INT8 routing: every linear on
+    per-row int8 activations (src/operators.cpp:770-845) with f32 outputs,
+    attention at its fp16 operand precision — Q, K and V rounded to f16 as
+    bmm_score_fp16.glsl / bmm_value_fp16.glsl read them
+    (src/encoder.cpp:389-396) — with f32 scores, softmax and accumulation, and
+    the f32 attention output and GELU hidden quantized by the next linear."""
+    emb, heads, _, _, _, _ = ENCODERS[encoder]
+    q8 = q8 if q8 is not None else _Int8Weights(sd)
+    tokens = tokens or x.shape[0]
+    p = f"pretrained.blocks.{block}"
+    n = layer_norm(x, sd[p + ".norm1.weight"], sd[p + ".norm1.bias"])
+    qkv = _linear(sd, q8, n, p + ".attn.qkv", precision)
+    if precision == "int8":
+        qkv = qkv.astype(np.float16).astype(np.float32)
+    att = np.concatenate([attention_head64(qkv[i:i + tokens], tokens, heads)
+                          for i in range(0, x.shape[0], tokens)]).reshape(x.shape[0], emb)
+    y = _linear(sd, q8, att, p + ".attn.proj", precision)
+    x = add_scaled(x, y, sd[p + ".ls1.gamma"])
+    n = layer_norm(x, sd[p + ".norm2.weight"], sd[p + ".norm2.bias"])
+    hdn = gelu(_linear(sd, q8, n, p + ".mlp.fc1", precision))
+    y = _linear(sd, q8, hdn, p + ".mlp.fc2", precision)
+    return add_scaled(x, y, sd[p + ".ls2.gamma"])
+
+
+def embed(sd, image, encoder, precision="fp32"):
+    """Patch embedding + cls + positional embedding (src/operators.cpp:1211-1406)
+    of one planar [3,H,W] image: the residual rows entering block 0."""
+    emb = ENCODERS[encoder][0]
     _, h, w = image.shape
     pw, ph = w // 14, h // 14
-    q8 = _Int8Weights(sd)
     if precision == "int8":
+        q8 = _Int8Weights(sd)
         packed, scales = im2col_quantize_s8(image, 14, 14, 0)
         pwt, swt = q8.get("pretrained.patch_embed.proj.weight")
         tokens = np.zeros(((pw * ph + 1), emb), np.float32)
@@ -420,19 +454,24 @@ def encoder_forward(sd, image, encoder, precision="fp32"):
         tokens = patch_embed_f32(image, sd["pretrained.patch_embed.proj.weight"],
                                  sd["pretrained.patch_embed.proj.bias"], sd["pretrained.cls_token"])
     planar = position_bicubic(sd["pretrained.pos_embed"], pw, ph)
-    x = add_position(tokens, planar, sd["pretrained.pos_embed"], pw, ph)
+    return add_position(tokens, planar, sd["pretrained.pos_embed"], pw, ph)
+
+
+def encoder_forward(sd, image, encoder, precision="fp32"):
+    """DINOv2 forward of src/encoder.cpp:322-597 on one planar [3,H,W] image.
+
+    precision "fp32" restates the FP32 executor; "int8" the INT8 routing
+    (encoder_block) with the int8 patch embedding of src/operators.cpp:1270-1308.
+    Returns the four tapped, normalized token matrices [1+hw, D] and (pw, ph).
+    """
+    _, _, blocks, taps, _, _ = ENCODERS[encoder]
+    _, h, w = image.shape
+    pw, ph = w // 14, h // 14
+    q8 = _Int8Weights(sd)
+    x = embed(sd, image, encoder, precision)
     feats = []
     for i in range(blocks):
-        p = f"pretrained.blocks.{i}"
-        n = layer_norm(x, sd[p + ".norm1.weight"], sd[p + ".norm1.bias"])
-        qkv = _linear(sd, q8, n, p + ".attn.qkv", precision)
-        att = attention_head64(qkv, x.shape[0], heads)
-        y = _linear(sd, q8, att, p + ".attn.proj", precision)
-        x = add_scaled(x, y, sd[p + ".ls1.gamma"])
-        n = layer_norm(x, sd[p + ".norm2.weight"], sd[p + ".norm2.bias"])
-        hdn = gelu(_linear(sd, q8, n, p + ".mlp.fc1", precision))
-        y = _linear(sd, q8, hdn, p + ".mlp.fc2", precision)
-        x = add_scaled(x, y, sd[p + ".ls2.gamma"])
+        x = encoder_block(sd, x, i, encoder, precision, q8)
         if i in taps:
             feats.append(layer_norm(x, sd["pretrained.norm.weight"], sd["pretrained.norm.bias"]))
     return feats, pw, ph

@@ -199,8 +199,12 @@ def test_preprocess_bgr8_bilinear(cuda, dav2lib):
 
 
 # ------------------------------------------------------------------ int8
-@pytest.mark.parametrize("rows,cols,offset", [(1369, 384, 384), (5, 4, 0), (300, 4096, 0), (7, 1028, 8)])
+@pytest.mark.parametrize("rows,cols,offset", [(1369, 384, 384), (5, 4, 0), (300, 4096, 0), (7, 1028, 8),
+                                             (8221, 1024, 0), (2741, 4096, 0), (513, 768, 0), (1370, 2048, 0)])
 def test_quantize_rows_bit_exact(cuda, dav2lib, rows, cols, offset):
+    """Generic, warp-per-row (<= 2048 columns) and register-resident (4096)
+    f32 quantizers — the latter two are the graph's attention-output and
+    GELU-hidden quantizers."""
     x = rng(cols).standard_normal(rows * cols + offset).astype(np.float32)
     x[offset + 3 * cols: offset + 4 * cols] = 0 if rows > 3 else x[offset + 3 * cols: offset + 4 * cols]  # zero row
     pk, sc = empty(cuda, (rows, cols // 4), np.uint32), empty(cuda, (rows,))
@@ -451,3 +455,35 @@ def test_invalid_arguments_do_not_launch(cuda, dav2lib):
     assert dav2lib.dav2cuda_quantize_rows_s8(None, None, None, 2, 6, 0, None) == 1
     assert dav2lib.dav2cuda_linear_s8_packed(None, None, None, None, None, None, 4, 20, 4, 0, 4, 0, 0, None) == 1
     assert dav2lib.dav2cuda_launch_count(0) == before
+
+
+@pytest.mark.parametrize("kind,shape", [(0, (1152, 384)), (0, (96, 1020)), (1, (256, 256, 4, 4)), (1, (48, 48, 4, 4)),
+                                        (2, (64, 96, 3, 3)), (2, (256, 1024, 3, 3))])
+def test_device_weight_packing_bit_exact(cuda, dav2lib, kind, shape):
+    """The executor's on-device int8 weight packer (per-output-row symmetric
+    codes, src/gpu_model.cpp:207-284) against the oracle's packer: kind 0 a
+    linear [N][K]; kind 1 a conv-transpose [Ci][Co][k][k] read as rows
+    (ky*k+kx)*Co+co over Ci; kind 2 a conv [Co][Ci][k][k] whose columns the
+    device orders (ky, kx, ci) — the oracle's (ci, ky, kx) codes permuted."""
+    w = (rng(sum(shape)).standard_normal(shape) * 0.02).astype(np.float32)
+    w.reshape(shape[0], -1)[1] = 0.0  # an all-zero row (scale floor 1e-8)
+    if kind == 0:
+        rows, K, co, k, ci = shape[0], shape[1], 0, 0, 0
+    elif kind == 1:
+        ci, co, k = shape[0], shape[1], shape[2]
+        rows, K = k * k * co, ci
+    else:
+        co, ci, k = shape[0], shape[1], shape[2]
+        rows, K = co, ci * k * k
+    kp = (K + 15) // 16 * 16
+    out, sc = empty(cuda, (rows, kp), np.uint8), empty(cuda, (rows,))
+    call(dav2lib, "dav2cuda_pack_weight_s8", ptr(out), ptr(sc), ptr(dev(cuda, w)), kind, rows, K, kp, co, k, ci, None)
+    finish(cuda, dav2lib)
+    codes = host(out).view(np.int8)[:, :K]
+    want_pk, want_sc = oracle.pack_weight_s8(w, transposed_conv=(kind == 1))
+    want = want_pk.view(np.int8).reshape(rows, -1)[:, :K]
+    if kind == 2:  # oracle columns (ci, ky, kx) -> device columns (ky, kx, ci)
+        want = want.reshape(rows, ci, k, k).transpose(0, 2, 3, 1).reshape(rows, K)
+    assert np.array_equal(host(sc), want_sc)
+    assert np.array_equal(codes, want)
+    assert not host(out)[:, K:].any()  # padding columns are zero

@@ -492,10 +492,250 @@ int dav2cuda_conv_transpose_int8(float* output, const float* input, const uint32
     return launch_gemm(g, st);
 }
 
+// ------------------------------------------------------------ token ops
+// VulkanOperators::prepare_tokens (src/operators.cpp:1211-1406): patch
+// embedding (conv 14/14 as a GEMM over 588-column patches, padded to 592),
+// class token at row 0, the 37x37 positional grid bicubic-resized to the
+// patch grid (identity at 37x37) and added. tokens = 1 + (w/14)(h/14).
+uint64_t dav2cuda_prepare_tokens_workspace_size(uint32_t w, uint32_t h, uint32_t embedding) {
+    const uint64_t hw = (uint64_t)(w / 14) * (h / 14);
+    return align256(hw * embedding * 4) + align256(hw * 592 * 2) + align256(hw * 4) +
+           align256((uint64_t)embedding * 592 * 2) + 256;
+}
+
+namespace {
+
+int prepare_tokens_common(float* output, const float* image, const void* weight, const float* weight_scales,
+                          const float* bias, const float* class_token, const float* position, uint32_t w,
+                          uint32_t h, uint32_t e, int elem, void* workspace, uint64_t workspace_bytes,
+                          cudaStream_t st) {
+    const uint32_t pw = w / 14, ph = h / 14, hw = pw * ph;
+    Carve ws(workspace, workspace_bytes);
+    float* interp = ws.take<float>((uint64_t)hw * e * 4);
+    void* patches = ws.take<uint8_t>((uint64_t)hw * 592 * 2);
+    float* scales = ws.take<float>((uint64_t)hw * 4);
+    void* wts = ws.take<uint8_t>((uint64_t)e * 592 * 2);
+    if (!ws.ok()) return set_error(DAV2CUDA_INVALID_ARGUMENT, "prepare_tokens: workspace is too small");
+    if (int rc = launch_position_bicubic(interp, position, e, pw, ph, st)) return rc;
+    if (int rc = launch_fill_tokens(output, class_token, position, interp, e, hw + 1, 1, st)) return rc;
+    int rc = 0;
+    if (elem == kElemS8) {
+        rc = launch_im2col_quantize(static_cast<uint32_t*>(patches), scales, image, 1, w, h, 3, pw, ph, 14, 14, 0,
+                                    592 / 4, st);
+        if (!rc) rc = pad_byte_rows(static_cast<uint8_t*>(wts), weight, e, 588, 592, st);
+    } else if (elem == kElemBF16) {
+        rc = launch_patch_im2col<__nv_bfloat16>(static_cast<__nv_bfloat16*>(patches), image, 1, h, w, 592, st);
+        if (!rc)
+            rc = launch_pad_rows_half<__nv_bfloat16>(static_cast<__nv_bfloat16*>(wts), static_cast<const float*>(weight),
+                                                     e, 588, 592, st);
+    } else {
+        rc = launch_patch_im2col<__half>(static_cast<__half*>(patches), image, 1, h, w, 592, st);
+        if (!rc)
+            rc = launch_pad_rows_half<__half>(static_cast<__half*>(wts), static_cast<const float*>(weight), e, 588,
+                                              592, st);
+    }
+    if (rc) return rc;
+    GemmArgs g;
+    g.elem = elem;
+    g.a = patches;
+    g.lda = 592;
+    g.b = wts;
+    g.ldb = 592;
+    g.m = hw;
+    g.n = e;
+    g.k = 592;
+    g.flags = kEpiBias | kEpiResidual1 | (elem == kElemS8 ? kEpiDequant : 0u);
+    g.s_in = scales;
+    g.s_w = weight_scales;
+    g.bias = bias;
+    g.res1 = output;  // the class row and positions written above: out = patch + bias + position
+    g.out = output;
+    g.out_kind = kOutF32Rows;
+    g.ldo = e;
+    g.rows_per_img = hw;
+    g.out_rows_per_img = hw + 1;
+    g.row_offset = 1;
+    return launch_gemm(g, st);
+}
+
+}  // namespace
+
+int dav2cuda_prepare_tokens_half(float* output, const float* image, const float* patch_weight, const float* patch_bias,
+                                 const float* class_token, const float* position, uint32_t w, uint32_t h,
+                                 uint32_t embedding, uint32_t precision, void* workspace, uint64_t workspace_bytes,
+                                 void* stream) {
+    REQUIRE(w && h && w % 14 == 0 && h % 14 == 0 && embedding && (precision == 1 || precision == 2),
+            "invalid patch embedding dimensions");
+    REQUIRE(!null_any(output, image, patch_weight, patch_bias, class_token, position, workspace),
+            "prepare_tokens: null buffer");
+    REQUIRE(workspace_bytes >= dav2cuda_prepare_tokens_workspace_size(w, h, embedding),
+            "prepare_tokens: workspace is too small");
+    return prepare_tokens_common(output, image, patch_weight, nullptr, patch_bias, class_token, position, w, h,
+                                 embedding, precision == 1 ? kElemBF16 : kElemF16, workspace, workspace_bytes,
+                                 as_stream(stream));
+}
+
+int dav2cuda_prepare_tokens_int8(float* output, const float* image, const uint32_t* patch_int8_weight,
+                                 const float* patch_weight_scales, const float* patch_bias, const float* class_token,
+                                 const float* position, uint32_t w, uint32_t h, uint32_t embedding, void* workspace,
+                                 uint64_t workspace_bytes, void* stream) {
+    REQUIRE(w && h && w % 14 == 0 && h % 14 == 0 && embedding, "invalid patch embedding dimensions");
+    REQUIRE(!null_any(output, image, patch_int8_weight, patch_weight_scales, patch_bias, class_token, position,
+                      workspace),
+            "prepare_tokens: null buffer");
+    REQUIRE(workspace_bytes >= dav2cuda_prepare_tokens_workspace_size(w, h, embedding),
+            "prepare_tokens: workspace is too small");
+    return prepare_tokens_common(output, image, patch_int8_weight, patch_weight_scales, patch_bias, class_token,
+                                 position, w, h, embedding, kElemS8, workspace, workspace_bytes, as_stream(stream));
+}
+
+// VulkanOperators::project_tokens* (src/operators.cpp:1408-1526): 1x1
+// convolution of the patch tokens (the class row skipped) into planar
+// output [Cout][height*width].
+uint64_t dav2cuda_project_tokens_workspace_size(uint32_t w, uint32_t h, uint32_t embedding, uint32_t output_channels) {
+    const uint64_t hw = (uint64_t)w * h;
+    const uint64_t kp = ((uint64_t)embedding + 15) / 16 * 16;
+    return align256(hw * kp * 2) + align256(hw * 4) + align256((uint64_t)output_channels * kp * 2) + 256;
+}
+
+namespace {
+
+int project_tokens_common(float* output, const float* tokens, const void* weight, const float* weight_scales,
+                          const float* bias, uint32_t w, uint32_t h, uint32_t e, uint32_t co, int elem,
+                          void* workspace, uint64_t workspace_bytes, cudaStream_t st) {
+    const uint32_t hw = w * h, kp = round_up(e, 16);
+    Carve ws(workspace, workspace_bytes);
+    void* a = ws.take<uint8_t>((uint64_t)hw * kp * 2);
+    float* scales = ws.take<float>((uint64_t)hw * 4);
+    void* b = ws.take<uint8_t>((uint64_t)co * kp * 2);
+    if (!ws.ok()) return set_error(DAV2CUDA_INVALID_ARGUMENT, "project_tokens: workspace is too small");
+    int rc = 0;
+    const void* wb = b;
+    if (elem == kElemS8) {
+        // quantize_rows_int8_fused with the input offset of one row (src/operators.cpp:1510-1522)
+        rc = launch_quantize_rows<float>(static_cast<uint32_t*>(a), scales, tokens, hw, e, e, hw, (uint64_t)hw * e, e,
+                                         kp / 4, st);
+        if (!rc && kp != e) rc = pad_byte_rows(static_cast<uint8_t*>(b), weight, co, e, kp, st);
+        if (kp == e) wb = weight;
+    } else if (elem == kElemBF16) {
+        rc = launch_pad_rows_half<__nv_bfloat16>(static_cast<__nv_bfloat16*>(a), tokens + e, hw, e, kp, st);
+        if (!rc)
+            rc = launch_pad_rows_half<__nv_bfloat16>(static_cast<__nv_bfloat16*>(b), static_cast<const float*>(weight),
+                                                     co, e, kp, st);
+    } else {
+        rc = launch_pad_rows_half<__half>(static_cast<__half*>(a), tokens + e, hw, e, kp, st);
+        if (!rc) rc = launch_pad_rows_half<__half>(static_cast<__half*>(b), static_cast<const float*>(weight), co, e, kp, st);
+    }
+    if (rc) return rc;
+    GemmArgs g;
+    g.elem = elem;
+    g.a = a;
+    g.lda = kp;
+    g.b = wb;
+    g.ldb = kp;
+    g.m = hw;
+    g.n = co;
+    g.k = kp;
+    g.flags = (bias ? kEpiBias : 0u) | (elem == kElemS8 ? kEpiDequant : 0u);
+    g.s_in = scales;
+    g.s_w = weight_scales;
+    g.bias = bias;
+    g.out = output;
+    g.out_kind = kOutF32Planar;
+    g.img_stride = 0;
+    g.col_stride = hw;
+    g.row_offset = 0;
+    return launch_gemm(g, st);
+}
+
+}  // namespace
+
+int dav2cuda_project_tokens_half(float* output, const float* tokens, const float* weight, const float* bias,
+                                 uint32_t w, uint32_t h, uint32_t embedding, uint32_t output_channels,
+                                 uint32_t precision, void* workspace, uint64_t workspace_bytes, void* stream) {
+    REQUIRE(w && h && embedding && output_channels && (precision == 1 || precision == 2),
+            "invalid token projection dimensions");
+    REQUIRE(!null_any(output, tokens, weight, workspace), "project_tokens: null buffer");
+    REQUIRE(workspace_bytes >= dav2cuda_project_tokens_workspace_size(w, h, embedding, output_channels),
+            "project_tokens: workspace is too small");
+    return project_tokens_common(output, tokens, weight, nullptr, bias, w, h, embedding, output_channels,
+                                 precision == 1 ? kElemBF16 : kElemF16, workspace, workspace_bytes, as_stream(stream));
+}
+
+int dav2cuda_project_tokens_int8(float* output, const float* tokens, const uint32_t* int8_weight,
+                                 const float* weight_scales, const float* bias, uint32_t w, uint32_t h,
+                                 uint32_t embedding, uint32_t output_channels, void* workspace,
+                                 uint64_t workspace_bytes, void* stream) {
+    REQUIRE(w && h && embedding && output_channels && embedding % 4 == 0, "invalid token projection dimensions");
+    REQUIRE(!null_any(output, tokens, int8_weight, weight_scales, workspace), "project_tokens: null buffer");
+    REQUIRE(workspace_bytes >= dav2cuda_project_tokens_workspace_size(w, h, embedding, output_channels),
+            "project_tokens: workspace is too small");
+    return project_tokens_common(output, tokens, int8_weight, weight_scales, bias, w, h, embedding, output_channels,
+                                 kElemS8, workspace, workspace_bytes, as_stream(stream));
+}
+
+// VulkanOperators::conv_transpose_nonoverlap (src/operators.cpp:1807-1906)
+// with 16-bit operands: kernel == stride k, weight [Ci][Co][k][k], planar
+// f32 in [Ci][H][W] and out [Co][H*k][W*k].
+uint64_t dav2cuda_conv_transpose_half_workspace_size(uint32_t w, uint32_t h, uint32_t ic, uint32_t oc, uint32_t k) {
+    const uint64_t cp = ((uint64_t)ic + 7) / 8 * 8;
+    return align256((uint64_t)w * h * cp * 2) + align256((uint64_t)k * k * oc * cp * 2) +
+           align256((uint64_t)k * k * oc * 4) + 256;
+}
+
+int dav2cuda_conv_transpose_half(float* output, const float* input, const float* weight, const float* bias,
+                                 uint32_t w, uint32_t h, uint32_t ic, uint32_t oc, uint32_t k, uint32_t precision,
+                                 void* workspace, uint64_t workspace_bytes, void* stream) {
+    REQUIRE(w && h && ic && oc && k && (precision == 1 || precision == 2), "invalid transposed convolution");
+    REQUIRE(!null_any(output, input, weight, bias, workspace), "transposed convolution: null buffer");
+    REQUIRE(workspace_bytes >= dav2cuda_conv_transpose_half_workspace_size(w, h, ic, oc, k),
+            "transposed convolution: workspace is too small");
+    cudaStream_t st = as_stream(stream);
+    const uint32_t cp = round_up(ic, 8), wrows = k * k * oc;
+    const bool bf = precision == 1;
+    Carve ws(workspace, workspace_bytes);
+    void* a = ws.take<uint8_t>((uint64_t)w * h * cp * 2);
+    void* b = ws.take<uint8_t>((uint64_t)wrows * cp * 2);
+    float* bias_cols = ws.take<float>((uint64_t)wrows * 4);
+    int rc = bf ? launch_nchw_to_nhwc<__nv_bfloat16>(static_cast<__nv_bfloat16*>(a), input, 1, ic, h, w, cp, st)
+                : launch_nchw_to_nhwc<__half>(static_cast<__half*>(a), input, 1, ic, h, w, cp, st);
+    if (!rc)
+        rc = bf ? launch_half_weight<__nv_bfloat16>(static_cast<__nv_bfloat16*>(b), weight, 1, wrows, ic, cp, oc, k, ic,
+                                                    cp, st)
+                : launch_half_weight<__half>(static_cast<__half*>(b), weight, 1, wrows, ic, cp, oc, k, ic, cp, st);
+    if (!rc) rc = launch_expand_bias(bias_cols, bias, oc, k * k, st);
+    if (rc) return rc;
+    GemmArgs g;
+    g.elem = bf ? kElemBF16 : kElemF16;
+    g.a = a;
+    g.lda = cp;
+    g.b = b;
+    g.ldb = cp;
+    g.m = w * h;
+    g.n = wrows;
+    g.k = cp;
+    g.flags = kEpiBias;
+    g.bias = bias_cols;
+    g.out = output;
+    g.out_kind = kOutConvTF32;
+    g.convt_k = k;
+    g.convt_cout = oc;
+    g.convt_w = w;
+    g.convt_h = h;
+    return launch_gemm(g, st);
+}
+
+// BASELINE configuration 2(d): the reference's conv2d_int8 (3x3, pad 1;
+// src/operators.cpp:1735-1805) then bilinear_align_true 2x
+// (src/operators.cpp:1978-2012), batched. The input goes channels-last once
+// (f32), so the im2col quantizer reads each pixel's 256 channels as
+// contiguous 32-byte groups instead of gathering across planes; the weight
+// codes are permuted to the same (ky, kx, c) column order, which leaves each
+// row's scale, codes and integer dot products unchanged.
 uint64_t dav2cuda_conv3x3_int8_up2_workspace_size(uint32_t batch, uint32_t w, uint32_t h, uint32_t ic, uint32_t oc) {
     const uint32_t kp = round_up(ic * 9, 16);
     const uint64_t rows = (uint64_t)batch * w * h;
-    return align256(rows * kp) + align256(rows * 4) + align256((uint64_t)oc * kp) +
+    return align256(rows * ic * 4) + align256(rows * kp) + align256(rows * 4) + align256((uint64_t)oc * kp) +
            align256((uint64_t)batch * oc * w * h * 4) + 256;
 }
 
@@ -510,16 +750,15 @@ int dav2cuda_conv3x3_int8_up2(float* output, const float* input, const uint32_t*
     const uint32_t K = ic * 9, kp = round_up(K, 16);
     const uint64_t hw = (uint64_t)w * h, rows = batch * hw;
     Carve ws(workspace, workspace_bytes);
-    uint32_t* codes = ws.take<uint32_t>(rows * kp);
+    float* xt = ws.take<float>(rows * ic * 4);
+    uint8_t* codes = ws.take<uint8_t>(rows * kp);
     float* scales = ws.take<float>(rows * 4);
-    const void* wt = int8_weight;
-    if (kp != K) {
-        uint8_t* wp = ws.take<uint8_t>((uint64_t)oc * kp);
-        if (int rc = pad_byte_rows(wp, int8_weight, oc, K, kp, st)) return rc;
-        wt = wp;
-    }
+    uint8_t* wt = ws.take<uint8_t>((uint64_t)oc * kp);
     float* conv = ws.take<float>((uint64_t)batch * oc * hw * 4);
-    if (int rc = launch_im2col_quantize(codes, scales, input, batch, w, h, ic, w, h, 3, 1, 1, kp / 4, st)) return rc;
+    int rc = launch_nchw_to_nhwc<float>(xt, input, batch, ic, h, w, ic, st);
+    if (!rc) rc = launch_conv_codes_tap_major(wt, reinterpret_cast<const uint8_t*>(int8_weight), oc, ic, 9, K, kp, st);
+    if (!rc) rc = launch_im2col_quantize_nhwc<float>(codes, scales, xt, batch, h, w, ic, ic, 3, 1, 1, h, w, kp, st);
+    if (rc) return rc;
     GemmArgs g;
     g.elem = kElemS8;
     g.a = codes;
@@ -538,7 +777,7 @@ int dav2cuda_conv3x3_int8_up2(float* output, const float* input, const uint32_t*
     g.rows_per_img = (uint32_t)hw;
     g.img_stride = (uint64_t)oc * hw;
     g.col_stride = hw;
-    if (int rc = launch_gemm(g, st)) return rc;
+    if (int rc2 = launch_gemm(g, st)) return rc2;
     return launch_bilinear_align<float, float>(output, conv, w, h, 2 * w, 2 * h, batch * oc, st);
 }
 

@@ -158,7 +158,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     }
     // Thread-row epilogue with TMA stores: row-major outputs without row
     // remap (linear layers, 1x1 convolutions) or channels-last outputs of the
-    // implicit convolution with f16 operands; whole tiles along N, 16-byte
+    // implicit convolution with 16-bit operands; whole tiles along N, 16-byte
     // aligned rows; residuals in the output's layout.
     EpiMaps em;
     em.out = em.out2 = em.res1 = em.res2 = mb;  // placeholders when unused (never read)
@@ -166,7 +166,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     bool epi8 = false;
     p.tma_program = kTmaNone;
     const bool conv = g.a_mode != kAModeRows;
-    if (conv && g.elem == kElemF16 && bn == 32 && g.n == 32 && g.out_kind == kOutHeadF32 &&
+    if (conv && g.elem != kElemS8 && bn == 32 && g.n == 32 && g.out_kind == kOutHeadF32 &&
         (g.flags & ~uint32_t(kEpiMetricHead)) == (kEpiBias | kEpiHeadDot) &&
         reinterpret_cast<uintptr_t>(g.bias) % 16 == 0 && reinterpret_cast<uintptr_t>(g.head_w) % 16 == 0)
         p.tma_program = kTmaHeadDot;  // 8-warp kernel; needs no staging area, so the ring can be deeper
@@ -178,7 +178,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t st) {
     if (g.out_slot && p.tma_program != kTmaHeadDot)
         return set_error(DAV2CUDA_INVALID_ARGUMENT, "gemm: an output slot needs the output-head epilogue");
     if (p.tma_program == kTmaHeadDot || p.tma_program == kTmaHalfBiasCT) staging = 0;
-    if (p.tma_program == kTmaNone && (!conv || g.elem == kElemF16) && !p.rows_per_img &&
+    if (p.tma_program == kTmaNone && (!conv || g.elem != kElemS8) && !p.rows_per_img &&
         (g.out_kind == kOutF32Rows || g.out_kind == kOutHalfRows) && !(g.flags & kEpiHeadDot) &&
         ((g.flags & kEpiDequant) != 0) == (g.elem == kElemS8) && g.n % bn == 0) {
         const bool f32 = g.out_kind == kOutF32Rows;

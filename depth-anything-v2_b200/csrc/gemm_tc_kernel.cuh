@@ -1076,10 +1076,10 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
         if constexpr (AMODE == kAModeRows && EPI == 16)
             epilogue_ct_loop<BN, EPI, kInt8>(p, tmem_base, tfull, tempty, abort_flag, warp, lane);
     } else if (p.tma_program == kTmaHeadDot) {
-        if constexpr (BN == 32 && AMODE == kAModeConv3x3 && ELEM == kElemF16 && EPI == 8)
+        if constexpr (BN == 32 && AMODE == kAModeConv3x3 && ELEM != kElemS8 && EPI == 8)
             epilogue_head_loop<BN>(p, tmem_base, tfull, tempty, abort_flag, warp, lane);
     } else if (p.tma_program != kTmaNone) {
-        if constexpr (AMODE == kAModeRows || (AMODE == kAModeConv3x3 && ELEM == kElemF16 && EPI == 8))
+        if constexpr (AMODE == kAModeRows || (AMODE == kAModeConv3x3 && ELEM != kElemS8 && EPI == 8))
             epilogue_tma_dispatch<BN, EPI, AMODE, kInt8>(p, &em, tmem_base, tfull, tempty, rbars + 2u * (warp - 2u),
                                                          staging, abort_flag, warp, lane);
     } else if constexpr (EPI == 8) {

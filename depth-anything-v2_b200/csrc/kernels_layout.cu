@@ -13,6 +13,8 @@ template <>
 __device__ __forceinline__ __half cvt<__half>(float v) { return __float2half_rn(v); }
 template <>
 __device__ __forceinline__ __nv_bfloat16 cvt<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ float cvt<float>(float v) { return v; }
 
 // [B][C][H][W] f32 -> [B][H][W][Cp] half via a 32x32 shared-memory transpose
 // per (image, 32 channels, 32 pixels).
@@ -94,6 +96,23 @@ __global__ void conv_weight_kernel(H* __restrict__ out, const float* __restrict_
     }
 }
 
+// int8 convolution weight codes [Co][K] (K = Ci*k*k in the reference's
+// (ci, ky, kx) column order, rows k_in bytes apart) -> (ky, kx, ci) column
+// order with rows padded to kp bytes: the order of a channels-last im2col.
+// A permutation of each row's codes, so every dot product is unchanged.
+__global__ void conv_codes_tap_major_kernel(uint8_t* __restrict__ out, const uint8_t* __restrict__ in, uint32_t co,
+                                            uint32_t ci, uint32_t kk, uint32_t k_in, uint32_t kp) {
+    const uint64_t n = (uint64_t)co * kp;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint64_t o = i / kp;
+        const uint32_t col = (uint32_t)(i % kp);
+        uint8_t v = 0;
+        if (col < ci * kk) v = in[o * k_in + (uint64_t)(col % ci) * kk + col / ci];
+        out[i] = v;
+    }
+}
+
 unsigned grid_cap(uint64_t n) {
     const uint64_t g = (n + 255) / 256;
     return (unsigned)(g == 0 ? 1 : (g < 148 * 16 ? g : 148 * 16));
@@ -137,6 +156,15 @@ int launch_conv_weight_to_half(H* out, const float* w, uint32_t co, uint32_t ci,
     conv_weight_kernel<H><<<grid_cap((uint64_t)co * k * k * cip), 256, 0, st>>>(out, w, co, ci, k, cip);
     return check_launch("conv_weight");
 }
+
+int launch_conv_codes_tap_major(uint8_t* out, const uint8_t* in, uint32_t co, uint32_t ci, uint32_t kk, uint32_t k_in,
+                                uint32_t kp, cudaStream_t st) {
+    conv_codes_tap_major_kernel<<<grid_cap((uint64_t)co * kp), 256, 0, st>>>(out, in, co, ci, kk, k_in, kp);
+    return check_launch("conv_codes_tap_major");
+}
+
+template int launch_nchw_to_nhwc<float>(float*, const float*, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t,
+                                        cudaStream_t);
 
 #define DAV2_INST(H)                                                                                           \
     template int launch_nchw_to_nhwc<H>(H*, const float*, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t,    \

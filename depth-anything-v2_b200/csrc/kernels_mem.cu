@@ -6,6 +6,7 @@
 // reproduces.
 #include "kernels.cuh"
 
+#include <algorithm>
 #include <cfloat>
 
 namespace dav2cuda {
@@ -345,14 +346,20 @@ __device__ __forceinline__ float order_value(uint32_t k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-__global__ void minmax_init_kernel(uint32_t* keys) {
-    keys[0] = 0xffffffffu;  // +max key
-    keys[1] = 0u;           // -max key
+// Batched forms: image z (blockIdx.y of the reduction and normalization)
+// covers in[z*n, z*n + n) and owns range slots [2z, 2z + 1].
+__global__ void minmax_init_kernel(uint32_t* keys, uint32_t batch) {
+    const uint32_t z = blockIdx.x * blockDim.x + threadIdx.x;
+    if (z >= batch) return;
+    keys[2 * z] = 0xffffffffu;  // +max key
+    keys[2 * z + 1] = 0u;       // -max key
 }
 
 // reduce_minmax.glsl:10-33 as a grid-wide reduction: per-block warp
 // reductions, then order-preserving integer atomics on the two range slots.
 __global__ void minmax_reduce_kernel(uint32_t* keys, const float* __restrict__ in, uint64_t n) {
+    in += (uint64_t)blockIdx.y * n;
+    keys += 2u * blockIdx.y;
     float lo = INFINITY, hi = -INFINITY;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -368,16 +375,20 @@ __global__ void minmax_reduce_kernel(uint32_t* keys, const float* __restrict__ i
     }
 }
 
-__global__ void minmax_finish_kernel(uint32_t* keys) {
-    const float lo = order_value(keys[0]);
-    const float hi = order_value(keys[1]);
-    reinterpret_cast<float*>(keys)[0] = lo;
-    reinterpret_cast<float*>(keys)[1] = hi;
+__global__ void minmax_finish_kernel(uint32_t* keys, uint32_t batch) {
+    const uint32_t z = blockIdx.x * blockDim.x + threadIdx.x;
+    if (z >= batch) return;
+    const float lo = order_value(keys[2 * z]);
+    const float hi = order_value(keys[2 * z + 1]);
+    reinterpret_cast<float*>(keys)[2 * z] = lo;
+    reinterpret_cast<float*>(keys)[2 * z + 1] = hi;
 }
 
 // normalize_relative.glsl / normalize_metric.glsl (metric: maximum > 0).
 __global__ void normalize_kernel(float* __restrict__ d, const float* __restrict__ range, uint64_t n,
                                  float maximum) {
+    d += (uint64_t)blockIdx.y * n;
+    range += 2u * blockIdx.y;
     const float lo = range[0];
     const float span = (maximum > 0.0f ? maximum : range[1]) - lo;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -401,11 +412,16 @@ __constant__ float c_mean[3] = {0.485f, 0.456f, 0.406f};
 __constant__ float c_dev[3] = {0.229f, 0.224f, 0.225f};
 
 // preprocess_rgba.glsl:53-108 (per output pixel, 16 taps per channel).
+// Batched: image z = blockIdx.z reads px + z * img_stride and writes its own
+// three planes.
 __global__ void preprocess_u32_kernel(float* __restrict__ out, const uint32_t* __restrict__ px, uint32_t sw,
-                                      uint32_t sh, uint32_t stride, uint32_t rgba, uint32_t dw, uint32_t dh) {
+                                      uint32_t sh, uint32_t stride, uint32_t rgba, uint32_t dw, uint32_t dh,
+                                      uint64_t img_stride) {
     const uint32_t x = blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t y = blockIdx.y;
     if (x >= dw) return;
+    px += (uint64_t)blockIdx.z * img_stride;
+    out += (uint64_t)blockIdx.z * 3u * dw * dh;
     const float sx = ((float)x + 0.5f) * (float)sw / (float)dw - 0.5f;
     const float sy = ((float)y + 0.5f) * (float)sh / (float)dh - 0.5f;
     const int bx = (int)floorf(sx), by = (int)floorf(sy);
@@ -789,24 +805,44 @@ int launch_bilinear_align(TO* out, const TI* in, uint32_t iw, uint32_t ih, uint3
 template int launch_bilinear_align<float, float>(float*, const float*, uint32_t, uint32_t, uint32_t, uint32_t,
                                                  uint32_t, cudaStream_t);
 
-int launch_minmax(const float* in, float* range, uint64_t n, cudaStream_t st) {
-    uint32_t* keys = reinterpret_cast<uint32_t*>(range);
-    minmax_init_kernel<<<1, 1, 0, st>>>(keys);
-    minmax_reduce_kernel<<<grid_for(n), kBlock, 0, st>>>(keys, in, n);
-    minmax_finish_kernel<<<1, 1, 0, st>>>(keys);
+int launch_minmax_batched(const float* in, float* ranges, uint64_t n, uint32_t batch, cudaStream_t st) {
+    if (batch == 0 || batch > 65535) return set_error(DAV2CUDA_INVALID_ARGUMENT, "reduce_minmax: batch out of range");
+    uint32_t* keys = reinterpret_cast<uint32_t*>(ranges);
+    minmax_init_kernel<<<(batch + 127) / 128, 128, 0, st>>>(keys, batch);
+    const unsigned gx = (unsigned)std::max<uint64_t>(1, grid_for(n) / batch);
+    minmax_reduce_kernel<<<dim3(gx, batch), kBlock, 0, st>>>(keys, in, n);
+    minmax_finish_kernel<<<(batch + 127) / 128, 128, 0, st>>>(keys, batch);
     return check_launch("reduce_minmax");
 }
 
-int launch_normalize(float* d, const float* range, uint64_t n, float maximum, cudaStream_t st) {
-    normalize_kernel<<<grid_for(n), kBlock, 0, st>>>(d, range, n, maximum);
+int launch_minmax(const float* in, float* range, uint64_t n, cudaStream_t st) {
+    return launch_minmax_batched(in, range, n, 1, st);
+}
+
+int launch_normalize_batched(float* d, const float* ranges, uint64_t n, uint32_t batch, float maximum,
+                             cudaStream_t st) {
+    if (batch == 0 || batch > 65535) return set_error(DAV2CUDA_INVALID_ARGUMENT, "normalize: batch out of range");
+    const unsigned gx = (unsigned)std::max<uint64_t>(1, grid_for(n) / batch);
+    normalize_kernel<<<dim3(gx, batch), kBlock, 0, st>>>(d, ranges, n, maximum);
     return check_launch("normalize");
+}
+
+int launch_normalize(float* d, const float* range, uint64_t n, float maximum, cudaStream_t st) {
+    return launch_normalize_batched(d, range, n, 1, maximum, st);
+}
+
+int launch_preprocess_u32_batched(float* out, const uint32_t* px, uint32_t batch, uint32_t sw, uint32_t sh,
+                                  uint32_t stride, uint64_t img_stride, uint32_t rgba, uint32_t dw, uint32_t dh,
+                                  cudaStream_t st) {
+    if (batch == 0 || batch > 65535) return set_error(DAV2CUDA_INVALID_ARGUMENT, "preprocess_u32: batch out of range");
+    dim3 grid((dw + 127) / 128, dh, batch);
+    preprocess_u32_kernel<<<grid, 128, 0, st>>>(out, px, sw, sh, stride, rgba, dw, dh, img_stride);
+    return check_launch("preprocess_u32");
 }
 
 int launch_preprocess_u32(float* out, const uint32_t* px, uint32_t sw, uint32_t sh, uint32_t stride,
                           uint32_t rgba, uint32_t dw, uint32_t dh, cudaStream_t st) {
-    dim3 grid((dw + 127) / 128, dh);
-    preprocess_u32_kernel<<<grid, 128, 0, st>>>(out, px, sw, sh, stride, rgba, dw, dh);
-    return check_launch("preprocess_u32");
+    return launch_preprocess_u32_batched(out, px, 1, sw, sh, stride, 0, rgba, dw, dh, st);
 }
 
 int launch_preprocess_bgr8(float* out, const uint8_t* bgr, uint32_t batch, uint32_t sw, uint32_t sh,

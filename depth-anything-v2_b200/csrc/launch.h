@@ -49,8 +49,16 @@ int launch_bilinear_align(TO* out, const TI* in, uint32_t iw, uint32_t ih, uint3
                           uint32_t planes, cudaStream_t st);
 int launch_minmax(const float* in, float* range, uint64_t n, cudaStream_t st);
 int launch_normalize(float* d, const float* range, uint64_t n, float maximum, cudaStream_t st);
+// Per-image forms over `batch` images of n values each: ranges [batch][2].
+int launch_minmax_batched(const float* in, float* ranges, uint64_t n, uint32_t batch, cudaStream_t st);
+int launch_normalize_batched(float* d, const float* ranges, uint64_t n, uint32_t batch, float maximum,
+                             cudaStream_t st);
 int launch_preprocess_u32(float* out, const uint32_t* px, uint32_t sw, uint32_t sh, uint32_t stride,
                           uint32_t rgba, uint32_t dw, uint32_t dh, cudaStream_t st);
+// `batch` packed-pixel images img_stride pixels apart -> planar [batch][3][dh][dw].
+int launch_preprocess_u32_batched(float* out, const uint32_t* px, uint32_t batch, uint32_t sw, uint32_t sh,
+                                  uint32_t stride, uint64_t img_stride, uint32_t rgba, uint32_t dw, uint32_t dh,
+                                  cudaStream_t st);
 int launch_preprocess_bgr8(float* out, const uint8_t* bgr, uint32_t batch, uint32_t sw, uint32_t sh,
                            uint64_t row_stride, uint64_t img_stride, uint32_t dw, uint32_t dh, int bilinear,
                            cudaStream_t st);
@@ -63,11 +71,15 @@ int launch_im2col_quantize(uint32_t* packed, float* scales, const float* in, uin
                            uint32_t out_words, cudaStream_t st);
 
 // --------------------------------------------------------- layout helpers
-// planar f32 [B][C][H][W] -> channels-last half [B][H][W][Cp] (channels
-// beyond C are zero).
+// planar f32 [B][C][H][W] -> channels-last [B][H][W][Cp] half or f32
+// (channels beyond C are zero).
 template <typename H>
 int launch_nchw_to_nhwc(H* out, const float* in, uint32_t batch, uint32_t c, uint32_t h, uint32_t w,
                         uint32_t cp, cudaStream_t st);
+// int8 convolution weight codes [Co][Ci*k*k] ((ci, ky, kx) columns, rows k_in
+// bytes apart) -> (ky, kx, ci) columns, rows padded to kp bytes.
+int launch_conv_codes_tap_major(uint8_t* out, const uint8_t* in, uint32_t co, uint32_t ci, uint32_t kk, uint32_t k_in,
+                                uint32_t kp, cudaStream_t st);
 // f32 -> half (elementwise, any count).
 template <typename H>
 int launch_to_half(H* out, const float* in, uint64_t n, cudaStream_t st);

@@ -134,6 +134,7 @@ public:
         if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0) throw_no_device("no CUDA device is available");
         if (device < 0 || device >= count) throw std::invalid_argument("CUDA device index out of range");
         int8_ = (flags & DAV2_CREATE_FORCE_INT8) != 0;
+        bf16_ = (flags & DAV2_CREATE_FORCE_BF16) != 0;
         cuda_check(cudaSetDevice(device_), "cudaSetDevice");
         cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
         cuda_check(cudaEventCreateWithFlags(&done_, cudaEventDisableTiming), "cudaEventCreate");
@@ -178,63 +179,27 @@ public:
     void infer_bgr8(const uint8_t* bgr, int batch, int w, int h, std::ptrdiff_t row_stride,
                     std::ptrdiff_t image_stride, int input_size, float* depth, bool device_memory,
                     void* user_stream) override {
-        if (!bgr || !depth || batch <= 0 || w <= 0 || h <= 0 || row_stride < std::ptrdiff_t(w) * 3 ||
-            (batch > 1 && image_stride < row_stride * h))
-            throw std::invalid_argument("invalid source image");
-        const ImageShape s = network_shape(w, h, input_size);
-        std::lock_guard<std::mutex> lock(mutex_);
-        cuda_check(cudaSetDevice(device_), "cudaSetDevice");
-        poll_device_error();
-        Plan& p = plan(batch, s.width, s.height);
-        cudaStream_t st = user_stream ? static_cast<cudaStream_t>(user_stream) : stream_;
-        order_after_previous_call(st);
-        const uint64_t img_bytes = uint64_t(image_stride > 0 ? image_stride : row_stride * h);
-        const uint64_t in_bytes = img_bytes * (batch - 1) + uint64_t(row_stride) * (h - 1) + uint64_t(w) * 3;
-        const uint8_t* dbgr = bgr;
-        const bool pinned_in = !device_memory && is_pinned(bgr);
-        const bool pinned_out = !device_memory && is_pinned(depth);
-        if (!device_memory) {
-            ensure_staging(in_bytes);
-            ensure_host(pinned_in ? 0 : in_bytes, pinned_out ? 0 : uint64_t(batch) * w * h * 4);
-            const void* src = bgr;
-            if (!pinned_in) {
-                std::memcpy(host_in_, bgr, in_bytes);
-                src = host_in_;
-            }
-            cuda_check(cudaMemcpyAsync(staging_, src, in_bytes, cudaMemcpyHostToDevice, st), "H2D");
-            upload_bytes_ += in_bytes;
-            dbgr = staging_;
-        }
-        const bool resize = w != s.width || h != s.height;
-        // The graph's last convolution writes where the plan's slot points:
-        // straight into the caller's device buffer when no resize follows.
-        float* graph_out = device_memory && !resize ? depth : p.depth;
-        op(launch_store_pointer(reinterpret_cast<void**>(p.depth_slot), graph_out, st), "store_pointer");
-        op(launch_preprocess_bgr8(p.image, dbgr, batch, w, h, row_stride, img_bytes, s.width, s.height, 0, st),
-           "preprocess_bgr8");
-        launches_ += 2;
-        launch_plan(p, st);
-        float* result = graph_out;
-        if (resize) {
-            float* target = device_memory ? depth : resized_buffer(uint64_t(batch) * w * h);
-            op(launch_bilinear_align<float, float>(target, p.depth, s.width, s.height, w, h, batch, st),
-               "resize depth");
-            ++launches_;
-            result = target;
-        }
-        const uint64_t out_bytes = uint64_t(batch) * w * h * 4;
-        if (!device_memory) {
-            cuda_check(cudaMemcpyAsync(pinned_out ? static_cast<void*>(depth) : host_out_, result, out_bytes,
-                                       cudaMemcpyDeviceToHost, st),
-                       "D2H");
-            download_bytes_ += out_bytes;
-        }
-        queue_error_read(st);
-        finish_call(st);
-        if (device_memory && user_stream) return;  // asynchronous: checked at the next call or dav2_synchronize
-        cuda_check(cudaStreamSynchronize(st), "sync");
-        if (!device_memory && !pinned_out) std::memcpy(depth, host_out_, out_bytes);
-        raise_device_error();
+        ImagesCall c{bgr, batch, w, h, row_stride, image_stride, {}, Source::kBgr8Bicubic, false, false,
+                     depth, device_memory, user_stream};
+        if (w > 0 && h > 0) c.net = network_shape(w, h, input_size);
+        run_images(c);
+    }
+
+    void infer_frames_bgr8(const uint8_t* bgr, int batch, int w, int h, std::ptrdiff_t row_stride,
+                           std::ptrdiff_t image_stride, int network_size, float* depth, void* stream) override {
+        if (network_size <= 0 || network_size % 14)
+            throw std::invalid_argument("network size must be a positive multiple of 14");
+        ImagesCall c{bgr, batch, w, h, row_stride, image_stride, {network_size, network_size}, Source::kBgr8Bilinear,
+                     false, false, depth, true, stream};
+        run_images(c);
+    }
+
+    void submit_pixels(const uint8_t* pixels, int batch, int w, int h, std::ptrdiff_t row_stride,
+                       std::ptrdiff_t image_stride, bool rgba, int input_size, float* output, void* stream) override {
+        ImagesCall c{pixels, batch, w, h, row_stride, image_stride, {}, Source::kPixels32, rgba, true, output, true,
+                     stream};
+        if (w > 0 && h > 0) c.net = network_shape(w, h, input_size);
+        run_images(c);
     }
 
     void probe_block(int batch, int w, int h, int block, const float* x_in, float* x_out, int8_t* codes,
@@ -315,6 +280,110 @@ public:
     float metric_max_depth() const override { return model_.metric_max_depth(); }
 
 private:
+    // ------------------------------------------------------------- images
+    // Image entry points: packed 8-bit images (host or device memory) ->
+    // GPU preprocessing to the network shape -> graph -> optional per-image
+    // min/max normalization -> depth at the source size (resized on the
+    // device when the network shape differs).
+    enum class Source {
+        kBgr8Bicubic,   // BGR8, OpenCV-exact bicubic (dav2_infer_bgr8, src/image.cpp:163-269)
+        kBgr8Bilinear,  // BGR8, bilinear half-pixel to a square network input (video frames)
+        kPixels32,      // BGRA8 / RGBA8 words, bicubic (preprocess_rgba.glsl; the GPU submit path)
+    };
+    struct ImagesCall {
+        const uint8_t* pixels;
+        int batch, w, h;
+        std::ptrdiff_t row_stride, image_stride;
+        ImageShape net;
+        Source source;
+        bool rgba;       // kPixels32 channel order
+        bool normalize;  // min/max normalization at the network shape (submit path)
+        float* out;
+        bool device_memory;
+        void* stream;
+    };
+
+    void run_images(const ImagesCall& c) {
+        const std::ptrdiff_t bpp = c.source == Source::kPixels32 ? 4 : 3;
+        if (!c.pixels || !c.out || c.batch <= 0 || c.w <= 0 || c.h <= 0 || c.row_stride < std::ptrdiff_t(c.w) * bpp ||
+            (c.batch > 1 && c.image_stride < c.row_stride * c.h) ||
+            (bpp == 4 && (c.row_stride % 4 || c.image_stride % 4)))
+            throw std::invalid_argument("invalid source image");
+        const ImageShape s = c.net;
+        std::lock_guard<std::mutex> lock(mutex_);
+        cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+        poll_device_error();
+        Plan& p = plan(c.batch, s.width, s.height);
+        cudaStream_t st = c.stream ? static_cast<cudaStream_t>(c.stream) : stream_;
+        order_after_previous_call(st);
+        const int batch = c.batch, w = c.w, h = c.h;
+        const uint64_t img_bytes = uint64_t(c.image_stride > 0 ? c.image_stride : c.row_stride * h);
+        const uint64_t in_bytes = img_bytes * (batch - 1) + uint64_t(c.row_stride) * (h - 1) + uint64_t(w) * bpp;
+        const uint8_t* src_dev = c.pixels;
+        const bool pinned_in = !c.device_memory && is_pinned(c.pixels);
+        const bool pinned_out = !c.device_memory && is_pinned(c.out);
+        if (!c.device_memory) {
+            ensure_staging(in_bytes);
+            ensure_host(pinned_in ? 0 : in_bytes, pinned_out ? 0 : uint64_t(batch) * w * h * 4);
+            const void* src = c.pixels;
+            if (!pinned_in) {
+                std::memcpy(host_in_, c.pixels, in_bytes);
+                src = host_in_;
+            }
+            cuda_check(cudaMemcpyAsync(staging_, src, in_bytes, cudaMemcpyHostToDevice, st), "H2D");
+            upload_bytes_ += in_bytes;
+            src_dev = staging_;
+        }
+        const bool resize = w != s.width || h != s.height;
+        // The graph's last convolution writes where the plan's slot points:
+        // straight into the caller's device buffer when no resize follows.
+        float* graph_out = c.device_memory && !resize ? c.out : p.depth;
+        op(launch_store_pointer(reinterpret_cast<void**>(p.depth_slot), graph_out, st), "store_pointer");
+        if (c.source == Source::kPixels32)
+            op(launch_preprocess_u32_batched(p.image, reinterpret_cast<const uint32_t*>(src_dev), batch, w, h,
+                                             uint32_t(c.row_stride / 4), img_bytes / 4, c.rgba ? 1u : 0u, s.width,
+                                             s.height, st),
+               "preprocess_u32");
+        else
+            op(launch_preprocess_bgr8(p.image, src_dev, batch, w, h, c.row_stride, img_bytes, s.width, s.height,
+                                      c.source == Source::kBgr8Bilinear ? 1 : 0, st),
+               "preprocess_bgr8");
+        launches_ += 2;
+        launch_plan(p, st);
+        if (c.normalize) {
+            // src/vulkan_executor.cpp:763-786: min/max at the network resolution,
+            // relative [0,1] or the metric 25 m presentation span, then the
+            // (convex) bilinear expansion below
+            const uint64_t n = uint64_t(s.width) * s.height;
+            op(launch_minmax_batched(graph_out, p.range, n, batch, st), "reduce_minmax");
+            op(launch_normalize_batched(graph_out, p.range, n, batch, model_.metric_max_depth() > 0 ? 25.0f : 0.0f,
+                                        st),
+               "normalize");
+            launches_ += 4;
+        }
+        float* result = graph_out;
+        if (resize) {
+            float* target = c.device_memory ? c.out : resized_buffer(uint64_t(batch) * w * h);
+            op(launch_bilinear_align<float, float>(target, p.depth, s.width, s.height, w, h, batch, st),
+               "resize depth");
+            ++launches_;
+            result = target;
+        }
+        const uint64_t out_bytes = uint64_t(batch) * w * h * 4;
+        if (!c.device_memory) {
+            cuda_check(cudaMemcpyAsync(pinned_out ? static_cast<void*>(c.out) : host_out_, result, out_bytes,
+                                       cudaMemcpyDeviceToHost, st),
+                       "D2H");
+            download_bytes_ += out_bytes;
+        }
+        queue_error_read(st);
+        finish_call(st);
+        if (c.device_memory && c.stream) return;  // asynchronous: checked at the next call or dav2_synchronize
+        cuda_check(cudaStreamSynchronize(st), "sync");
+        if (!c.device_memory && !pinned_out) std::memcpy(c.out, host_out_, out_bytes);
+        raise_device_error();
+    }
+
     // ------------------------------------------------------------ weights
     const TensorView& t(const std::string& name) const { return model_.tensor(name); }
 
@@ -343,7 +412,7 @@ private:
             L.w = wa_.take<uint8_t>(uint64_t(n) * kp);
             L.s = wa_.take<float>(uint64_t(n) * 4);
         } else {
-            L.w = wa_.take<__half>(uint64_t(n) * kp * 2);
+            L.w = wa_.take<uint16_t>(uint64_t(n) * kp * 2);
         }
         if (!bname.empty()) L.b = kind == 1 ? wa_.take<float>(uint64_t(n) * 4) : f32(bname);
         const float* src = stage(wname);
@@ -352,8 +421,10 @@ private:
                 op(launch_pack_weight_s8(static_cast<uint8_t*>(L.w), L.s, src, kind, n, K, kp, co, k, ci, nullptr),
                    "pack_weight_s8");
             else
-                op(launch_half_weight<__half>(static_cast<__half*>(L.w), src, kind, n, K, kp, co, k, ci, cip,
-                                              nullptr),
+                op(bf16_ ? launch_half_weight<__nv_bfloat16>(static_cast<__nv_bfloat16*>(L.w), src, kind, n, K, kp, co,
+                                                             k, ci, cip, nullptr)
+                         : launch_half_weight<__half>(static_cast<__half*>(L.w), src, kind, n, K, kp, co, k, ci, cip,
+                                                      nullptr),
                    "half_weight");
             if (kind == 1 && L.b) {
                 const float* b = f32(bname);
@@ -456,6 +527,7 @@ private:
         float* image = nullptr;   // [B][3][H][W]
         float* depth = nullptr;   // [B][H][W]
         float** depth_slot = nullptr;  // destination of the graph's last convolution
+        float* range = nullptr;        // [B][2] per-image depth min/max (normalizing entry points)
         float* pos = nullptr;     // [hw][D]
         void* patch_a = nullptr;  // int8 [B*hw][592] or f16
         float* patch_s = nullptr;
@@ -494,6 +566,7 @@ private:
         p.image = A.take<float>(B * 3 * p.H * p.W * 4);
         p.depth = A.take<float>(B * p.H * p.W * 4);
         p.depth_slot = A.take<float*>(sizeof(float*));
+        p.range = A.take<float>(B * 2 * 4);
         p.pos = A.take<float>(uint64_t(p.hw) * D * 4);
         p.patch_a = A.take<uint8_t>(PH * 592 * (q ? 1 : 2));
         if (q) p.patch_s = A.take<float>(PH * 4);
@@ -669,9 +742,30 @@ private:
     }
 
     // ---------------------------------------------------------- the graph
+    // 16-bit launches in the context's 16-bit type (f16, or bf16 when bf16_).
+    int half_ln() const { return bf16_ ? kLnOutBF16 : kLnOutF16; }
+    int bilinear16(void* out, const void* in, uint32_t B, uint32_t ih, uint32_t iw, uint32_t oh, uint32_t ow,
+                   uint32_t c, cudaStream_t st) const {
+        if (bf16_)
+            return launch_bilinear_nhwc<__nv_bfloat16>(static_cast<__nv_bfloat16*>(out),
+                                                       static_cast<const __nv_bfloat16*>(in), B, ih, iw, oh, ow, c, st);
+        return launch_bilinear_nhwc<__half>(static_cast<__half*>(out), static_cast<const __half*>(in), B, ih, iw, oh, ow,
+                                            c, st);
+    }
+    int im2col_nhwc16(void* out, const void* in, uint32_t B, uint32_t h, uint32_t w, uint32_t c, uint32_t k,
+                      uint32_t s, uint32_t pad, uint32_t oh, uint32_t ow, uint32_t kp, cudaStream_t st) const {
+        if (bf16_)
+            return launch_im2col_nhwc<__nv_bfloat16>(static_cast<__nv_bfloat16*>(out),
+                                                     static_cast<const __nv_bfloat16*>(in), B, h, w, c, k, s, pad, oh,
+                                                     ow, kp, st);
+        return launch_im2col_nhwc<__half>(static_cast<__half*>(out), static_cast<const __half*>(in), B, h, w, c, k, s,
+                                          pad, oh, ow, kp, st);
+    }
+
     GemmArgs gemm(const Linear& L, const void* a, uint64_t lda, uint32_t m, bool int8_operands) const {
         GemmArgs g;
-        g.elem = int8_operands ? kElemS8 : kElemF16;
+        g.elem = int8_operands ? kElemS8 : bf16_ ? kElemBF16 : kElemF16;
+        g.out_half_bf16 = bf16_;  // 16-bit outputs in the 16-bit operand type
         g.a = a;
         g.lda = lda;
         g.b = L.w;
@@ -722,8 +816,11 @@ private:
                                       p.ph, 14, 14, 0, 592 / 4, st),
                "patch im2col_quantize");
         else
-            step(st, launch_patch_im2col<__half>(static_cast<__half*>(p.patch_a), p.image, B, p.H, p.W, 592, st),
-               "patch im2col");
+            step(st,
+                 bf16_ ? launch_patch_im2col<__nv_bfloat16>(static_cast<__nv_bfloat16*>(p.patch_a), p.image, B, p.H,
+                                                            p.W, 592, st)
+                       : launch_patch_im2col<__half>(static_cast<__half*>(p.patch_a), p.image, B, p.H, p.W, 592, st),
+                 "patch im2col");
         GemmArgs g = gemm(patch_, p.patch_a, 592, PH, q);
         g.s_in = p.patch_s;
         g.flags |= kEpiResidual1;
@@ -741,7 +838,7 @@ private:
     void enqueue_ln1(Plan& p, uint32_t i, cudaStream_t st) {
         const Block& b = blocks_[i];
         step(st, launch_layer_norm(p.xn, p.xn_s, p.x, b.ln1_w, b.ln1_b, p.B * p.T, arch_.d, 1e-6f,
-                                   int8_ ? kLnOutS8 : kLnOutF16, 1, 1, 0, st),
+                                   int8_ ? kLnOutS8 : half_ln(), 1, 1, 0, st),
              "ln1");
     }
 
@@ -764,7 +861,7 @@ private:
         // int8 path: attention output and GELU hidden stay f32 up to their
         // quantizers, as the reference's int8 mode keeps them
         // (src/operators.cpp:1098-1209 writes f32; src/encoder.cpp:526-528)
-        step(st, launch_attention_tc(p.att, q, p.qkv, false, B, p.T, a.heads, 3 * D, D, st), "attention");
+        step(st, launch_attention_tc(p.att, q, p.qkv, bf16_, B, p.T, a.heads, 3 * D, D, st), "attention");
         const void* att_in = p.att;
         if (q) {
             step(st, launch_quantize_rows<float>(static_cast<uint32_t*>(p.att_q), p.att_s,
@@ -783,7 +880,7 @@ private:
             g.ldo = D;
             step(st, launch_gemm(g, st), "proj");
         }
-        step(st, launch_layer_norm(p.xn, p.xn_s, p.x, b.ln2_w, b.ln2_b, R, D, 1e-6f, q ? kLnOutS8 : kLnOutF16, 1, 1, 0,
+        step(st, launch_layer_norm(p.xn, p.xn_s, p.x, b.ln2_w, b.ln2_b, R, D, 1e-6f, q ? kLnOutS8 : half_ln(), 1, 1, 0,
                              st),
            "ln2");
         {
@@ -818,7 +915,7 @@ private:
     // pretrained.norm of tap k on the patch rows only (cls dropped)
     void enqueue_tap(Plan& p, int k, cudaStream_t st) {
         step(st, launch_layer_norm(p.taps[k], p.taps_s[k], p.x, norm_w_, norm_b_, p.B * p.hw, arch_.d, 1e-6f,
-                                   int8_ ? kLnOutS8 : kLnOutF16, p.hw, p.T, 1, st),
+                                   int8_ ? kLnOutS8 : half_ln(), p.hw, p.T, 1, st),
              "tap norm");
     }
 
@@ -879,7 +976,7 @@ private:
                 g = gemm(resize_[3], p.r3_col, 9 * oc, rows, true);
                 g.s_in = p.r3_s;
             } else {
-                step(st, launch_im2col_nhwc<__half>(static_cast<__half*>(p.r3_col), p.proj[3], B, p.ph, p.pw, cp_[3], 3, 2, 1,
+                step(st, im2col_nhwc16(p.r3_col, p.proj[3], B, p.ph, p.pw, cp_[3], 3, 2, 1,
                                               p.lh[3], p.lw[3], 9 * cp_[3], st),
                    "resize3 im2col");
                 g = gemm(resize_[3], p.r3_col, 9 * cp_[3], rows, false);
@@ -942,7 +1039,7 @@ private:
             step(st, launch_gemm(g4, st), "rcu2.conv2");
             const uint32_t oh = r > 0 ? p.lh[r - 1] : 2 * p.lh[0];
             const uint32_t ow = r > 0 ? p.lw[r - 1] : 2 * p.lw[0];
-            step(st, launch_bilinear_nhwc<__half>(p.upb, p.y, B, h, w, oh, ow, F, st), "fusion resize");
+            step(st, bilinear16(p.upb, p.y, B, h, w, oh, ow, F, st), "fusion resize");
             GemmArgs g5 = gemm(rf.out, p.upb, F, B * oh * ow, false);
             g5.out = p.path[pi];
             g5.out_kind = kOutHalfRows;
@@ -960,7 +1057,7 @@ private:
             g.ldo = cp_half_;
             step(st, launch_gemm(g, st), "output_conv1");
         }
-        step(st, launch_bilinear_nhwc<__half>(p.full, p.oc1, B, h1, w1, p.H, p.W, cp_half_, st), "head resize");
+        step(st, bilinear16(p.full, p.oc1, B, h1, w1, p.H, p.W, cp_half_, st), "head resize");
         {
             GemmArgs g = conv3x3(out_conv2_, p.full, B, p.H, p.W, cp_half_);
             g.flags |= kEpiHeadDot | (model_.metric_max_depth() > 0 ? kEpiMetricHead : 0u);
@@ -1087,6 +1184,7 @@ private:
     int device_;
     Arch arch_;
     bool int8_ = false;
+    bool bf16_ = false;  // 16-bit operands and activations bf16 instead of f16 (not with int8_)
     cudaStream_t stream_ = nullptr;
     cudaEvent_t done_ = nullptr;       // end of the last call's work (on last_stream_)
     cudaStream_t last_stream_ = nullptr;

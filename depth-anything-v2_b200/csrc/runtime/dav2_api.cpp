@@ -126,9 +126,11 @@ DAV2_API dav2_status DAV2_CALL dav2_create(const char* path, const dav2_create_o
     if (!supported_encoder(options->encoder)) return fail(DAV2_STATUS_INVALID_ARGUMENT, "unsupported encoder");
     constexpr uint32_t supported = DAV2_CREATE_FORCE_FP32 | DAV2_CREATE_FORCE_FP32_WEIGHTS |
                                    DAV2_CREATE_FORCE_FP32_ATTENTION | DAV2_CREATE_FORCE_FP16 |
-                                   DAV2_CREATE_FORCE_INT8 | DAV2_CREATE_FORCE_METAL | DAV2_CREATE_FORCE_VULKAN;
+                                   DAV2_CREATE_FORCE_INT8 | DAV2_CREATE_FORCE_METAL | DAV2_CREATE_FORCE_VULKAN |
+                                   DAV2_CREATE_FORCE_BF16;
     if (options->flags & ~supported) return fail(DAV2_STATUS_INVALID_ARGUMENT, "unsupported create flags");
-    const uint32_t prec = options->flags & (DAV2_CREATE_FORCE_FP32 | DAV2_CREATE_FORCE_FP16 | DAV2_CREATE_FORCE_INT8);
+    const uint32_t prec = options->flags & (DAV2_CREATE_FORCE_FP32 | DAV2_CREATE_FORCE_FP16 | DAV2_CREATE_FORCE_INT8 |
+                                            DAV2_CREATE_FORCE_BF16);
     if (prec && (prec & (prec - 1)))
         return fail(DAV2_STATUS_INVALID_ARGUMENT, "multiple DAV2 execution precisions were requested");
     return protect([&] {
@@ -296,6 +298,31 @@ DAV2_API dav2_status DAV2_CALL dav2_infer_device_bgr8_batch(dav2_context* contex
     return protect([&] {
         dav2::network_shape(w, h, input_size);
         context->executor->infer_bgr8(bgr, int(batch), w, h, stride, image_stride, input_size, depth, true, stream);
+    });
+}
+
+DAV2_API dav2_status DAV2_CALL dav2_infer_device_frames_bgr8(dav2_context* context, const uint8_t* bgr, uint32_t batch,
+                                                             int32_t w, int32_t h, ptrdiff_t stride,
+                                                             ptrdiff_t image_stride, int32_t network_size,
+                                                             float* depth, void* stream) {
+    if (!context || !bgr || !depth || batch == 0) return fail(DAV2_STATUS_INVALID_ARGUMENT, "null inference argument");
+    return protect([&] {
+        context->executor->infer_frames_bgr8(bgr, int(batch), w, h, stride, image_stride, network_size, depth, stream);
+    });
+}
+
+DAV2_API dav2_status DAV2_CALL dav2_submit_device_pixels(dav2_context* context, const uint8_t* pixels, uint32_t batch,
+                                                         int32_t w, int32_t h, ptrdiff_t stride, ptrdiff_t image_stride,
+                                                         dav2_gpu_pixel_format format, int32_t input_size,
+                                                         float* output, void* stream) {
+    if (!context || !pixels || !output || batch == 0)
+        return fail(DAV2_STATUS_INVALID_ARGUMENT, "null submit argument");
+    if (format != DAV2_GPU_PIXEL_BGRA8 && format != DAV2_GPU_PIXEL_RGBA8)
+        return fail(DAV2_STATUS_INVALID_ARGUMENT, "unsupported pixel format");
+    return protect([&] {
+        dav2::network_shape(w, h, input_size);
+        context->executor->submit_pixels(pixels, int(batch), w, h, stride, image_stride, format == DAV2_GPU_PIXEL_RGBA8,
+                                         input_size, output, stream);
     });
 }
 

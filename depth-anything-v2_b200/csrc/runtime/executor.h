@@ -42,6 +42,17 @@ public:
     virtual void infer_bgr8(const std::uint8_t* bgr, int batch, int width, int height, std::ptrdiff_t row_stride,
                             std::ptrdiff_t image_stride, int input_size, float* depth, bool device_memory,
                             void* stream) = 0;
+    // Video frames (device memory): BGR8 -> bilinear (half-pixel) to a square
+    // network_size input -> graph -> depth resized to the frame size.
+    virtual void infer_frames_bgr8(const std::uint8_t* bgr, int batch, int width, int height,
+                                   std::ptrdiff_t row_stride, std::ptrdiff_t image_stride, int network_size,
+                                   float* depth, void* stream) = 0;
+    // The headless GPU submit path (src/vulkan_executor.cpp:656-812 without
+    // graphics interop): packed BGRA8/RGBA8 device images -> bicubic ->
+    // graph -> per-image min/max normalization -> output at the image size.
+    virtual void submit_pixels(const std::uint8_t* pixels, int batch, int width, int height,
+                               std::ptrdiff_t row_stride, std::ptrdiff_t image_stride, bool rgba, int input_size,
+                               float* output, void* stream) = 0;
     virtual void synchronize() = 0;
     // Kernels this executor has launched (graph kernel nodes per replay included).
     virtual std::uint64_t kernel_launches() const = 0;

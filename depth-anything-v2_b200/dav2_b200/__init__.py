@@ -56,6 +56,14 @@ DAV2CUDA = {
     "dav2cuda_conv_transpose_int8": (ctypes.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, u64, vp]),
     "dav2cuda_conv3x3_int8_up2_workspace_size": (u64, [u32, u32, u32, u32, u32]),
     "dav2cuda_conv3x3_int8_up2": (ctypes.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, u64, vp]),
+    "dav2cuda_prepare_tokens_workspace_size": (u64, [u32, u32, u32]),
+    "dav2cuda_prepare_tokens_half": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, vp, u64, vp]),
+    "dav2cuda_prepare_tokens_int8": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, vp, u64, vp]),
+    "dav2cuda_project_tokens_workspace_size": (u64, [u32, u32, u32, u32]),
+    "dav2cuda_project_tokens_half": (ctypes.c_int, [vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, u64, vp]),
+    "dav2cuda_project_tokens_int8": (ctypes.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, vp, u64, vp]),
+    "dav2cuda_conv_transpose_half_workspace_size": (u64, [u32, u32, u32, u32, u32]),
+    "dav2cuda_conv_transpose_half": (ctypes.c_int, [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, vp, u64, vp]),
     "dav2cuda_attention_head64": (ctypes.c_int, [vp, vp, u32, u32, u32, vp, u64, vp]),
     "dav2cuda_attention_head64_workspace_size": (u64, [u32, u32, u32]),
     "dav2cuda_linear_half_workspace_size": (u64, [u32, u32, u32]),

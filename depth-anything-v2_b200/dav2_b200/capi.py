@@ -34,7 +34,7 @@ class TransferCounters(ctypes.Structure):
 ABI_VERSION = 1
 ENCODERS = {"vits": 0, "vitb": 1, "vitl": 2}
 FLAGS = {"fp32": 1 << 0, "fp32_weights": 1 << 1, "fp32_attention": 1 << 2, "fp16": 1 << 3, "int8": 1 << 4,
-         "metal": 1 << 5, "vulkan": 1 << 6}
+         "metal": 1 << 5, "vulkan": 1 << 6, "bf16": 1 << 7}
 STATUS = {0: "ok", 1: "invalid argument", 2: "model I/O error", 3: "invalid model format",
           4: "Vulkan unavailable", 5: "out of memory", 6: "inference failed", 7: "buffer too small",
           8: "unsupported", 9: "internal error", 10: "invalid state", 11: "cancelled"}
@@ -73,6 +73,10 @@ PUBLIC = {
     "dav2_infer_device_bgr8_batch": (ctypes.c_int, [vp, vp, u32, i32, i32, ctypes.c_ssize_t, ctypes.c_ssize_t, i32,
                                                     vp, vp]),
     "dav2_synchronize": (ctypes.c_int, [vp]),
+    "dav2_infer_device_frames_bgr8": (ctypes.c_int, [vp, vp, u32, i32, i32, ctypes.c_ssize_t, ctypes.c_ssize_t, i32,
+                                                     vp, vp]),
+    "dav2_submit_device_pixels": (ctypes.c_int, [vp, vp, u32, i32, i32, ctypes.c_ssize_t, ctypes.c_ssize_t,
+                                                 ctypes.c_int, i32, vp, vp]),
     "dav2_probe_encoder_block": (ctypes.c_int, [vp, u32, i32, i32, u32, vp, vp, vp, vp]),
     "dav2_probe_head": (ctypes.c_int, [vp, u32, i32, i32, vp, vp]),
     "dav2_get_kernel_launch_count": (ctypes.c_int, [vp, ctypes.POINTER(u64)]),

@@ -266,6 +266,64 @@ DAV2CUDA_API int dav2cuda_conv3x3_int8_up2(float* output, const float* input,
                                            uint32_t output_channels, void* workspace,
                                            uint64_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------ token ops */
+
+/* VulkanOperators::prepare_tokens (src/operators.h:127-141,
+ * src/operators.cpp:1211-1406): planar image [3][h][w] (w, h multiples of
+ * 14) -> tokens [1 + (w/14)(h/14)][embedding]: the patch embedding (a 14x14
+ * stride-14 convolution, weight [embedding][3][14][14], + bias), the class
+ * token at row 0, and the 37x37 positional grid of `position` ([1370]
+ * [embedding]) resized bicubically to the patch grid (exact copy at 37x37,
+ * src/shaders/position_bicubic.glsl) and added. _half: weight f32, computed
+ * with bf16 (precision 1) or f16 (precision 2) operands and f32
+ * accumulation; _int8: the reference's int8 route — per-patch im2col
+ * quantization and packed int8 weight codes [embedding][147] with scales. */
+DAV2CUDA_API uint64_t dav2cuda_prepare_tokens_workspace_size(uint32_t input_width, uint32_t input_height,
+                                                             uint32_t embedding);
+DAV2CUDA_API int dav2cuda_prepare_tokens_half(float* output, const float* image, const float* patch_weight,
+                                              const float* patch_bias, const float* class_token,
+                                              const float* position, uint32_t input_width,
+                                              uint32_t input_height, uint32_t embedding, uint32_t precision,
+                                              void* workspace, uint64_t workspace_bytes, void* stream);
+DAV2CUDA_API int dav2cuda_prepare_tokens_int8(float* output, const float* image,
+                                              const uint32_t* patch_int8_weight,
+                                              const float* patch_weight_scales, const float* patch_bias,
+                                              const float* class_token, const float* position,
+                                              uint32_t input_width, uint32_t input_height, uint32_t embedding,
+                                              void* workspace, uint64_t workspace_bytes, void* stream);
+
+/* VulkanOperators::project_tokens / _fp16 / _int8 (src/operators.h:143-171,
+ * src/operators.cpp:1408-1526): tokens [1 + width*height][embedding] (row 0,
+ * the class token, is skipped) -> planar [output_channels][height*width]
+ * through a 1x1 convolution (weight [output_channels][embedding], bias
+ * nullable). _half: bf16 (precision 1) or f16 (precision 2) operands; _int8:
+ * per-row int8 tokens x packed int8 weight codes [output_channels]
+ * [embedding/4] with scales. */
+DAV2CUDA_API uint64_t dav2cuda_project_tokens_workspace_size(uint32_t width, uint32_t height, uint32_t embedding,
+                                                             uint32_t output_channels);
+DAV2CUDA_API int dav2cuda_project_tokens_half(float* output, const float* tokens, const float* weight,
+                                              const float* bias, uint32_t width, uint32_t height,
+                                              uint32_t embedding, uint32_t output_channels, uint32_t precision,
+                                              void* workspace, uint64_t workspace_bytes, void* stream);
+DAV2CUDA_API int dav2cuda_project_tokens_int8(float* output, const float* tokens, const uint32_t* int8_weight,
+                                              const float* weight_scales, const float* bias, uint32_t width,
+                                              uint32_t height, uint32_t embedding, uint32_t output_channels,
+                                              void* workspace, uint64_t workspace_bytes, void* stream);
+
+/* VulkanOperators::conv_transpose_nonoverlap / _fp16 (src/operators.h:
+ * 214-230, src/operators.cpp:1807-1906): transposed convolution with kernel
+ * == stride k, weight [Ci][Co][k][k], bias [Co]: planar [Ci][H][W] ->
+ * [Co][H*k][W*k], with bf16 (precision 1) or f16 (precision 2) operands and
+ * f32 accumulation. */
+DAV2CUDA_API uint64_t dav2cuda_conv_transpose_half_workspace_size(uint32_t input_width, uint32_t input_height,
+                                                                  uint32_t input_channels,
+                                                                  uint32_t output_channels, uint32_t kernel);
+DAV2CUDA_API int dav2cuda_conv_transpose_half(float* output, const float* input, const float* weight,
+                                              const float* bias, uint32_t input_width, uint32_t input_height,
+                                              uint32_t input_channels, uint32_t output_channels, uint32_t kernel,
+                                              uint32_t precision, void* workspace, uint64_t workspace_bytes,
+                                              void* stream);
+
 /* ------------------------------------------------------------- attention */
 
 /* VulkanOperators::attention_head64 (src/operators.h:124-131,

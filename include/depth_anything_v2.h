@@ -76,7 +76,11 @@ enum {
     DAV2_CREATE_FORCE_FP16 = 1u << 3u,
     DAV2_CREATE_FORCE_INT8 = 1u << 4u,
     DAV2_CREATE_FORCE_METAL = 1u << 5u,
-    DAV2_CREATE_FORCE_VULKAN = 1u << 6u
+    DAV2_CREATE_FORCE_VULKAN = 1u << 6u,
+    /* EXTENSION (no reference counterpart; the reference has fp16, not bf16):
+     * every GEMM, convolution and attention with bf16 operands and f32
+     * accumulation, bf16 activations between them. */
+    DAV2_CREATE_FORCE_BF16 = 1u << 7u
 };
 
 typedef struct dav2_model_info {
@@ -350,6 +354,35 @@ DAV2_API dav2_status DAV2_CALL dav2_infer_device_bgr8_batch(dav2_context* contex
                                                             int32_t image_height, ptrdiff_t row_stride_bytes,
                                                             ptrdiff_t image_stride_bytes, int32_t input_size,
                                                             float* device_depth, void* stream);
+
+/* EXTENSION: the high-resolution video path: `batch` device BGR8 frames of
+ * image_width x image_height, each resized bilinearly (half-pixel centres,
+ * align_corners=False) to a square network_size x network_size input
+ * (network_size a multiple of 14), through the graph, and the depth resized
+ * back (align-corners bilinear, as Executor::infer_resized does) to
+ * image_width x image_height in device_depth. Stream semantics as
+ * dav2_infer_device_bgr8_batch. */
+DAV2_API dav2_status DAV2_CALL dav2_infer_device_frames_bgr8(dav2_context* context, const uint8_t* device_bgr,
+                                                             uint32_t batch, int32_t image_width,
+                                                             int32_t image_height, ptrdiff_t row_stride_bytes,
+                                                             ptrdiff_t image_stride_bytes, int32_t network_size,
+                                                             float* device_depth, void* stream);
+
+/* EXTENSION: the headless analogue of the reference's GPU submit path
+ * (src/vulkan_executor.cpp:656-812, dav2_submit_d3d12 without the D3D12
+ * interop): `batch` device images of packed 8-bit pixels (pixel_format
+ * DAV2_GPU_PIXEL_BGRA8 or DAV2_GPU_PIXEL_RGBA8, row_stride_bytes and
+ * image_stride_bytes multiples of 4) -> GPU bicubic preprocessing to the
+ * network shape (preprocess_rgba.glsl) -> graph -> per-image min/max
+ * normalization at the network resolution (normalize_relative, or
+ * normalize_metric with the 25 m presentation span for a metric model) ->
+ * align-corners bilinear expansion to image_width x image_height in
+ * device_output. Stream semantics as dav2_infer_device_bgr8_batch. */
+DAV2_API dav2_status DAV2_CALL dav2_submit_device_pixels(dav2_context* context, const uint8_t* device_pixels,
+                                                         uint32_t batch, int32_t image_width, int32_t image_height,
+                                                         ptrdiff_t row_stride_bytes, ptrdiff_t image_stride_bytes,
+                                                         dav2_gpu_pixel_format pixel_format, int32_t input_size,
+                                                         float* device_output, void* stream);
 
 /* EXTENSION: number of device kernels the context has launched so far
  * (each CUDA-graph replay counts its kernel nodes). */

@@ -114,12 +114,13 @@ def head(w, feats, ph, pw, name, metric_max_depth=0.0):
 
 
 @torch.inference_mode()
-def forward(w, images, name, out_size=None):
+def forward(w, images, name, out_size=None, metric_max_depth=0.0):
     """images: float32 [B, 3, H, W] (normalized RGB) -> depth [B, H, W]
-    (or [B, out_h, out_w] with the align-corners resize of infer_image)."""
+    (or [B, out_h, out_w] with the align-corners resize of infer_image);
+    metric_max_depth > 0 selects the metric head (sigmoid * max depth)."""
     x = images if isinstance(images, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(images))
     feats, ph, pw = encoder(w, x, name)
-    d = head(w, feats, ph, pw, name)
+    d = head(w, feats, ph, pw, name, metric_max_depth)
     if out_size is not None and tuple(out_size) != tuple(d.shape[-2:]):
         d = F.interpolate(d[:, None], out_size, mode="bilinear", align_corners=True)[:, 0]
     return d

@@ -487,3 +487,105 @@ def test_device_weight_packing_bit_exact(cuda, dav2lib, kind, shape):
     assert np.array_equal(host(sc), want_sc)
     assert np.array_equal(codes, want)
     assert not host(out)[:, K:].any()  # padding columns are zero
+
+
+# ------------------------------------------------------------- token ops
+def _prepare_tokens(cuda, dav2lib, image, w_patch, bias, cls, pos, e, mode):
+    _, h, w = image.shape
+    t = 1 + (w // 14) * (h // 14)
+    ws = dav2lib.dav2cuda_prepare_tokens_workspace_size(w, h, e)
+    out, wsb = empty(cuda, (t, e)), empty(cuda, (ws,), np.uint8)
+    if mode == "int8":
+        pw, sw = oracle.pack_weight_s8(w_patch.reshape(e, -1))
+        call(dav2lib, "dav2cuda_prepare_tokens_int8", ptr(out), ptr(dev(cuda, image)), ptr(dev(cuda, pw)),
+             ptr(dev(cuda, sw)), ptr(dev(cuda, bias)), ptr(dev(cuda, cls)), ptr(dev(cuda, pos)), w, h, e, ptr(wsb), ws,
+             None)
+    else:
+        call(dav2lib, "dav2cuda_prepare_tokens_half", ptr(out), ptr(dev(cuda, image)), ptr(dev(cuda, w_patch)),
+             ptr(dev(cuda, bias)), ptr(dev(cuda, cls)), ptr(dev(cuda, pos)), w, h, e, {"bf16": 1, "f16": 2}[mode],
+             ptr(wsb), ws, None)
+    finish(cuda, dav2lib)
+    return host(out)
+
+
+@pytest.mark.parametrize("mode", ["f16", "bf16", "int8"])
+def test_prepare_tokens_reference_kat(cuda, dav2lib, mode):
+    """tests/vulkan_smoke.cpp:630-754: a 42x28 zero image (3x2 patch grid, not
+    37x37), zero patch weights, embedding 3: every token is its bias plus the
+    bicubic-resized position (class row: class token + position row 0),
+    within 2e-6 (exact zeros through the tensor-core GEMM)."""
+    e, w, h = 3, 42, 28
+    image = np.zeros((3, h, w), np.float32)
+    w_patch = np.zeros((e, 3, 14, 14), np.float32)
+    bias = np.array([0.25, -0.5, 0.75], np.float32)
+    cls = np.array([1.0, 2.0, 3.0], np.float32)
+    pos = ((np.arange(1370 * e) % 31 - 15) * 0.015625).astype(np.float32).reshape(1370, e)
+    got = _prepare_tokens(cuda, dav2lib, image, w_patch, bias, cls, pos, e, mode)
+    assert np.array_equal(got[0], cls + pos[0])
+    planar = oracle.position_bicubic(pos, w // 14, h // 14)  # [e][ph][pw], pinned to the same KAT on the CPU
+    want = bias[None, :] + planar.reshape(e, -1).T
+    assert np.abs(got[1:] - want).max() <= 2e-6
+
+
+@pytest.mark.parametrize("mode", ["f16", "int8"])
+@pytest.mark.parametrize("w,h", [(84, 70), (518, 518)])
+def test_prepare_tokens_vs_oracle(cuda, dav2lib, mode, w, h):
+    """Seeded image and ViT-S-sized weights; 518x518 is the 37x37 identity
+    grid, 84x70 a resized one. int8: codes, integer GEMM and dequant are
+    exact, so only the bicubic position sum can differ in the last bit."""
+    r = rng(w + h)
+    e = 384
+    image = r.standard_normal((3, h, w)).astype(np.float32)
+    w_patch = (r.standard_normal((e, 3, 14, 14)) * 0.02).astype(np.float32)
+    bias = (r.standard_normal(e) * 0.02).astype(np.float32)
+    cls = (r.standard_normal(e) * 0.02).astype(np.float32)
+    pos = (r.standard_normal((1370, e)) * 0.02).astype(np.float32)
+    got = _prepare_tokens(cuda, dav2lib, image, w_patch, bias, cls, pos, e, mode)
+    pw, ph = w // 14, h // 14
+    sd = {"pretrained.patch_embed.proj.weight": w_patch, "pretrained.patch_embed.proj.bias": bias,
+          "pretrained.cls_token": cls, "pretrained.pos_embed": pos}
+    want = oracle.embed(sd, image, "vits", "int8" if mode == "int8" else "fp32")
+    err = max_rel(got, want)
+    print(f"prepare_tokens {mode} {w}x{h}: max rel {err:.2e}")
+    assert err < (1e-5 if mode == "int8" else 4e-3)
+
+
+@pytest.mark.parametrize("mode", ["f16", "bf16", "int8"])
+@pytest.mark.parametrize("pw,ph,e,co", [(37, 37, 1024, 256), (6, 5, 384, 48), (37, 37, 768, 768)])
+def test_project_tokens_vs_oracle(cuda, dav2lib, mode, pw, ph, e, co):
+    r = rng(e + co)
+    tokens = r.standard_normal((1 + pw * ph, e)).astype(np.float32)
+    wt = (r.standard_normal((co, e)) * 0.02).astype(np.float32)
+    b = (r.standard_normal(co) * 0.02).astype(np.float32)
+    ws = dav2lib.dav2cuda_project_tokens_workspace_size(pw, ph, e, co)
+    out, wsb = empty(cuda, (co, ph, pw)), empty(cuda, (ws,), np.uint8)
+    if mode == "int8":
+        pk, sw = oracle.pack_weight_s8(wt)
+        call(dav2lib, "dav2cuda_project_tokens_int8", ptr(out), ptr(dev(cuda, tokens)), ptr(dev(cuda, pk)),
+             ptr(dev(cuda, sw)), ptr(dev(cuda, b)), pw, ph, e, co, ptr(wsb), ws, None)
+        finish(cuda, dav2lib)
+        px, sx = oracle.quantize_rows_s8(tokens, pw * ph, e, input_offset=e)
+        want = oracle.linear_s8(px, pk, sx, sw, b, pw * ph, e, co, transposed=True).reshape(co, ph, pw)
+        assert np.array_equal(host(out), want)  # bit-exact: codes, integer GEMM, dequant order
+    else:
+        call(dav2lib, "dav2cuda_project_tokens_half", ptr(out), ptr(dev(cuda, tokens)), ptr(dev(cuda, wt)),
+             ptr(dev(cuda, b)), pw, ph, e, co, {"bf16": 1, "f16": 2}[mode], ptr(wsb), ws, None)
+        finish(cuda, dav2lib)
+        want = oracle.project_tokens_f32(tokens, wt, b, pw, ph)
+        assert max_rel(host(out), want) < (4e-3 if mode == "f16" else 2e-2)
+
+
+@pytest.mark.parametrize("mode", ["f16", "bf16"])
+@pytest.mark.parametrize("c,h,w,o,k", [(256, 37, 37, 256, 4), (512, 37, 37, 512, 2), (48, 5, 7, 48, 4), (20, 3, 4, 12, 2)])
+def test_conv_transpose_half_vs_oracle(cuda, dav2lib, mode, c, h, w, o, k):
+    r = rng(c + k)
+    x = r.standard_normal((c, h, w)).astype(np.float32)
+    wt = (r.standard_normal((c, o, k, k)) * 0.05).astype(np.float32)
+    b = r.standard_normal(o).astype(np.float32)
+    ws = dav2lib.dav2cuda_conv_transpose_half_workspace_size(w, h, c, o, k)
+    out, wsb = empty(cuda, (o, h * k, w * k)), empty(cuda, (ws,), np.uint8)
+    call(dav2lib, "dav2cuda_conv_transpose_half", ptr(out), ptr(dev(cuda, x)), ptr(dev(cuda, wt)), ptr(dev(cuda, b)),
+         w, h, c, o, k, {"bf16": 1, "f16": 2}[mode], ptr(wsb), ws, None)
+    finish(cuda, dav2lib)
+    want = oracle.conv_transpose_f32(x, wt, b)
+    assert max_rel(host(out), want) < (4e-3 if mode == "f16" else 2e-2)

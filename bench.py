@@ -30,6 +30,9 @@ carries the timing barrier and the max-over-ranks reduction.
            fraction of max(bytes / HBM, work / peak) it reaches; `hbm_ops`
            the bandwidth-bound operations of the graph against both the
            measured copy bandwidth and the 8 TB/s nominal;
+  other_configs (rank 0, N=1) BASELINE configurations 3 (ViT-B bf16, 16
+           images) and 5 (ViT-L bf16, 8 1920x1080 frames at 1036x1036) through
+           the public API, device value and e2e;
   op_microbench (rank 0, N=1) BASELINE configuration 2: the stand-alone
            LayerNorm, erf-GELU, row softmax and int8 3x3-conv + 2x upsample
            kernels at their BASELINE shapes, achieved GB/s of algorithmic bytes;
@@ -63,7 +66,7 @@ NOMINAL_HBM_GBS = 8000.0  # B200 HBM3e nominal (DGX figure) named by the BASELIN
 def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--encoder", default="vitl")
@@ -71,7 +74,7 @@ def parse(argv=None):
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--precision", choices=["int8", "fp16"], default="int8")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-microbench", action="store_true")
+    ap.add_argument("--no-microbench", action="store_true", help="skip configurations 2, 3 and 5")
     ap.add_argument("--profile-only", action="store_true", help="print the per-operation profile and exit")
     return ap.parse_args(argv)
 
@@ -135,8 +138,25 @@ class ClockSampler:
                                          stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        # wait for the first sample: nvidia-smi's start-up (NVML initialisation)
+        # can stall CUDA calls of this process for a few hundred ms, which must
+        # not land inside a timed region
+        t0 = time.time()
+        while self.proc is not None and time.time() - t0 < 10 and self.lines() == 0:
+            time.sleep(0.05)
         time.sleep(0.3)
+        self.first = self.last = None
         return self
+
+    def lines(self) -> int:
+        self.file.flush()
+        return len([l for l in Path(self.file.name).read_text().splitlines() if l.strip()])
+
+    def mark_start(self):
+        self.first = self.lines()
+
+    def mark_end(self):
+        self.last = self.lines()
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -147,8 +167,12 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        """Samples taken between mark_start() and mark_end() (the timed region;
+        all samples when unmarked): median SM clock, max clock, reasons."""
         self.file.flush()
         rows = [l.split(",") for l in Path(self.file.name).read_text().splitlines() if l.strip()]
+        if self.first is not None:
+            rows = rows[self.first:self.last if self.last and self.last > self.first else None] or rows[-1:]
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
@@ -410,6 +434,84 @@ def op_microbench(lib, torch, hbm_pk):
     return out
 
 
+def extra_configs(lib, torch, steps=5, warmup=2):
+    """BASELINE configurations 3 and 5 on this GPU (rank 0, N=1), each through
+    the public API on device buffers (value) and with the host copies of its
+    inputs and outputs inside the timed region (e2e):
+      vitb_bf16_b16   ViT-B full graph, bf16, 16 random-u8 518x518 BGR8 images
+                      per step (dav2_infer_device_bgr8_batch);
+      vitl_bf16_1036_frames_b8  ViT-L, bf16, 8 random-u8 1920x1080 BGR8 frames
+                      per step (seed = frame index) resized bilinearly to
+                      1036x1036 on the GPU (5477 tokens), depth back at
+                      1920x1080 (dav2_infer_device_frames_bgr8).
+    CUDA-event device time per step, 256 MiB L2 flush between steps."""
+    import numpy as np
+
+    from dav2_b200 import capi
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    out = {}
+    cases = (("vitb_bf16_b16", "vitb", 16, 518, 518, None),
+             ("vitl_bf16_1036_frames_b8", "vitl", 8, 1920, 1080, 1036))
+    for name, enc, B, W, H, net in cases:
+        path = model_path(enc, 0, 1)
+        opts = capi.CreateOptions(ctypes.sizeof(capi.CreateOptions), 1, capi.ENCODERS[enc], 0, capi.FLAGS["bf16"], None)
+        ctx = ctypes.c_void_p()
+        if lib.dav2_create(str(path).encode(), ctypes.byref(opts), ctypes.byref(ctx)) != 0:
+            raise RuntimeError(f"dav2_create: {lib.dav2_last_error().decode()}")
+        try:
+            host = torch.from_numpy(images(range(B), W) if W == H else np.stack(
+                [np.random.default_rng(f).integers(0, 256, (H, W, 3), dtype=np.uint8) for f in range(B)])).pin_memory()
+            dev_in = host.cuda()
+            dev_out = torch.empty((B, H, W), dtype=torch.float32, device="cuda")
+            host_out = torch.empty((B, H, W), dtype=torch.float32).pin_memory()
+            stream = torch.cuda.Stream()
+
+            def call():
+                sp = ctypes.c_void_p(stream.cuda_stream)
+                if net is None:
+                    rc = lib.dav2_infer_device_bgr8_batch(ctx, dev_in.data_ptr(), B, W, H, W * 3, W * H * 3, W,
+                                                         dev_out.data_ptr(), sp)
+                else:
+                    rc = lib.dav2_infer_device_frames_bgr8(ctx, dev_in.data_ptr(), B, W, H, W * 3, W * H * 3, net,
+                                                          dev_out.data_ptr(), sp)
+                if rc != 0:
+                    raise RuntimeError(f"{name}: {lib.dav2_last_error().decode()}")
+
+            with torch.cuda.stream(stream):
+                for _ in range(warmup):
+                    call()
+                torch.cuda.synchronize()
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(stream)
+                for _ in range(steps):
+                    flush.zero_()
+                    call()
+                e.record(stream)
+                torch.cuda.synchronize()
+                dev_ms = s.elapsed_time(e) / steps
+                t0 = time.perf_counter()
+                for _ in range(steps):
+                    dev_in.copy_(host, non_blocking=True)
+                    call()
+                    host_out.copy_(dev_out, non_blocking=True)
+                    stream.synchronize()
+                e2e_s = (time.perf_counter() - t0) / steps
+            if lib.dav2_synchronize(ctx) != 0:
+                raise RuntimeError(f"{name}: {lib.dav2_last_error().decode()}")
+            assert np.isfinite(host_out.numpy()).all()
+            unit = "frames/s" if net else "images/s"
+            out[name] = {"value": round(B / (dev_ms * 1e-3), 2), "unit": unit, "ms_per_step": round(dev_ms, 3),
+                         "batch": B, "encoder": enc, "dtype": "bf16",
+                         "network_input": f"{net or W}x{net or H}", "source": f"{W}x{H} BGR8",
+                         "e2e": {"value": round(B / e2e_s, 2), "unit": unit,
+                                 "h2d_bytes_per_step": int(B * W * H * 3), "d2h_bytes_per_step": int(B * W * H * 4)}}
+        finally:
+            lib.dav2_destroy(ctx)
+            torch.cuda.empty_cache()
+    return out
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -487,7 +589,7 @@ def main():
             dist.destroy_process_group()
         return
 
-    with torch.cuda.stream(stream):
+    with torch.cuda.stream(stream), ClockSampler(local) as clocks:
         for _ in range(args.warmup):
             device_step()
         torch.cuda.synchronize()
@@ -495,14 +597,15 @@ def main():
         lib.dav2_get_kernel_launch_count(ctx, ctypes.byref(launches0))
         barrier()
         torch.cuda.synchronize()
-        with ClockSampler(local) as clocks:
-            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            start.record(stream)
-            for _ in range(args.steps):
-                flush.zero_()
-                device_step()
-            end.record(stream)
-            torch.cuda.synchronize()
+        clocks.mark_start()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            flush.zero_()
+            device_step()
+        end.record(stream)
+        torch.cuda.synchronize()
+        clocks.mark_end()
         barrier()
         dev_ms = max_over_ranks(start.elapsed_time(end), dist)
         launches1 = ctypes.c_uint64()
@@ -589,9 +692,10 @@ def main():
         roof["hbm_ops"] = hbm_ops
         roof["hbm_peak_source"] = hbm_src
         roof["op_shares"] = shares
-        micro = None
+        micro = extra = None
         if world == 1 and not args.no_microbench:
             micro = op_microbench(lib, torch, hbm_pk)
+            extra = extra_configs(lib, torch)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(args.encoder, S)
@@ -615,6 +719,7 @@ def main():
             "check": check,
             "roofline": roof,
             "op_microbench": micro,
+            "other_configs": extra,
             "cpu_baseline": cpu,
             "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
             "gpu_launches": int(launches1.value - launches0.value),

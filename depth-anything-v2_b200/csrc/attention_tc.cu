@@ -102,6 +102,15 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
+// 2^x of two f16 values at once (one exponential-unit operation).
+__device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
+    uint32_t y;
+    asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+__device__ __forceinline__ __half2 as_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
+
 
 // Packed f32x2 arithmetic of sm_100 (two IEEE fp32 lanes per instruction,
 // each lane rounded exactly as the scalar operation) and the three-input
@@ -470,20 +479,46 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint64_t mul2 = pack_f32x2(c, c), add2 = pack_f32x2(-mc, -mc);
 #pragma unroll
                 for (int i = 0; i < 64; i += 2) ffma2(s[i], s[i + 1], mul2, add2);
-#pragma unroll
-                for (int i = 0; i < 64; ++i) s[i] = ex2_approx(s[i]);
-
                 float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                if constexpr (!kBF16) {
+                    // f16 P: the exponent arguments (s - m)*c rounded to f16 pairs
+                    // and exponentiated two per MUFU operation (ex2.approx.f16x2),
+                    // which halves the exponential unit's work. The reference's fp16
+                    // attention rounds the scores themselves to f16 before its
+                    // softmax (bmm_score_fp16.glsl, softmax_lastdim_half.glsl), a
+                    // coarser rounding than this one of the max-shifted argument.
+                    // Row sums: groups of eight P values in f16, then f32.
+                    uint32_t h[32];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    uint32_t hv[4];
+                    for (int i = 0; i < 32; ++i) h[i] = pack_h2<false>(s[2 * i], s[2 * i + 1]);
 #pragma unroll
-                    for (int v = 0; v < 4; ++v) {
-                        fadd2(ls[2 * v], ls[2 * v + 1], s[8 * q + 2 * v], s[8 * q + 2 * v + 1]);
-                        hv[v] = pack_h2<kBF16>(s[8 * q + 2 * v], s[8 * q + 2 * v + 1]);
+                    for (int i = 0; i < 32; ++i) h[i] = ex2_h2(h[i]);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const __half2 a = __hadd2(as_h2(h[4 * q]), as_h2(h[4 * q + 1]));
+                        const __half2 b = __hadd2(as_h2(h[4 * q + 2]), as_h2(h[4 * q + 3]));
+                        const float2 f = __half22float2(__hadd2(a, b));
+                        ls[q & 3] += f.x;
+                        ls[4 + (q & 3)] += f.y;
+                        *reinterpret_cast<uint4*>(atoms + (gtt % kPBufs) * 2u * kTile +
+                                                  (((uint32_t)q ^ (row & 7u)) << 4)) =
+                            make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
                     }
-                    *reinterpret_cast<uint4*>(atoms + (gtt % kPBufs) * 2u * kTile + (((uint32_t)q ^ (row & 7u)) << 4)) =
-                        make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) s[i] = ex2_approx(s[i]);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        uint32_t hv[4];
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            fadd2(ls[2 * v], ls[2 * v + 1], s[8 * q + 2 * v], s[8 * q + 2 * v + 1]);
+                            hv[v] = pack_h2<true>(s[8 * q + 2 * v], s[8 * q + 2 * v + 1]);
+                        }
+                        *reinterpret_cast<uint4*>(atoms + (gtt % kPBufs) * 2u * kTile +
+                                                  (((uint32_t)q ^ (row & 7u)) << 4)) =
+                            make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                    }
                 }
                 l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
                 tc_fence_before();

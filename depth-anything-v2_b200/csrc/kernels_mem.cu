@@ -212,9 +212,20 @@ __global__ void sigmoid_scale_kernel(float* __restrict__ out, const float* __res
 // multiply by 1/max(sum, 1e-20). One warp per row, the row kept in
 // registers (MAXV float2 per lane), so each element is read and written
 // exactly once.
+// exp(x) as 2^(x*log2e) on the exponential unit (relative error ~2^-22).
+__device__ __forceinline__ float exp_fast(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+    return y;
+}
+
+// softmax_lastdim.glsl:19-69: row max of x*scale, exp(x*scale - max), sum,
+// normalize. One warp per row, the row held in registers (read once,
+// written once); the register budget is capped at three 256-thread blocks
+// per SM so that 24 warps (24 rows) per SM keep loads in flight.
 template <int MAXV>
-__global__ void __launch_bounds__(256) softmax_warp_kernel(float* __restrict__ out, const float* __restrict__ in,
-                                                           uint64_t rows, uint32_t cols, float scale) {
+__global__ void __launch_bounds__(256, MAXV <= 24 ? 3 : 1) softmax_warp_kernel(float* __restrict__ out, const float* __restrict__ in,
+                                                              uint64_t rows, uint32_t cols, float scale) {
     const uint64_t warp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint32_t lane = threadIdx.x & 31;
     if (warp >= rows) return;
@@ -245,13 +256,13 @@ __global__ void __launch_bounds__(256) softmax_warp_kernel(float* __restrict__ o
     for (int i = 0; i < MAXV; ++i) {
         const uint32_t c = lane + 32u * i;
         if (c < n2) {
-            v[i].x = expf(v[i].x - m);
-            v[i].y = expf(v[i].y - m);
+            v[i].x = exp_fast(v[i].x - m);
+            v[i].y = exp_fast(v[i].y - m);
             s += v[i].x + v[i].y;
         }
     }
     if (odd) {
-        tail = expf(tail - m);
+        tail = exp_fast(tail - m);
         s += tail;
     }
     s = warp_sum(s);

@@ -487,23 +487,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // attention rounds the scores themselves to f16 before its
                     // softmax (bmm_score_fp16.glsl, softmax_lastdim_half.glsl), a
                     // coarser rounding than this one of the max-shifted argument.
-                    // Row sums: groups of eight P values in f16, then f32.
+                    // Row sum of the block: a pairwise f16x2 tree over the 64 P
+                    // values (six levels), converted to f32 once and added to l in f32.
                     uint32_t h[32];
 #pragma unroll
                     for (int i = 0; i < 32; ++i) h[i] = pack_h2<false>(s[2 * i], s[2 * i + 1]);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) h[i] = ex2_h2(h[i]);
+                    __half2 part[8];
 #pragma unroll
                     for (int q = 0; q < 8; ++q) {
-                        const __half2 a = __hadd2(as_h2(h[4 * q]), as_h2(h[4 * q + 1]));
-                        const __half2 b = __hadd2(as_h2(h[4 * q + 2]), as_h2(h[4 * q + 3]));
-                        const float2 f = __half22float2(__hadd2(a, b));
-                        ls[q & 3] += f.x;
-                        ls[4 + (q & 3)] += f.y;
+                        part[q] = __hadd2(__hadd2(as_h2(h[4 * q]), as_h2(h[4 * q + 1])),
+                                          __hadd2(as_h2(h[4 * q + 2]), as_h2(h[4 * q + 3])));
                         *reinterpret_cast<uint4*>(atoms + (gtt % kPBufs) * 2u * kTile +
                                                   (((uint32_t)q ^ (row & 7u)) << 4)) =
                             make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
                     }
+                    const __half2 t4 = __hadd2(__hadd2(__hadd2(part[0], part[1]), __hadd2(part[2], part[3])),
+                                               __hadd2(__hadd2(part[4], part[5]), __hadd2(part[6], part[7])));
+                    const float2 f = __half22float2(t4);
+                    ls[0] = f.x + f.y;
                 } else {
 #pragma unroll
                     for (int i = 0; i < 64; ++i) s[i] = ex2_approx(s[i]);

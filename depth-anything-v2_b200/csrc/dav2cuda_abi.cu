@@ -727,15 +727,16 @@ int dav2cuda_conv_transpose_half(float* output, const float* input, const float*
 
 // BASELINE configuration 2(d): the reference's conv2d_int8 (3x3, pad 1;
 // src/operators.cpp:1735-1805) then bilinear_align_true 2x
-// (src/operators.cpp:1978-2012), batched. The input goes channels-last once
-// (f32), so the im2col quantizer reads each pixel's 256 channels as
-// contiguous 32-byte groups instead of gathering across planes; the weight
-// codes are permuted to the same (ky, kx, c) column order, which leaves each
-// row's scale, codes and integer dot products unchanged.
+// (src/operators.cpp:1978-2012), batched. Row scales come exactly from a
+// per-pixel channel abs-max pre-pass and a 3x3 maximum, so the im2col
+// quantizer needs no row reduction and reads the planar input directly; its
+// codes are in (ky, kx, c) column order and the weight codes are permuted
+// alike, which leaves each row's scale, codes and integer dot products
+// unchanged.
 uint64_t dav2cuda_conv3x3_int8_up2_workspace_size(uint32_t batch, uint32_t w, uint32_t h, uint32_t ic, uint32_t oc) {
     const uint32_t kp = round_up(ic * 9, 16);
     const uint64_t rows = (uint64_t)batch * w * h;
-    return align256(rows * ic * 4) + align256(rows * kp) + align256(rows * 4) + align256((uint64_t)oc * kp) +
+    return align256(rows * 4) + align256(rows * kp) + align256(rows * 4) + align256((uint64_t)oc * kp) +
            align256((uint64_t)batch * oc * w * h * 4) + 256;
 }
 
@@ -750,14 +751,13 @@ int dav2cuda_conv3x3_int8_up2(float* output, const float* input, const uint32_t*
     const uint32_t K = ic * 9, kp = round_up(K, 16);
     const uint64_t hw = (uint64_t)w * h, rows = batch * hw;
     Carve ws(workspace, workspace_bytes);
-    float* xt = ws.take<float>(rows * ic * 4);
+    float* pix = ws.take<float>(rows * 4);
     uint8_t* codes = ws.take<uint8_t>(rows * kp);
     float* scales = ws.take<float>(rows * 4);
     uint8_t* wt = ws.take<uint8_t>((uint64_t)oc * kp);
     float* conv = ws.take<float>((uint64_t)batch * oc * hw * 4);
-    int rc = launch_nchw_to_nhwc<float>(xt, input, batch, ic, h, w, ic, st);
-    if (!rc) rc = launch_conv_codes_tap_major(wt, reinterpret_cast<const uint8_t*>(int8_weight), oc, ic, 9, K, kp, st);
-    if (!rc) rc = launch_im2col_quantize_nhwc<float>(codes, scales, xt, batch, h, w, ic, ic, 3, 1, 1, h, w, kp, st);
+    int rc = launch_conv_codes_tap_major(wt, reinterpret_cast<const uint8_t*>(int8_weight), oc, ic, 9, K, kp, st);
+    if (!rc) rc = launch_im2col_quantize_3x3_planar(codes, scales, pix, input, batch, ic, h, w, kp, st);
     if (rc) return rc;
     GemmArgs g;
     g.elem = kElemS8;

@@ -330,6 +330,46 @@ __device__ __forceinline__ float lerp_rn(float a, float b, float f) {
     return __fadd_rn(__fmul_rn(a, __fsub_rn(1.0f, f)), __fmul_rn(b, f));
 }
 
+// Planar form for many planes: one block per (output row, chunk of
+// kPlanesPerBlock planes). The row's x table (source columns, weight) is
+// computed once in shared memory and the y terms once per block, so the
+// per-element work is four loads, three lerps and one store.
+constexpr uint32_t kPlanesPerBlock = 8;
+
+template <typename TI, typename TO>
+__global__ void __launch_bounds__(256) bilinear_align_rows_kernel(TO* __restrict__ out, const TI* __restrict__ in,
+                                                                  uint32_t iw, uint32_t ih, uint32_t ow, uint32_t oh,
+                                                                  uint32_t planes) {
+    extern __shared__ uint32_t tab[];  // [ow] x0 | x1 << 16, then [ow] fx
+    float* tfx = reinterpret_cast<float*>(tab + ow);
+    const uint32_t y = blockIdx.x;
+    for (uint32_t x = threadIdx.x; x < ow; x += blockDim.x) {
+        uint32_t x0, x1;
+        float fx;
+        align_coord(x, iw, ow, x0, x1, fx);
+        tab[x] = x0 | (x1 << 16);
+        tfx[x] = fx;
+    }
+    uint32_t y0, y1;
+    float fy;
+    align_coord(y, ih, oh, y0, y1, fy);
+    __syncthreads();
+    const uint32_t c0 = blockIdx.y * kPlanesPerBlock;
+    const uint32_t c1 = min(c0 + kPlanesPerBlock, planes);
+    for (uint32_t c = c0; c < c1; ++c) {
+        const TI* r0 = in + ((uint64_t)c * ih + y0) * iw;
+        const TI* r1 = in + ((uint64_t)c * ih + y1) * iw;
+        TO* o = out + ((uint64_t)c * oh + y) * ow;
+        for (uint32_t x = threadIdx.x; x < ow; x += blockDim.x) {
+            const uint32_t t = tab[x], x0 = t & 0xffffu, x1 = t >> 16;
+            const float fx = tfx[x];
+            const float top = lerp_rn(to_f(__ldg(r0 + x0)), to_f(__ldg(r0 + x1)), fx);
+            const float bot = lerp_rn(to_f(__ldg(r1 + x0)), to_f(__ldg(r1 + x1)), fx);
+            o[x] = from_f<TO>(lerp_rn(top, bot, fy));
+        }
+    }
+}
+
 template <typename TI, typename TO>
 __global__ void bilinear_align_kernel(TO* __restrict__ out, const TI* __restrict__ in, uint32_t iw, uint32_t ih,
                                       uint32_t ow, uint32_t oh, uint32_t planes) {
@@ -712,7 +752,114 @@ __global__ void __launch_bounds__(128) im2col_quantize_kernel(
     }
 }
 
+// Per-pixel channel abs-max of planar [B][C][HW] maps -> [B][HW] (one
+// thread per pixel, coalesced along pixels for each channel).
+__global__ void __launch_bounds__(256) pixel_absmax_kernel(float* __restrict__ out, const float* __restrict__ in,
+                                                           uint32_t c, uint32_t hw, uint64_t pixels) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= pixels) return;
+    const uint64_t img = i / hw, px = i % hw;
+    const float* src = in + img * c * hw + px;
+    float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
+    uint32_t ch = 0;
+    for (; ch + 4 <= c; ch += 4) {
+        m0 = fmaxf(m0, fabsf(__ldg(src + (uint64_t)ch * hw)));
+        m1 = fmaxf(m1, fabsf(__ldg(src + (uint64_t)(ch + 1) * hw)));
+        m2 = fmaxf(m2, fabsf(__ldg(src + (uint64_t)(ch + 2) * hw)));
+        m3 = fmaxf(m3, fabsf(__ldg(src + (uint64_t)(ch + 3) * hw)));
+    }
+    for (; ch < c; ++ch) m0 = fmaxf(m0, fabsf(__ldg(src + (uint64_t)ch * hw)));
+    out[i] = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+}
+
+// im2col_quantize_int8.glsl:26-84 for a 3x3, stride-1, pad-1 convolution of
+// planar [B][C][H][W] maps, without materialising floats: the row (output
+// pixel) abs-max over its C*9 im2col values is the maximum of the per-pixel
+// channel abs-maxima over the 3x3 neighbourhood (padding contributes 0), so
+// the exact row scale max(absmax/127, 1e-8) is known before any code is
+// formed. A block quantizes kIm2colPixels consecutive pixels of one image
+// row: warps walk the channels, lanes the pixels (coalesced loads along the
+// row for every channel and tap), codes x*(1/scale) go to a shared tile in
+// (ky, kx, c) column order (rows padded by 4 bytes: conflict-free byte
+// stores), then the rows are written out coalesced, padded with zero
+// columns to kp bytes.
+constexpr uint32_t kIm2colPixels = 32;
+
+__global__ void __launch_bounds__(256) im2col_quantize_3x3_planar_kernel(
+    uint8_t* __restrict__ codes, float* __restrict__ scales, const float* __restrict__ in,
+    const float* __restrict__ pix_absmax, uint32_t c, uint32_t h, uint32_t w, uint32_t kp) {
+    extern __shared__ uint32_t smem_words[];
+    const uint32_t stride = kp + 4;  // bytes per shared row
+    uint8_t* tile = reinterpret_cast<uint8_t*>(smem_words);
+    float* inv_s = reinterpret_cast<float*>(tile + (size_t)kIm2colPixels * stride);
+    const uint32_t tiles_x = (w + kIm2colPixels - 1) / kIm2colPixels;
+    const uint32_t y = (blockIdx.x / tiles_x) % h;
+    const uint64_t img = (uint64_t)blockIdx.x / ((uint64_t)tiles_x * h);
+    const uint32_t x0 = (blockIdx.x % tiles_x) * kIm2colPixels;
+    const uint32_t np = min(kIm2colPixels, w - x0);
+    const uint64_t row0 = (img * h + y) * w + x0;  // GEMM row of the tile's first pixel
+    if (threadIdx.x < kIm2colPixels) {
+        float m = 0.f;
+        const uint32_t x = x0 + threadIdx.x;
+        if (threadIdx.x < np) {
+            for (int dy = -1; dy <= 1; ++dy)
+                for (int dx = -1; dx <= 1; ++dx) {
+                    const int yy = (int)y + dy, xx = (int)x + dx;
+                    if (yy >= 0 && yy < (int)h && xx >= 0 && xx < (int)w)
+                        m = fmaxf(m, pix_absmax[(img * h + yy) * w + xx]);
+                }
+            const float scale = fmaxf(m / 127.0f, 1.0e-8f);
+            scales[row0 + threadIdx.x] = scale;
+            inv_s[threadIdx.x] = 1.0f / scale;
+        } else {
+            inv_s[threadIdx.x] = 0.f;
+        }
+    }
+    __syncthreads();
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float inv = inv_s[lane];
+    const int x = (int)(x0 + lane);
+    const float* plane0 = in + img * (uint64_t)c * h * w;
+    for (uint32_t ch = warp; ch < c; ch += blockDim.x >> 5) {
+        const float* plane = plane0 + (uint64_t)ch * h * w;
+        for (uint32_t tap = 0; tap < 9; ++tap) {
+            const int yy = (int)y + (int)(tap / 3) - 1, xx = x + (int)(tap % 3) - 1;
+            float v = 0.f;
+            if (lane < np && yy >= 0 && yy < (int)h && xx >= 0 && xx < (int)w) v = __ldg(plane + (uint64_t)yy * w + xx);
+            tile[lane * stride + tap * c + ch] = (uint8_t)q8(__fmul_rn(v, inv));
+        }
+    }
+    __syncthreads();
+    // rows out: 4-byte words, zero columns beyond 9*c
+    const uint32_t words = kp / 4, cols = 9 * c;
+    for (uint32_t i = threadIdx.x; i < np * words; i += blockDim.x) {
+        const uint32_t r = i / words, wd = i % words;
+        const uint8_t* src = tile + r * stride + 4 * wd;
+        uint32_t v = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (4 * wd + j < cols) v |= (uint32_t)src[j] << (8 * j);
+        reinterpret_cast<uint32_t*>(codes + (row0 + r) * kp)[wd] = v;
+    }
+}
+
 }  // namespace
+
+int launch_im2col_quantize_3x3_planar(uint8_t* codes, float* scales, float* pix_absmax, const float* in,
+                                      uint32_t batch, uint32_t c, uint32_t h, uint32_t w, uint32_t kp,
+                                      cudaStream_t st) {
+    if (kp % 4 || kp < 9 * c) return set_error(DAV2CUDA_INVALID_ARGUMENT, "im2col 3x3: row width");
+    const uint64_t pixels = (uint64_t)batch * h * w;
+    pixel_absmax_kernel<<<(unsigned)((pixels + 255) / 256), 256, 0, st>>>(pix_absmax, in, c, h * w, pixels);
+    const size_t smem = (size_t)kIm2colPixels * (kp + 4) + kIm2colPixels * 4;
+    if (smem > 200 * 1024) return set_error(DAV2CUDA_INVALID_ARGUMENT, "im2col 3x3: too many channels");
+    if (cudaFuncSetAttribute(im2col_quantize_3x3_planar_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+        return set_error(DAV2CUDA_LAUNCH_FAILED, "im2col 3x3: cannot set shared memory size");
+    const uint64_t blocks = (uint64_t)batch * h * ((w + kIm2colPixels - 1) / kIm2colPixels);
+    im2col_quantize_3x3_planar_kernel<<<(unsigned)blocks, 256, smem, st>>>(codes, scales, in, pix_absmax, c, h, w, kp);
+    return check_launch("im2col_quantize_3x3_planar");
+}
 
 // ============================================================ launchers
 static unsigned grid_for(uint64_t n, unsigned block = kBlock) {
@@ -809,6 +956,17 @@ int launch_sigmoid_scale(float* out, const float* in, uint64_t n, float s, cudaS
 template <typename TI, typename TO>
 int launch_bilinear_align(TO* out, const TI* in, uint32_t iw, uint32_t ih, uint32_t ow, uint32_t oh,
                           uint32_t planes, cudaStream_t st) {
+    if (planes >= kPlanesPerBlock && iw <= 65535 && oh <= 2147483647u &&
+        (planes + kPlanesPerBlock - 1) / kPlanesPerBlock <= 65535 && (size_t)ow * 8 <= 96 * 1024) {
+        dim3 grid(oh, (planes + kPlanesPerBlock - 1) / kPlanesPerBlock);
+        const size_t smem = (size_t)ow * 8;
+        if (smem > 48 * 1024 &&
+            cudaFuncSetAttribute(bilinear_align_rows_kernel<TI, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem) != cudaSuccess)
+            return set_error(DAV2CUDA_LAUNCH_FAILED, "bilinear_align_true: cannot set shared memory size");
+        bilinear_align_rows_kernel<TI, TO><<<grid, 256, smem, st>>>(out, in, iw, ih, ow, oh, planes);
+        return check_launch("bilinear_align_true");
+    }
     dim3 grid((ow + 127) / 128, oh, planes < 65535 ? planes : 65535);
     bilinear_align_kernel<TI, TO><<<grid, 128, 0, st>>>(out, in, iw, ih, ow, oh, planes);
     return check_launch("bilinear_align_true");

@@ -66,6 +66,13 @@ template <typename T>
 int launch_quantize_rows(uint32_t* packed, float* scales, const T* in, uint64_t rows, uint32_t cols,
                          uint64_t offset, uint32_t group, uint64_t group_stride, uint32_t row_stride,
                          uint32_t out_words, cudaStream_t st);
+// 3x3 / stride 1 / pad 1 im2col-quantize of planar f32 maps [B][C][H][W]:
+// codes [B*H*W][kp] in (ky, kx, c) column order (the reference's (c, ky, kx)
+// order permuted; rows and scales unchanged), exact row scales from a
+// per-pixel channel abs-max pre-pass (pix_absmax: [B*H*W] floats of scratch).
+int launch_im2col_quantize_3x3_planar(uint8_t* codes, float* scales, float* pix_absmax, const float* in,
+                                      uint32_t batch, uint32_t c, uint32_t h, uint32_t w, uint32_t kp,
+                                      cudaStream_t st);
 int launch_im2col_quantize(uint32_t* packed, float* scales, const float* in, uint32_t batch, uint32_t iw,
                            uint32_t ih, uint32_t ic, uint32_t ow, uint32_t oh, uint32_t k, uint32_t s, int pad,
                            uint32_t out_words, cudaStream_t st);

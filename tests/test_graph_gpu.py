@@ -9,11 +9,14 @@ Error measures: max|a-b| / max|b| (the 1e-2 bound) and max|a-b| / (max b -
 min b) (sensitivity to the spatial signal, reported alongside).
 
 The int8 graph is chaotic under last-bit changes before a quantization (a
-1-ulp perturbation of the LayerNorm outputs moves the oracle's own int8
-ViT-L output by ~4%), so the 1e-2 same-precision bound is asserted where the
-network is well conditioned (ViT-S / ViT-B at the BASELINE init); elsewhere
-the deviation is bounded by the int8 path's own noise floor (the oracle's
-int8-vs-fp32 distance)."""
+code that flips at a rounding tie moves every later block; the oracle's own
+int8 ViT-L output moves by several percent under a 1e-7 perturbation of its
+first LayerNorm). So the free-running int8 graph is held to 1e-2 where the
+network is well conditioned (ViT-S / ViT-B at the BASELINE init), and
+everywhere else the int8 chain is checked teacher-forced: every block and the
+head, through the stage probes, on the GPU's own input to that stage, each
+within 1e-2 of the oracle's same-precision stage (the free-running distance
+is printed)."""
 from pathlib import Path
 
 import numpy as np
@@ -64,6 +67,34 @@ def test_fp16_vs_reference_python(cuda, dav2lib, models, tag, shape):
     assert rel < 1e-2
 
 
+def teacher_forced_int8(lib, ctx, sd, encoder, image, metric_max_depth=0.0):
+    """Every int8 stage on the GPU's own input to it, against the oracle's
+    same-precision stage: returns (max block error, head error), both max
+    relative. Block i is fed the GPU's block i-1 output; the head the GPU's
+    tapped residual streams."""
+    import ctypes
+
+    _, _, blocks, taps, _, _ = oracle.ENCODERS[encoder]
+    _, h, w = image.shape
+    x = np.ascontiguousarray(oracle.embed(sd, image, encoder, "int8"), np.float32)
+    worst, tapped = 0.0, []
+    for i in range(blocks):
+        out = np.empty_like(x)
+        rc = lib.dav2_probe_encoder_block(ctx, 1, w, h, i, x.ctypes.data, out.ctypes.data, None, None)
+        assert rc == 0, lib.dav2_last_error()
+        want = oracle.encoder_block(sd, x, i, encoder, "int8")
+        worst = max(worst, errs(out, want)[0])
+        x = out
+        if i in taps:
+            tapped.append(x)
+    depth = np.empty((h, w), np.float32)
+    tap_x = np.ascontiguousarray(np.stack(tapped), np.float32)
+    assert lib.dav2_probe_head(ctx, 1, w, h, tap_x.ctypes.data, depth.ctypes.data) == 0, lib.dav2_last_error()
+    feats = [oracle.layer_norm(t, sd["pretrained.norm.weight"], sd["pretrained.norm.bias"]) for t in tapped]
+    want = oracle.dpt_forward(sd, feats, w // 14, h // 14, encoder, "int8", metric_max_depth)
+    return worst, errs(depth, want)[0]
+
+
 @pytest.mark.parametrize("tag", ["base", "strong"])
 def test_int8_vs_oracle_same_precision(cuda, dav2lib, models, tag):
     fx = np.load(G / "model_vits.npz")
@@ -71,16 +102,16 @@ def test_int8_vs_oracle_same_precision(cuda, dav2lib, models, tag):
     ctx = context(dav2lib, models[tag][0], flags=capi.FLAGS["int8"])
     try:
         got = infer_tensor(dav2lib, ctx, img)
+        stages = teacher_forced_int8(dav2lib, ctx, models[tag][1], "vits", img)
     finally:
         dav2lib.dav2_destroy(ctx)
     want = oracle.infer_tensor(models[tag][1], img, "vits", precision="int8")
     rel, rng_rel = errs(got, want)
-    floor, _ = errs(want, fx[f"{tag}_126x126_out"])  # int8 vs fp32, both from the reference's algorithm
-    print(f"int8 {tag}: rel {rel:.2e} range-rel {rng_rel:.2e} (int8 noise floor {floor:.2e})")
+    print(f"int8 {tag}: free-running rel {rel:.2e} range-rel {rng_rel:.2e}; teacher-forced blocks {stages[0]:.2e} "
+          f"head {stages[1]:.2e}")
+    assert stages[0] < 1e-2 and stages[1] < 1e-2
     if tag == "base":
         assert rel < 1e-2
-    else:
-        assert rel < max(1e-2, 3 * floor)
 
 
 def test_infer_bgr8_vs_reference_python(cuda, dav2lib, models):
@@ -146,13 +177,17 @@ def test_larger_encoders_vs_oracle(cuda, dav2lib, tmp_path, encoder):
     int8 = oracle.infer_tensor(sd, img, encoder, precision="int8")
     rel16, _ = errs(got["fp16"], fp32)
     rel8, rr8 = errs(got["int8"], int8)
-    floor, _ = errs(int8, fp32)
-    print(f"{encoder}: fp16 vs fp32 {rel16:.2e}; int8 vs int8 {rel8:.2e} range-rel {rr8:.2e} (floor {floor:.2e})")
+    ctx = context(dav2lib, path, encoder, flags=capi.FLAGS["int8"])
+    try:
+        stages = teacher_forced_int8(dav2lib, ctx, sd, encoder, img)
+    finally:
+        dav2lib.dav2_destroy(ctx)
+    print(f"{encoder}: fp16 vs fp32 {rel16:.2e}; int8 free-running {rel8:.2e} range-rel {rr8:.2e}; teacher-forced "
+          f"blocks {stages[0]:.2e} head {stages[1]:.2e}")
     assert rel16 < 1e-2
+    assert stages[0] < 1e-2 and stages[1] < 1e-2
     if encoder == "vitb":
         assert rel8 < 1e-2
-    else:
-        assert rel8 < max(1e-2, 3 * floor)
 
 
 def test_errors_and_counters(cuda, dav2lib, models):
@@ -227,10 +262,15 @@ def test_metric_int8_vs_oracle_same_precision(cuda, dav2lib, metric_models):
         dav2lib.dav2_destroy(ctx)
     want = oracle.infer_tensor(metric_models["strong"][1], img, "vits", precision="int8", metric_max_depth=20.0)
     rel, rng_rel = errs(got, want)
-    floor, floor_rng = errs(want, fx["strong_126x126_out"])
-    print(f"metric int8: rel {rel:.2e} range-rel {rng_rel:.2e} (int8 floor {floor:.2e} / {floor_rng:.2e})")
+    ctx = context(dav2lib, metric_models["strong"][0], flags=capi.FLAGS["int8"])
+    try:
+        stages = teacher_forced_int8(dav2lib, ctx, metric_models["strong"][1], "vits", img, metric_max_depth=20.0)
+    finally:
+        dav2lib.dav2_destroy(ctx)
+    print(f"metric int8: free-running rel {rel:.2e} range-rel {rng_rel:.2e}; teacher-forced blocks {stages[0]:.2e} "
+          f"head {stages[1]:.2e}")
     assert rel < 1e-2
-    assert rng_rel < max(5e-2, 3 * floor_rng)
+    assert stages[0] < 1e-2 and stages[1] < 1e-2
 
 
 @pytest.mark.parametrize("kind", ["relative", "metric"])

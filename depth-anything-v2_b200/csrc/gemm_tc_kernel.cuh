@@ -108,18 +108,43 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParamsDev& p, const uin
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = kInt8 ? (float)(int32_t)acc[j] : __uint_as_float(acc[j]);
+    // per-column parameters as 16-byte loads for whole, aligned chunks
+    const bool vec_sw = full && (reinterpret_cast<uintptr_t>(p.s_w) & 15u) == 0;
+    const bool vec_b = full && (reinterpret_cast<uintptr_t>(p.bias) & 15u) == 0;
     if (f & kEpiDequant) {
         const float si = __ldg(p.s_in + r);
+        if (vec_sw) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const float sw = (full || col0 + j < p.n) ? __ldg(p.s_w + col0 + j) : 0.f;
-            v[j] = __fmul_rn(__fmul_rn(v[j], si), sw);
+            for (int j = 0; j < 32; j += 4) {
+                const float4 sw = __ldg(reinterpret_cast<const float4*>(p.s_w + col0 + j));
+                v[j] = __fmul_rn(__fmul_rn(v[j], si), sw.x);
+                v[j + 1] = __fmul_rn(__fmul_rn(v[j + 1], si), sw.y);
+                v[j + 2] = __fmul_rn(__fmul_rn(v[j + 2], si), sw.z);
+                v[j + 3] = __fmul_rn(__fmul_rn(v[j + 3], si), sw.w);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float sw = (full || col0 + j < p.n) ? __ldg(p.s_w + col0 + j) : 0.f;
+                v[j] = __fmul_rn(__fmul_rn(v[j], si), sw);
+            }
         }
     }
     if (f & kEpiBias) {
+        if (vec_b) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-            if (full || col0 + j < p.n) v[j] = __fadd_rn(v[j], __ldg(p.bias + col0 + j));
+            for (int j = 0; j < 32; j += 4) {
+                const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + j));
+                v[j] = __fadd_rn(v[j], b.x);
+                v[j + 1] = __fadd_rn(v[j + 1], b.y);
+                v[j + 2] = __fadd_rn(v[j + 2], b.z);
+                v[j + 3] = __fadd_rn(v[j + 3], b.w);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (full || col0 + j < p.n) v[j] = __fadd_rn(v[j], __ldg(p.bias + col0 + j));
+        }
     }
     if (f & kEpiGelu) {
 #pragma unroll
@@ -237,9 +262,15 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParamsDev& p, const uin
             img = r / p.rows_per_img;
             px = r % p.rows_per_img;
         }
-        float* o = reinterpret_cast<float*>(p.out) + img * p.img_stride + p.row_offset + px;
-        for (int j = 0; j < 32; ++j)
-            if (col0 + j < p.n) o[(uint64_t)(col0 + j) * p.col_stride] = v[j];
+        float* o = reinterpret_cast<float*>(p.out) + img * p.img_stride + p.row_offset + px +
+                   (uint64_t)col0 * p.col_stride;
+        if (full) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[(uint64_t)j * p.col_stride] = v[j];
+        } else {
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.n) o[(uint64_t)j * p.col_stride] = v[j];
+        }
         return;
     }
     // conv-transpose scatter (kernel == stride)

@@ -330,43 +330,35 @@ __device__ __forceinline__ float lerp_rn(float a, float b, float f) {
     return __fadd_rn(__fmul_rn(a, __fsub_rn(1.0f, f)), __fmul_rn(b, f));
 }
 
-// Planar form for many planes: one block per (output row, chunk of
-// kPlanesPerBlock planes). The row's x table (source columns, weight) is
-// computed once in shared memory and the y terms once per block, so the
-// per-element work is four loads, three lerps and one store.
-constexpr uint32_t kPlanesPerBlock = 8;
+// Planar form for many planes: a thread per output column of one row walks
+// a chunk of kPlanesPerBlock planes with its source columns and weights
+// computed once, so the per-element work is four loads, the three lerps and
+// one store with pointer increments.
+constexpr uint32_t kPlanesPerBlock = 16;
 
 template <typename TI, typename TO>
-__global__ void __launch_bounds__(256) bilinear_align_rows_kernel(TO* __restrict__ out, const TI* __restrict__ in,
-                                                                  uint32_t iw, uint32_t ih, uint32_t ow, uint32_t oh,
-                                                                  uint32_t planes) {
-    extern __shared__ uint32_t tab[];  // [ow] x0 | x1 << 16, then [ow] fx
-    float* tfx = reinterpret_cast<float*>(tab + ow);
-    const uint32_t y = blockIdx.x;
-    for (uint32_t x = threadIdx.x; x < ow; x += blockDim.x) {
-        uint32_t x0, x1;
-        float fx;
-        align_coord(x, iw, ow, x0, x1, fx);
-        tab[x] = x0 | (x1 << 16);
-        tfx[x] = fx;
-    }
-    uint32_t y0, y1;
-    float fy;
+__global__ void __launch_bounds__(1024) bilinear_align_rows_kernel(TO* __restrict__ out, const TI* __restrict__ in,
+                                                                   uint32_t iw, uint32_t ih, uint32_t ow, uint32_t oh,
+                                                                   uint32_t planes) {
+    const uint32_t x = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t y = blockIdx.y;
+    if (x >= ow) return;
+    uint32_t x0, x1, y0, y1;
+    float fx, fy;
+    align_coord(x, iw, ow, x0, x1, fx);
     align_coord(y, ih, oh, y0, y1, fy);
-    __syncthreads();
-    const uint32_t c0 = blockIdx.y * kPlanesPerBlock;
+    const float gx = __fsub_rn(1.0f, fx), gy = __fsub_rn(1.0f, fy);
+    const uint32_t c0 = blockIdx.z * kPlanesPerBlock;
     const uint32_t c1 = min(c0 + kPlanesPerBlock, planes);
-    for (uint32_t c = c0; c < c1; ++c) {
-        const TI* r0 = in + ((uint64_t)c * ih + y0) * iw;
-        const TI* r1 = in + ((uint64_t)c * ih + y1) * iw;
-        TO* o = out + ((uint64_t)c * oh + y) * ow;
-        for (uint32_t x = threadIdx.x; x < ow; x += blockDim.x) {
-            const uint32_t t = tab[x], x0 = t & 0xffffu, x1 = t >> 16;
-            const float fx = tfx[x];
-            const float top = lerp_rn(to_f(__ldg(r0 + x0)), to_f(__ldg(r0 + x1)), fx);
-            const float bot = lerp_rn(to_f(__ldg(r1 + x0)), to_f(__ldg(r1 + x1)), fx);
-            o[x] = from_f<TO>(lerp_rn(top, bot, fy));
-        }
+    const uint64_t in_plane = (uint64_t)iw * ih, out_plane = (uint64_t)ow * oh;
+    const TI* r0 = in + c0 * in_plane + (uint64_t)y0 * iw;
+    const TI* r1 = in + c0 * in_plane + (uint64_t)y1 * iw;
+    TO* o = out + c0 * out_plane + (uint64_t)y * ow + x;
+    for (uint32_t c = c0; c < c1; ++c, r0 += in_plane, r1 += in_plane, o += out_plane) {
+        // the shader's order: a*(1-f) + b*f, each product and sum rounded
+        const float top = __fadd_rn(__fmul_rn(to_f(__ldg(r0 + x0)), gx), __fmul_rn(to_f(__ldg(r0 + x1)), fx));
+        const float bot = __fadd_rn(__fmul_rn(to_f(__ldg(r1 + x0)), gx), __fmul_rn(to_f(__ldg(r1 + x1)), fx));
+        *o = from_f<TO>(__fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, fy)));
     }
 }
 
@@ -752,6 +744,20 @@ __global__ void __launch_bounds__(128) im2col_quantize_kernel(
     }
 }
 
+// Four codes q8(x * inv) (x * inv rounded once, clamped to +-127, rounded to
+// the nearest integer, ties to even) packed little-endian: the rounding is
+// the f32 addition of 1.5*2^23, whose low mantissa byte is the code.
+__device__ __forceinline__ uint32_t q8x4_mul(float v0, float v1, float v2, float v3, float inv) {
+    constexpr float C = 12582912.0f;
+    const float t0 = __fadd_rn(fminf(fmaxf(__fmul_rn(v0, inv), -127.0f), 127.0f), C);
+    const float t1 = __fadd_rn(fminf(fmaxf(__fmul_rn(v1, inv), -127.0f), 127.0f), C);
+    const float t2 = __fadd_rn(fminf(fmaxf(__fmul_rn(v2, inv), -127.0f), 127.0f), C);
+    const float t3 = __fadd_rn(fminf(fmaxf(__fmul_rn(v3, inv), -127.0f), 127.0f), C);
+    const uint32_t lo = __byte_perm(__float_as_uint(t0), __float_as_uint(t1), 0x0040);
+    const uint32_t hi = __byte_perm(__float_as_uint(t2), __float_as_uint(t3), 0x0040);
+    return __byte_perm(lo, hi, 0x5410);
+}
+
 // Per-pixel channel abs-max of planar [B][C][HW] maps -> [B][HW] (one
 // thread per pixel, coalesced along pixels for each channel).
 __global__ void __launch_bounds__(256) pixel_absmax_kernel(float* __restrict__ out, const float* __restrict__ in,
@@ -778,20 +784,20 @@ __global__ void __launch_bounds__(256) pixel_absmax_kernel(float* __restrict__ o
 // channel abs-maxima over the 3x3 neighbourhood (padding contributes 0), so
 // the exact row scale max(absmax/127, 1e-8) is known before any code is
 // formed. A block quantizes kIm2colPixels consecutive pixels of one image
-// row: warps walk the channels, lanes the pixels (coalesced loads along the
-// row for every channel and tap), codes x*(1/scale) go to a shared tile in
-// (ky, kx, c) column order (rows padded by 4 bytes: conflict-free byte
-// stores), then the rows are written out coalesced, padded with zero
-// columns to kp bytes.
+// row: lanes walk the pixels, warps four channels at a time (coalesced loads
+// along the row for every channel and tap), codes x*(1/scale) go to a shared
+// tile as 4-code words in (ky, kx, c) column order (rows padded to an odd
+// word count: conflict-free stores), then the rows are written out
+// coalesced, padded with zero columns to kp bytes.
 constexpr uint32_t kIm2colPixels = 32;
 
 __global__ void __launch_bounds__(256) im2col_quantize_3x3_planar_kernel(
     uint8_t* __restrict__ codes, float* __restrict__ scales, const float* __restrict__ in,
     const float* __restrict__ pix_absmax, uint32_t c, uint32_t h, uint32_t w, uint32_t kp) {
     extern __shared__ uint32_t smem_words[];
-    const uint32_t stride = kp + 4;  // bytes per shared row
-    uint8_t* tile = reinterpret_cast<uint8_t*>(smem_words);
-    float* inv_s = reinterpret_cast<float*>(tile + (size_t)kIm2colPixels * stride);
+    const uint32_t stride_w = kp / 4 + 1;  // words per shared row (odd: conflict-free word stores)
+    uint32_t* tile = smem_words;
+    float* inv_s = reinterpret_cast<float*>(tile + (size_t)kIm2colPixels * stride_w);
     const uint32_t tiles_x = (w + kIm2colPixels - 1) / kIm2colPixels;
     const uint32_t y = (blockIdx.x / tiles_x) % h;
     const uint64_t img = (uint64_t)blockIdx.x / ((uint64_t)tiles_x * h);
@@ -816,30 +822,31 @@ __global__ void __launch_bounds__(256) im2col_quantize_3x3_planar_kernel(
         }
     }
     __syncthreads();
-    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const float inv = inv_s[lane];
-    const int x = (int)(x0 + lane);
-    const float* plane0 = in + img * (uint64_t)c * h * w;
-    for (uint32_t ch = warp; ch < c; ch += blockDim.x >> 5) {
-        const float* plane = plane0 + (uint64_t)ch * h * w;
-        for (uint32_t tap = 0; tap < 9; ++tap) {
-            const int yy = (int)y + (int)(tap / 3) - 1, xx = x + (int)(tap % 3) - 1;
-            float v = 0.f;
-            if (lane < np && yy >= 0 && yy < (int)h && xx >= 0 && xx < (int)w) v = __ldg(plane + (uint64_t)yy * w + xx);
-            tile[lane * stride + tap * c + ch] = (uint8_t)q8(__fmul_rn(v, inv));
+    const uint64_t hw = (uint64_t)h * w;
+    const float* plane0 = in + img * (uint64_t)c * hw;
+    uint32_t* my_row = tile + lane * stride_w;
+    const uint64_t step = (uint64_t)(4 * nwarps) * hw;  // pointer step between a warp's channel groups
+    for (uint32_t tap = 0; tap < 9; ++tap) {
+        const int yy = (int)y + (int)(tap / 3) - 1, xx = (int)(x0 + lane) + (int)(tap % 3) - 1;
+        const bool valid = lane < np && yy >= 0 && yy < (int)h && xx >= 0 && xx < (int)w;
+        const float* q = plane0 + (valid ? (uint64_t)yy * w + xx : 0) + (uint64_t)(4 * warp) * hw;
+        uint32_t* dst = my_row + tap * (c / 4) + warp;
+        // four channels per step: four coalesced loads (one per plane) -> one code word
+        for (uint32_t ch = 4 * warp; ch < c; ch += 4 * nwarps, q += step, dst += nwarps) {
+            const float v0 = valid ? __ldg(q) : 0.f, v1 = valid ? __ldg(q + hw) : 0.f;
+            const float v2 = valid ? __ldg(q + 2 * hw) : 0.f, v3 = valid ? __ldg(q + 3 * hw) : 0.f;
+            *dst = q8x4_mul(v0, v1, v2, v3, inv);
         }
     }
     __syncthreads();
-    // rows out: 4-byte words, zero columns beyond 9*c
-    const uint32_t words = kp / 4, cols = 9 * c;
-    for (uint32_t i = threadIdx.x; i < np * words; i += blockDim.x) {
-        const uint32_t r = i / words, wd = i % words;
-        const uint8_t* src = tile + r * stride + 4 * wd;
-        uint32_t v = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            if (4 * wd + j < cols) v |= (uint32_t)src[j] << (8 * j);
-        reinterpret_cast<uint32_t*>(codes + (row0 + r) * kp)[wd] = v;
+    // rows out, a warp per row, 4-byte words (columns beyond 9*c are zero)
+    const uint32_t words = kp / 4, used = 9 * c / 4;
+    for (uint32_t r = warp; r < np; r += nwarps) {
+        const uint32_t* src = tile + r * stride_w;
+        uint32_t* o = reinterpret_cast<uint32_t*>(codes + (row0 + r) * kp);
+        for (uint32_t wd = lane; wd < words; wd += 32) o[wd] = wd < used ? src[wd] : 0u;
     }
 }
 
@@ -851,6 +858,7 @@ int launch_im2col_quantize_3x3_planar(uint8_t* codes, float* scales, float* pix_
     if (kp % 4 || kp < 9 * c) return set_error(DAV2CUDA_INVALID_ARGUMENT, "im2col 3x3: row width");
     const uint64_t pixels = (uint64_t)batch * h * w;
     pixel_absmax_kernel<<<(unsigned)((pixels + 255) / 256), 256, 0, st>>>(pix_absmax, in, c, h * w, pixels);
+    if (c % 4) return set_error(DAV2CUDA_INVALID_ARGUMENT, "im2col 3x3: channels % 4");
     const size_t smem = (size_t)kIm2colPixels * (kp + 4) + kIm2colPixels * 4;
     if (smem > 200 * 1024) return set_error(DAV2CUDA_INVALID_ARGUMENT, "im2col 3x3: too many channels");
     if (cudaFuncSetAttribute(im2col_quantize_3x3_planar_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -956,15 +964,10 @@ int launch_sigmoid_scale(float* out, const float* in, uint64_t n, float s, cudaS
 template <typename TI, typename TO>
 int launch_bilinear_align(TO* out, const TI* in, uint32_t iw, uint32_t ih, uint32_t ow, uint32_t oh,
                           uint32_t planes, cudaStream_t st) {
-    if (planes >= kPlanesPerBlock && iw <= 65535 && oh <= 2147483647u &&
-        (planes + kPlanesPerBlock - 1) / kPlanesPerBlock <= 65535 && (size_t)ow * 8 <= 96 * 1024) {
-        dim3 grid(oh, (planes + kPlanesPerBlock - 1) / kPlanesPerBlock);
-        const size_t smem = (size_t)ow * 8;
-        if (smem > 48 * 1024 &&
-            cudaFuncSetAttribute(bilinear_align_rows_kernel<TI, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem) != cudaSuccess)
-            return set_error(DAV2CUDA_LAUNCH_FAILED, "bilinear_align_true: cannot set shared memory size");
-        bilinear_align_rows_kernel<TI, TO><<<grid, 256, smem, st>>>(out, in, iw, ih, ow, oh, planes);
+    if (planes >= kPlanesPerBlock && (planes + kPlanesPerBlock - 1) / kPlanesPerBlock <= 65535 && oh <= 65535) {
+        const uint32_t threads = std::min<uint32_t>((ow + 31) / 32 * 32, 1024u);
+        dim3 grid((ow + threads - 1) / threads, oh, (planes + kPlanesPerBlock - 1) / kPlanesPerBlock);
+        bilinear_align_rows_kernel<TI, TO><<<grid, threads, 0, st>>>(out, in, iw, ih, ow, oh, planes);
         return check_launch("bilinear_align_true");
     }
     dim3 grid((ow + 127) / 128, oh, planes < 65535 ? planes : 65535);

@@ -556,7 +556,11 @@ def main():
 
         import torch.distributed as dist
 
-        # host-side group: barrier + max-over-ranks only; nothing on the data path
+        # host-side group: barrier + max-over-ranks only; nothing on the data path.
+        # Loopback rendezvous: gloo binds the loopback interface (the host name
+        # may not resolve on the GPU box).
+        if os.environ.get("MASTER_ADDR", "127.0.0.1") in ("127.0.0.1", "localhost"):
+            os.environ.setdefault("GLOO_SOCKET_IFNAME", "lo")
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
 
     def barrier():

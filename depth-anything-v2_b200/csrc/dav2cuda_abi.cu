@@ -773,6 +773,14 @@ int dav2cuda_conv3x3_int8_up2(float* output, const float* input, const uint32_t*
     g.s_w = weight_scales;
     g.bias = bias;
     g.out = conv;
+    if (oc % 32 == 0) {
+        // channels-last conv output (thread-row TMA epilogue), then the upsample
+        // writes the planar result
+        g.out_kind = kOutF32Rows;
+        g.ldo = oc;
+        if (int rc2 = launch_gemm(g, st)) return rc2;
+        return launch_bilinear_nhwc_to_planar(output, conv, batch, h, w, oc, 2 * h, 2 * w, st);
+    }
     g.out_kind = kOutF32Planar;
     g.rows_per_img = (uint32_t)hw;
     g.img_stride = (uint64_t)oc * hw;

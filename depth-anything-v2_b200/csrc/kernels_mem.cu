@@ -354,11 +354,65 @@ __global__ void __launch_bounds__(1024) bilinear_align_rows_kernel(TO* __restric
     const TI* r0 = in + c0 * in_plane + (uint64_t)y0 * iw;
     const TI* r1 = in + c0 * in_plane + (uint64_t)y1 * iw;
     TO* o = out + c0 * out_plane + (uint64_t)y * ow + x;
+#pragma unroll 4
     for (uint32_t c = c0; c < c1; ++c, r0 += in_plane, r1 += in_plane, o += out_plane) {
         // the shader's order: a*(1-f) + b*f, each product and sum rounded
         const float top = __fadd_rn(__fmul_rn(to_f(__ldg(r0 + x0)), gx), __fmul_rn(to_f(__ldg(r0 + x1)), fx));
         const float bot = __fadd_rn(__fmul_rn(to_f(__ldg(r1 + x0)), gx), __fmul_rn(to_f(__ldg(r1 + x1)), fx));
         *o = from_f<TO>(__fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, fy)));
+    }
+}
+
+// Channels-last f32 [B][ih][iw][C] -> planar f32 [B][C][oh][ow] with the same
+// align-corners arithmetic: a block per (image, output row, 32 channels) and
+// segment of kNhwcSeg output columns; lanes are channels, so each source
+// pixel read is one 128-byte line; results go through a shared tile
+// [32][kNhwcSeg + 1] and leave as coalesced planar rows.
+constexpr uint32_t kNhwcSeg = 320;
+
+__global__ void __launch_bounds__(256) bilinear_nhwc_to_planar_kernel(float* __restrict__ out,
+                                                                      const float* __restrict__ in, uint32_t ih,
+                                                                      uint32_t iw, uint32_t c, uint32_t oh,
+                                                                      uint32_t ow) {
+    __shared__ float tile[32 * (kNhwcSeg + 1)];
+    __shared__ uint32_t tx[kNhwcSeg];
+    __shared__ float tf[kNhwcSeg];
+    const uint32_t groups = c / 32;
+    const uint32_t g = blockIdx.x % groups;
+    const uint32_t y = (blockIdx.x / groups) % oh;
+    const uint64_t b = blockIdx.x / ((uint64_t)groups * oh);
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t y0, y1;
+    float fy;
+    align_coord(y, ih, oh, y0, y1, fy);
+    const float gy = __fsub_rn(1.0f, fy);
+    const float* r0 = in + ((b * ih + y0) * iw) * c + 32u * g + lane;
+    const float* r1 = in + ((b * ih + y1) * iw) * c + 32u * g + lane;
+    for (uint32_t xs = 0; xs < ow; xs += kNhwcSeg) {
+        const uint32_t n = min(kNhwcSeg, ow - xs);
+        __syncthreads();  // the previous segment's tile has been written out
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+            uint32_t x0, x1;
+            float fx;
+            align_coord(xs + i, iw, ow, x0, x1, fx);
+            tx[i] = x0 | (x1 << 16);
+            tf[i] = fx;
+        }
+        __syncthreads();
+        for (uint32_t i = warp; i < n; i += 8) {
+            const uint32_t t = tx[i], x0 = t & 0xffffu, x1 = t >> 16;
+            const float fx = tf[i], gx = __fsub_rn(1.0f, fx);
+            const float a = __ldg(r0 + (uint64_t)x0 * c), bb = __ldg(r0 + (uint64_t)x1 * c);
+            const float cc = __ldg(r1 + (uint64_t)x0 * c), d = __ldg(r1 + (uint64_t)x1 * c);
+            const float top = __fadd_rn(__fmul_rn(a, gx), __fmul_rn(bb, fx));
+            const float bot = __fadd_rn(__fmul_rn(cc, gx), __fmul_rn(d, fx));
+            tile[lane * (kNhwcSeg + 1) + i] = __fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, fy));
+        }
+        __syncthreads();
+        for (uint32_t ch = warp; ch < 32; ch += 8) {
+            float* o = out + ((b * c + 32u * g + ch) * oh + y) * ow + xs;
+            for (uint32_t i = lane; i < n; i += 32) o[i] = tile[ch * (kNhwcSeg + 1) + i];
+        }
     }
 }
 
@@ -834,6 +888,7 @@ __global__ void __launch_bounds__(256) im2col_quantize_3x3_planar_kernel(
         const float* q = plane0 + (valid ? (uint64_t)yy * w + xx : 0) + (uint64_t)(4 * warp) * hw;
         uint32_t* dst = my_row + tap * (c / 4) + warp;
         // four channels per step: four coalesced loads (one per plane) -> one code word
+#pragma unroll 2
         for (uint32_t ch = 4 * warp; ch < c; ch += 4 * nwarps, q += step, dst += nwarps) {
             const float v0 = valid ? __ldg(q) : 0.f, v1 = valid ? __ldg(q + hw) : 0.f;
             const float v2 = valid ? __ldg(q + 2 * hw) : 0.f, v3 = valid ? __ldg(q + 3 * hw) : 0.f;
@@ -976,6 +1031,16 @@ int launch_bilinear_align(TO* out, const TI* in, uint32_t iw, uint32_t ih, uint3
 }
 template int launch_bilinear_align<float, float>(float*, const float*, uint32_t, uint32_t, uint32_t, uint32_t,
                                                  uint32_t, cudaStream_t);
+
+int launch_bilinear_nhwc_to_planar(float* out, const float* in, uint32_t batch, uint32_t ih, uint32_t iw, uint32_t c,
+                                   uint32_t oh, uint32_t ow, cudaStream_t st) {
+    if (c % 32 || iw > 65535 || !batch || !ih || !iw || !oh || !ow)
+        return set_error(DAV2CUDA_INVALID_ARGUMENT, "bilinear_nhwc_to_planar: channels % 32, width <= 65535");
+    const uint64_t blocks = (uint64_t)batch * oh * (c / 32);
+    if (blocks > 0x7fffffffull) return set_error(DAV2CUDA_INVALID_ARGUMENT, "bilinear_nhwc_to_planar: grid too large");
+    bilinear_nhwc_to_planar_kernel<<<(unsigned)blocks, 256, 0, st>>>(out, in, ih, iw, c, oh, ow);
+    return check_launch("bilinear_nhwc_to_planar");
+}
 
 int launch_minmax_batched(const float* in, float* ranges, uint64_t n, uint32_t batch, cudaStream_t st) {
     if (batch == 0 || batch > 65535) return set_error(DAV2CUDA_INVALID_ARGUMENT, "reduce_minmax: batch out of range");

@@ -20,7 +20,8 @@ def _free_port():
 
 
 def _rank(rank, world, port, batch, q):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      GLOO_SOCKET_IFNAME="lo")
     sys.path.insert(0, str(ROOT))
     import datetime
 

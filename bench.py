@@ -77,6 +77,8 @@ def parse(argv=None):
     ap.add_argument("--no-microbench", action="store_true", help="skip configurations 2, 3 and 5")
     ap.add_argument("--profile-only", action="store_true", help="print the per-operation profile and exit")
     ap.add_argument("--microbench-only", action="store_true", help="print configuration 2's operator timings and exit")
+    ap.add_argument("--microbench-op", action="append", choices=MICRO_OPS,
+                    help="with --microbench-only: time only this operation (repeatable)")
     return ap.parse_args(argv)
 
 
@@ -389,11 +391,17 @@ def _time_rotating(torch, fns, reps=6):
     return s.elapsed_time(e) / (reps * len(fns))
 
 
-def op_microbench(lib, torch, hbm_pk):
+MICRO_OPS = ("layer_norm", "gelu", "softmax", "conv3x3_int8_up2")
+
+
+def op_microbench(lib, torch, hbm_pk, ops=MICRO_OPS):
     """BASELINE configuration 2 through the operator C ABI (include/dav2cuda.h):
-    seeded N(0,1) inputs, the kernels the ABI runs, algorithmic bytes (every
-    tensor read once and written once) over the median event-timed launch."""
-    g = torch.Generator(device="cuda").manual_seed(0)
+    seeded N(0,1) inputs (a generator per operation, so a subset sees the same
+    inputs), the kernels the ABI runs, algorithmic bytes (every tensor read once
+    and written once) over the median event-timed launch."""
+    def gen(i):
+        return torch.Generator(device="cuda").manual_seed(i)
+
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     out = {}
 
@@ -407,6 +415,19 @@ def op_microbench(lib, torch, hbm_pk):
         if rc != 0:
             raise RuntimeError(f"{name}: {lib.dav2cuda_last_error().decode()}")
 
+    if "layer_norm" in ops:
+        _micro_layer_norm(lib, torch, gen(0), check, rec)
+    if "gelu" in ops:
+        _micro_gelu(lib, torch, gen(1), flush, check, rec)
+    if "softmax" in ops:
+        _micro_softmax(lib, torch, gen(2), flush, check, rec)
+    if "conv3x3_int8_up2" in ops:
+        _micro_conv(lib, torch, gen(3), flush, check, rec)
+    torch.cuda.empty_cache()
+    return out
+
+
+def _micro_layer_norm(lib, torch, g, check, rec):
     # (a) LayerNorm eps 1e-6, f32 [10960, 1024]: 90 MB per launch, ~20 us, so
     #     timed over back-to-back launches rotating over 4 buffer sets (360 MB)
     r, c = 10960, 1024
@@ -418,14 +439,18 @@ def op_microbench(lib, torch, hbm_pk):
     ms = _time_rotating(torch, fns)
     rec("layer_norm", ms, 2 * r * c * 4, [r, c], "layer_norm_warp_kernel",
         {"timing": "back-to-back launches over 4 buffer sets (360 MB > L2), ms per launch"})
-    del sets
+
+
+def _micro_gelu(lib, torch, g, flush, check, rec):
     # (b) erf-GELU f32 [10960, 4096]
     n = 10960 * 4096
     x = torch.randn(n, generator=g, device="cuda")
     y = torch.empty_like(x)
     ms = _time_kernel(torch, lambda: check(lib.dav2cuda_gelu(y.data_ptr(), x.data_ptr(), n, None), "gelu"), flush)
     rec("gelu", ms, 2 * n * 4, [10960, 4096], "gelu_kernel")
-    del x, y
+
+
+def _micro_softmax(lib, torch, g, flush, check, rec):
     # (c) row softmax over [8, 16, 1370, 1370] scores, scaled by 1/8
     rows, cols = 8 * 16 * 1370, 1370
     x = torch.randn((rows, cols), generator=g, device="cuda")
@@ -433,7 +458,9 @@ def op_microbench(lib, torch, hbm_pk):
     ms = _time_kernel(torch, lambda: check(lib.dav2cuda_softmax_rows(y.data_ptr(), x.data_ptr(), rows, cols, 0.125,
                                                                     None), "softmax"), flush)
     rec("softmax", ms, 2 * rows * cols * 4, [8, 16, 1370, 1370], "softmax_warp_kernel")
-    del x, y
+
+
+def _micro_conv(lib, torch, g, flush, check, rec):
     # (d) int8 3x3 pad-1 conv [8,256,148,148] (per-row im2col quantize, s8 GEMM,
     #     dequant) then 2x align-corners upsample -> [8,256,296,296]
     B, C, H, W, Co = 8, 256, 148, 148, 256
@@ -449,11 +476,8 @@ def op_microbench(lib, torch, hbm_pk):
         wsz, None), "conv3x3_int8_up2"), flush)
     ops = 2 * B * H * W * Co * C * 9
     rec("conv3x3_int8_up2", ms, B * C * H * W * 4 + Co * C * 9 + B * Co * 4 * H * W * 4, [B, C, H, W],
-        "im2col quantize + gemm_tc kind::i8 + bilinear_align",
+        "pixel abs-max + staged im2col quantize + gemm_tc kind::i8 (channels-last f32) + staged bilinear to planar",
         {"tops": round(ops / (ms * 1e-3) / 1e12, 1), "int_ops": ops})
-    del x, y, ws
-    torch.cuda.empty_cache()
-    return out
 
 
 def extra_configs(lib, torch, steps=5, warmup=2):
@@ -548,7 +572,8 @@ def main():
     rank, local, world = dist_env()
     torch.cuda.set_device(local)
     if args.microbench_only:
-        print(json.dumps(op_microbench(dav2_b200.load(), torch, hbm_peak_gbs()[0])), flush=True)
+        print(json.dumps(op_microbench(dav2_b200.load(), torch, hbm_peak_gbs()[0],
+                                       tuple(args.microbench_op or MICRO_OPS))), flush=True)
         return
     dist = None
     if world > 1:

@@ -773,7 +773,7 @@ int dav2cuda_conv3x3_int8_up2(float* output, const float* input, const uint32_t*
     g.s_w = weight_scales;
     g.bias = bias;
     g.out = conv;
-    if (oc % 32 == 0) {
+    if (bilinear_nhwc_to_planar_supported(w, oc, 2 * w)) {
         // channels-last conv output (thread-row TMA epilogue), then the upsample
         // writes the planar result
         g.out_kind = kOutF32Rows;

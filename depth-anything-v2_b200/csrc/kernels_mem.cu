@@ -364,54 +364,124 @@ __global__ void __launch_bounds__(1024) bilinear_align_rows_kernel(TO* __restric
 }
 
 // Channels-last f32 [B][ih][iw][C] -> planar f32 [B][C][oh][ow] with the same
-// align-corners arithmetic: a block per (image, output row, 32 channels) and
-// segment of kNhwcSeg output columns; lanes are channels, so each source
-// pixel read is one 128-byte line; results go through a shared tile
-// [32][kNhwcSeg + 1] and leave as coalesced planar rows.
-constexpr uint32_t kNhwcSeg = 320;
+// align-corners arithmetic. A block per (image, 32 channels, source row pair
+// k): it stages source rows k and k+1 of its channels ([2][iw][32] floats,
+// each pixel one 128-byte line read as float4 by 8 lanes, every load of a
+// thread issued before its first store) in shared memory with a 33-word
+// pixel stride (conflict-free staging stores and reads), then writes every
+// output row whose top source row is k (the last block also the rows on the
+// last source row). Each horizontal lerp of a staged row is computed once and
+// shared by all those output rows (about oh/ih of them), which halves the
+// shared-memory reads of a 2x upsample. Warps take channels, lanes output
+// columns: every output row leaves as coalesced stores from registers.
+constexpr uint32_t kNhwcPixelWords = 33;
+constexpr uint32_t kNhwcMaxSmem = 200 * 1024;
+constexpr uint32_t kNhwcStageLoads = 8;  // float4 loads in flight per thread while staging
 
-__global__ void __launch_bounds__(256) bilinear_nhwc_to_planar_kernel(float* __restrict__ out,
-                                                                      const float* __restrict__ in, uint32_t ih,
-                                                                      uint32_t iw, uint32_t c, uint32_t oh,
-                                                                      uint32_t ow) {
-    __shared__ float tile[32 * (kNhwcSeg + 1)];
-    __shared__ uint32_t tx[kNhwcSeg];
-    __shared__ float tf[kNhwcSeg];
-    const uint32_t groups = c / 32;
-    const uint32_t g = blockIdx.x % groups;
-    const uint32_t y = (blockIdx.x / groups) % oh;
-    const uint64_t b = blockIdx.x / ((uint64_t)groups * oh);
-    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// block (source row pair) of output row y: its top source row, the last
+// source row folded into the last pair
+__device__ __forceinline__ uint32_t nhwc_pair_of(uint32_t y, uint32_t ih, uint32_t oh, uint32_t pairs) {
     uint32_t y0, y1;
     float fy;
     align_coord(y, ih, oh, y0, y1, fy);
-    const float gy = __fsub_rn(1.0f, fy);
-    const float* r0 = in + ((b * ih + y0) * iw) * c + 32u * g + lane;
-    const float* r1 = in + ((b * ih + y1) * iw) * c + 32u * g + lane;
-    for (uint32_t xs = 0; xs < ow; xs += kNhwcSeg) {
-        const uint32_t n = min(kNhwcSeg, ow - xs);
-        __syncthreads();  // the previous segment's tile has been written out
-        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
-            uint32_t x0, x1;
-            float fx;
-            align_coord(xs + i, iw, ow, x0, x1, fx);
-            tx[i] = x0 | (x1 << 16);
-            tf[i] = fx;
+    return min(y0, pairs - 1);
+}
+
+__global__ void __launch_bounds__(256, 4) bilinear_nhwc_to_planar_kernel(float* __restrict__ out,
+                                                                         const float* __restrict__ in, uint32_t ih,
+                                                                         uint32_t iw, uint32_t c, uint32_t oh,
+                                                                         uint32_t ow) {
+    extern __shared__ float src_rows[];  // [2][iw][kNhwcPixelWords]
+    const uint32_t groups = c / 32, pairs = ih > 1 ? ih - 1 : 1;
+    // consecutive blocks take consecutive row pairs of one channel group:
+    // the blocks in flight write long runs of the same planes
+    const uint32_t k = blockIdx.x % pairs;
+    const uint32_t g = (blockIdx.x / pairs) % groups;
+    const uint64_t b = blockIdx.x / ((uint64_t)groups * pairs);
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t r0 = k, r1 = min(k + 1, ih - 1);
+    // output rows of this pair: [y_lo, y_hi) (the pair index is monotone in y)
+    const uint64_t y_est = (uint64_t)k * (oh - 1) / pairs;  // within a few rows of the first one
+    uint32_t y_lo = (uint32_t)(y_est < oh ? y_est : oh - 1);
+    while (y_lo > 0 && nhwc_pair_of(y_lo - 1, ih, oh, pairs) >= k) --y_lo;
+    while (y_lo < oh && nhwc_pair_of(y_lo, ih, oh, pairs) < k) ++y_lo;
+    uint32_t y_hi = y_lo;
+    while (y_hi < oh && nhwc_pair_of(y_hi, ih, oh, pairs) == k) ++y_hi;
+    if (y_lo >= y_hi) return;  // no output row on this pair (downsampling)
+
+    const uint32_t per_row = iw * 8;  // float4s per staged row
+    const float* base0 = in + ((b * ih + r0) * iw) * c + 32u * g;
+    const float* base1 = in + ((b * ih + r1) * iw) * c + 32u * g;
+    for (uint32_t i0 = threadIdx.x; i0 < 2 * per_row; i0 += kNhwcStageLoads * 256) {
+        float4 v[kNhwcStageLoads];
+#pragma unroll
+        for (uint32_t j = 0; j < kNhwcStageLoads; ++j) {
+            const uint32_t i = i0 + j * 256;
+            if (i < 2 * per_row) {
+                const uint32_t r = i >= per_row, rem = i - r * per_row;
+                v[j] = __ldg(reinterpret_cast<const float4*>((r ? base1 : base0) + (uint64_t)(rem >> 3) * c) +
+                             (rem & 7));
+            }
         }
-        __syncthreads();
-        for (uint32_t i = warp; i < n; i += 8) {
-            const uint32_t t = tx[i], x0 = t & 0xffffu, x1 = t >> 16;
-            const float fx = tf[i], gx = __fsub_rn(1.0f, fx);
-            const float a = __ldg(r0 + (uint64_t)x0 * c), bb = __ldg(r0 + (uint64_t)x1 * c);
-            const float cc = __ldg(r1 + (uint64_t)x0 * c), d = __ldg(r1 + (uint64_t)x1 * c);
-            const float top = __fadd_rn(__fmul_rn(a, gx), __fmul_rn(bb, fx));
-            const float bot = __fadd_rn(__fmul_rn(cc, gx), __fmul_rn(d, fx));
-            tile[lane * (kNhwcSeg + 1) + i] = __fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, fy));
+#pragma unroll
+        for (uint32_t j = 0; j < kNhwcStageLoads; ++j) {
+            const uint32_t i = i0 + j * 256;
+            if (i < 2 * per_row) {
+                const uint32_t r = i >= per_row, rem = i - r * per_row;
+                float* d = src_rows + (r * iw + (rem >> 3)) * kNhwcPixelWords + 4 * (rem & 7);
+                d[0] = v[j].x;
+                d[1] = v[j].y;
+                d[2] = v[j].z;
+                d[3] = v[j].w;
+            }
         }
-        __syncthreads();
-        for (uint32_t ch = warp; ch < 32; ch += 8) {
-            float* o = out + ((b * c + 32u * g + ch) * oh + y) * ow + xs;
-            for (uint32_t i = lane; i < n; i += 32) o[i] = tile[ch * (kNhwcSeg + 1) + i];
+    }
+    // x coordinates of the output columns, once per block
+    uint32_t* tab_x = reinterpret_cast<uint32_t*>(src_rows + 2 * iw * kNhwcPixelWords);  // x0 | x1 << 16
+    float* tab_f = reinterpret_cast<float*>(tab_x + ow);
+    for (uint32_t x = threadIdx.x; x < ow; x += blockDim.x) {
+        uint32_t x0, x1;
+        float fx;
+        align_coord(x, iw, ow, x0, x1, fx);
+        tab_x[x] = x0 | (x1 << 16);
+        tab_f[x] = fx;
+    }
+    __syncthreads();
+    const float* s0 = src_rows;
+    const float* s1 = src_rows + iw * kNhwcPixelWords;
+    const uint64_t plane = (uint64_t)oh * ow;
+    for (uint32_t yc = y_lo; yc < y_hi; yc += 2) {
+        // two output rows per pass: vertical weights, and which staged row is
+        // each one's top / bottom (rows 0 / 1 for all but the last pair)
+        const bool two = yc + 1 < y_hi;
+        uint32_t ya0, ya1, yb0 = r0, yb1 = r1;
+        float fa, fb = 0.f;
+        align_coord(yc, ih, oh, ya0, ya1, fa);
+        if (two) align_coord(yc + 1, ih, oh, yb0, yb1, fb);
+        const float ga = __fsub_rn(1.0f, fa), gb = __fsub_rn(1.0f, fb);
+        const bool plain = ya0 == r0 && ya1 != r0 && yb0 == r0 && yb1 != r0;
+        const bool ta = ya0 != r0, ba = ya1 != r0, tb = yb0 != r0, bb = yb1 != r0;
+#pragma unroll 1
+        for (uint32_t q = 0; q < 4; ++q) {
+            const uint32_t cw = warp + 8 * q;
+            float* oa = out + (b * c + 32u * g + cw) * plane + (uint64_t)yc * ow;
+            float* ob = oa + ow;
+            for (uint32_t x = lane; x < ow; x += 32) {
+                const uint32_t t = tab_x[x], x0 = t & 0xffffu, x1 = t >> 16;
+                const float fx = tab_f[x], gx = __fsub_rn(1.0f, fx);
+                // the shader's order: a*(1-f) + b*f, each product and sum rounded
+                const float h0 = __fadd_rn(__fmul_rn(s0[x0 * kNhwcPixelWords + cw], gx),
+                                           __fmul_rn(s0[x1 * kNhwcPixelWords + cw], fx));
+                const float h1 = __fadd_rn(__fmul_rn(s1[x0 * kNhwcPixelWords + cw], gx),
+                                           __fmul_rn(s1[x1 * kNhwcPixelWords + cw], fx));
+                if (plain) {
+                    oa[x] = __fadd_rn(__fmul_rn(h0, ga), __fmul_rn(h1, fa));
+                    if (two) ob[x] = __fadd_rn(__fmul_rn(h0, gb), __fmul_rn(h1, fb));
+                } else {
+                    oa[x] = __fadd_rn(__fmul_rn(ta ? h1 : h0, ga), __fmul_rn(ba ? h1 : h0, fa));
+                    if (two) ob[x] = __fadd_rn(__fmul_rn(tb ? h1 : h0, gb), __fmul_rn(bb ? h1 : h0, fb));
+                }
+            }
         }
     }
 }
@@ -800,36 +870,63 @@ __global__ void __launch_bounds__(128) im2col_quantize_kernel(
 
 // Four codes q8(x * inv) (x * inv rounded once, clamped to +-127, rounded to
 // the nearest integer, ties to even) packed little-endian: the rounding is
-// the f32 addition of 1.5*2^23, whose low mantissa byte is the code.
+// the f32 addition of 1.5*2^23, whose low mantissa byte is the code. For the
+// exact row abs-max m, inv = 1/max(m/127, 1e-8) gives |x * inv| <= 127 *
+// (1 + 3 * 2^-24) < 127.5, so only the lower clamp can act (on NaN: -127,
+// as fmaxf returns the other operand). It also must stay: with nothing
+// between them, the packed product and rounding addition were contracted
+// into one fused multiply-add, which rounds once and moves codes at
+// half-integers.
 __device__ __forceinline__ uint32_t q8x4_mul(float v0, float v1, float v2, float v3, float inv) {
     constexpr float C = 12582912.0f;
-    const float t0 = __fadd_rn(fminf(fmaxf(__fmul_rn(v0, inv), -127.0f), 127.0f), C);
-    const float t1 = __fadd_rn(fminf(fmaxf(__fmul_rn(v1, inv), -127.0f), 127.0f), C);
-    const float t2 = __fadd_rn(fminf(fmaxf(__fmul_rn(v2, inv), -127.0f), 127.0f), C);
-    const float t3 = __fadd_rn(fminf(fmaxf(__fmul_rn(v3, inv), -127.0f), 127.0f), C);
+    float q0, q1, q2, q3, t0, t1, t2, t3;
+    f2_mul(q0, q1, v0, v1, inv, inv);  // the same IEEE products, two per instruction
+    f2_mul(q2, q3, v2, v3, inv, inv);
+    q0 = fmaxf(q0, -127.0f);
+    q1 = fmaxf(q1, -127.0f);
+    q2 = fmaxf(q2, -127.0f);
+    q3 = fmaxf(q3, -127.0f);
+    f2_add(t0, t1, q0, q1, C, C);
+    f2_add(t2, t3, q2, q3, C, C);
     const uint32_t lo = __byte_perm(__float_as_uint(t0), __float_as_uint(t1), 0x0040);
     const uint32_t hi = __byte_perm(__float_as_uint(t2), __float_as_uint(t3), 0x0040);
     return __byte_perm(lo, hi, 0x5410);
 }
 
-// Per-pixel channel abs-max of planar [B][C][HW] maps -> [B][HW] (one
-// thread per pixel, coalesced along pixels for each channel).
-__global__ void __launch_bounds__(256) pixel_absmax_kernel(float* __restrict__ out, const float* __restrict__ in,
-                                                           uint32_t c, uint32_t hw, uint64_t pixels) {
-    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= pixels) return;
-    const uint64_t img = i / hw, px = i % hw;
-    const float* src = in + img * c * hw + px;
+// Per-pixel channel abs-max of planar [B][C][HW] maps -> [B][HW]. A block covers kAbsmaxPixels consecutive pixels; each pixel's channels are
+// split over kAbsmaxSplit threads (channel j goes to thread j % kAbsmaxSplit),
+// lanes walk pixels (coalesced plane reads), partial maxima meet in shared
+// memory.
+constexpr uint32_t kAbsmaxPixels = 64, kAbsmaxSplit = 4;
+
+__global__ void __launch_bounds__(kAbsmaxPixels * kAbsmaxSplit) pixel_absmax_kernel(
+    float* __restrict__ out, const float* __restrict__ in, uint32_t c, uint32_t hw, uint64_t pixels) {
+    __shared__ float part[kAbsmaxSplit][kAbsmaxPixels];
+    const uint32_t lp = threadIdx.x % kAbsmaxPixels, q = threadIdx.x / kAbsmaxPixels;
+    const uint64_t i = (uint64_t)blockIdx.x * kAbsmaxPixels + lp;
     float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
-    uint32_t ch = 0;
-    for (; ch + 4 <= c; ch += 4) {
-        m0 = fmaxf(m0, fabsf(__ldg(src + (uint64_t)ch * hw)));
-        m1 = fmaxf(m1, fabsf(__ldg(src + (uint64_t)(ch + 1) * hw)));
-        m2 = fmaxf(m2, fabsf(__ldg(src + (uint64_t)(ch + 2) * hw)));
-        m3 = fmaxf(m3, fabsf(__ldg(src + (uint64_t)(ch + 3) * hw)));
+    if (i < pixels) {
+        const uint64_t img = i / hw, px = i % hw;
+        const float* src = in + img * c * hw + px + (uint64_t)q * hw;
+        const uint64_t step = (uint64_t)kAbsmaxSplit * hw;
+        uint32_t ch = q;
+#pragma unroll 2
+        for (; ch + 3 * kAbsmaxSplit < c; ch += 4 * kAbsmaxSplit, src += 4 * step) {
+            m0 = fmaxf(m0, fabsf(__ldg(src)));
+            m1 = fmaxf(m1, fabsf(__ldg(src + step)));
+            m2 = fmaxf(m2, fabsf(__ldg(src + 2 * step)));
+            m3 = fmaxf(m3, fabsf(__ldg(src + 3 * step)));
+        }
+        for (; ch < c; ch += kAbsmaxSplit, src += step) m0 = fmaxf(m0, fabsf(__ldg(src)));
     }
-    for (; ch < c; ++ch) m0 = fmaxf(m0, fabsf(__ldg(src + (uint64_t)ch * hw)));
-    out[i] = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+    part[q][lp] = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+    __syncthreads();
+    if (q == 0 && i < pixels) {
+        float m = part[0][lp];
+#pragma unroll
+        for (uint32_t k = 1; k < kAbsmaxSplit; ++k) m = fmaxf(m, part[k][lp]);
+        out[i] = m;
+    }
 }
 
 // im2col_quantize_int8.glsl:26-84 for a 3x3, stride-1, pad-1 convolution of
@@ -837,21 +934,27 @@ __global__ void __launch_bounds__(256) pixel_absmax_kernel(float* __restrict__ o
 // pixel) abs-max over its C*9 im2col values is the maximum of the per-pixel
 // channel abs-maxima over the 3x3 neighbourhood (padding contributes 0), so
 // the exact row scale max(absmax/127, 1e-8) is known before any code is
-// formed. A block quantizes kIm2colPixels consecutive pixels of one image
-// row: lanes walk the pixels, warps four channels at a time (coalesced loads
-// along the row for every channel and tap), codes x*(1/scale) go to a shared
-// tile as 4-code words in (ky, kx, c) column order (rows padded to an odd
-// word count: conflict-free stores), then the rows are written out
-// coalesced, padded with zero columns to kp bytes.
+// formed. A block (8 warps) quantizes kIm2colPixels consecutive pixels of one
+// image row, kIm2colChunk channels at a time: the chunk's 3-row x
+// (kIm2colPixels+2)-pixel halo is staged channel-fastest in shared memory
+// (lanes walk the pixels, so every plane read is coalesced; one float4 store
+// per 4 channels), then a warp takes one pixel at a time, a lane 4 channels,
+// and walks the 9 taps: one float4 shared read, x*(1/scale) for each value,
+// one 4-code word, the warp's 32 words one 128-byte store into the pixel's
+// GEMM row at column tap*C + channel ((ky, kx, c) order). Columns [9C, kp)
+// are written zero.
 constexpr uint32_t kIm2colPixels = 32;
+constexpr uint32_t kIm2colChunk = 128;
+constexpr uint32_t kIm2colHalo = kIm2colPixels + 2;
+constexpr uint32_t kIm2colPixelWords = kIm2colChunk + 4;  // 16-byte rows; conflict-free float4 staging stores
+constexpr uint32_t kIm2colStageItems = 6;                  // (group, row) pairs in flight per warp while staging
 
 __global__ void __launch_bounds__(256) im2col_quantize_3x3_planar_kernel(
     uint8_t* __restrict__ codes, float* __restrict__ scales, const float* __restrict__ in,
     const float* __restrict__ pix_absmax, uint32_t c, uint32_t h, uint32_t w, uint32_t kp) {
-    extern __shared__ uint32_t smem_words[];
-    const uint32_t stride_w = kp / 4 + 1;  // words per shared row (odd: conflict-free word stores)
-    uint32_t* tile = smem_words;
-    float* inv_s = reinterpret_cast<float*>(tile + (size_t)kIm2colPixels * stride_w);
+    extern __shared__ float4 im2col_smem[];  // halo [3][kIm2colHalo][kIm2colPixelWords], then inv_s
+    float* halo = reinterpret_cast<float*>(im2col_smem);
+    float* inv_s = halo + 3 * kIm2colHalo * kIm2colPixelWords;
     const uint32_t tiles_x = (w + kIm2colPixels - 1) / kIm2colPixels;
     const uint32_t y = (blockIdx.x / tiles_x) % h;
     const uint64_t img = (uint64_t)blockIdx.x / ((uint64_t)tiles_x * h);
@@ -875,34 +978,81 @@ __global__ void __launch_bounds__(256) im2col_quantize_3x3_planar_kernel(
             inv_s[threadIdx.x] = 0.f;
         }
     }
-    __syncthreads();
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    const float inv = inv_s[lane];
     const uint64_t hw = (uint64_t)h * w;
     const float* plane0 = in + img * (uint64_t)c * hw;
-    uint32_t* my_row = tile + lane * stride_w;
-    const uint64_t step = (uint64_t)(4 * nwarps) * hw;  // pointer step between a warp's channel groups
-    for (uint32_t tap = 0; tap < 9; ++tap) {
-        const int yy = (int)y + (int)(tap / 3) - 1, xx = (int)(x0 + lane) + (int)(tap % 3) - 1;
-        const bool valid = lane < np && yy >= 0 && yy < (int)h && xx >= 0 && xx < (int)w;
-        const float* q = plane0 + (valid ? (uint64_t)yy * w + xx : 0) + (uint64_t)(4 * warp) * hw;
-        uint32_t* dst = my_row + tap * (c / 4) + warp;
-        // four channels per step: four coalesced loads (one per plane) -> one code word
-#pragma unroll 2
-        for (uint32_t ch = 4 * warp; ch < c; ch += 4 * nwarps, q += step, dst += nwarps) {
-            const float v0 = valid ? __ldg(q) : 0.f, v1 = valid ? __ldg(q + hw) : 0.f;
-            const float v2 = valid ? __ldg(q + 2 * hw) : 0.f, v3 = valid ? __ldg(q + 3 * hw) : 0.f;
-            *dst = q8x4_mul(v0, v1, v2, v3, inv);
+    for (uint32_t ch0 = 0; ch0 < c; ch0 += kIm2colChunk) {
+        const uint32_t groups = min(kIm2colChunk, c - ch0) / 4;  // 4-channel groups in this chunk
+        __syncthreads();  // inv_s written; the previous chunk's halo consumed
+        const uint32_t prs = groups * 3;  // (4-channel group, halo row) pairs, pair = 3 * group + row
+        // stage, halo pixels 0..31: lanes walk the pixels (coalesced plane
+        // reads), warps the pairs, kIm2colStageItems pairs' loads in flight
+        {
+            const int xx = (int)(x0 + lane) - 1;
+            const bool x_in = xx >= 0 && xx < (int)w;
+            for (uint32_t pr0 = warp; pr0 < prs; pr0 += kIm2colStageItems * 8) {
+                float4 v[kIm2colStageItems];
+#pragma unroll
+                for (uint32_t k = 0; k < kIm2colStageItems; ++k) {
+                    const uint32_t pr = pr0 + 8 * k, grp = pr / 3;
+                    const int yy = (int)y + (int)(pr - 3 * grp) - 1;
+                    v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (pr < prs && x_in && yy >= 0 && yy < (int)h) {
+                        const float* q = plane0 + (uint64_t)(ch0 + 4 * grp) * hw + (uint64_t)yy * w + xx;
+                        v[k].x = __ldg(q);
+                        v[k].y = __ldg(q + hw);
+                        v[k].z = __ldg(q + 2 * hw);
+                        v[k].w = __ldg(q + 3 * hw);
+                    }
+                }
+#pragma unroll
+                for (uint32_t k = 0; k < kIm2colStageItems; ++k) {
+                    const uint32_t pr = pr0 + 8 * k, grp = pr / 3;
+                    if (pr < prs)
+                        *reinterpret_cast<float4*>(halo + ((pr - 3 * grp) * kIm2colHalo + lane) * kIm2colPixelWords +
+                                                   4 * grp) = v[k];
+                }
+            }
+        }
+        // stage, halo pixels 32 and 33 of every pair
+        for (uint32_t i = threadIdx.x; i < 2 * prs; i += blockDim.x) {
+            const uint32_t pr = i >> 1, px = kIm2colPixels + (i & 1), grp = pr / 3, r = pr - 3 * grp;
+            const int yy = (int)y + (int)r - 1, xx = (int)(x0 + px) - 1;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (yy >= 0 && yy < (int)h && xx >= 0 && xx < (int)w) {
+                const float* q = plane0 + (uint64_t)(ch0 + 4 * grp) * hw + (uint64_t)yy * w + xx;
+                v.x = __ldg(q);
+                v.y = __ldg(q + hw);
+                v.z = __ldg(q + 2 * hw);
+                v.w = __ldg(q + 3 * hw);
+            }
+            *reinterpret_cast<float4*>(halo + (r * kIm2colHalo + px) * kIm2colPixelWords + 4 * grp) = v;
+        }
+        __syncthreads();
+        // codes: a warp per pixel (p = warp, warp + 8, ...), a lane per 4
+        // channels, the 9 taps unrolled (constant shared offsets)
+        if (lane < groups) {
+            const uint32_t tap_words = c / 4;
+            for (uint32_t p = warp; p < np; p += nwarps) {
+                const float inv = inv_s[p];
+                const float* hp = halo + p * kIm2colPixelWords + 4 * lane;
+                uint32_t* o = reinterpret_cast<uint32_t*>(codes + (row0 + p) * kp + ch0) + lane;
+#pragma unroll
+                for (uint32_t tap = 0; tap < 9; ++tap, o += tap_words) {
+                    const float4 v = *reinterpret_cast<const float4*>(
+                        hp + ((tap / 3) * kIm2colHalo + tap % 3) * kIm2colPixelWords);
+                    *o = q8x4_mul(v.x, v.y, v.z, v.w, inv);
+                }
+            }
         }
     }
-    __syncthreads();
-    // rows out, a warp per row, 4-byte words (columns beyond 9*c are zero)
+    // zero columns beyond 9*c, a warp per row
     const uint32_t words = kp / 4, used = 9 * c / 4;
-    for (uint32_t r = warp; r < np; r += nwarps) {
-        const uint32_t* src = tile + r * stride_w;
-        uint32_t* o = reinterpret_cast<uint32_t*>(codes + (row0 + r) * kp);
-        for (uint32_t wd = lane; wd < words; wd += 32) o[wd] = wd < used ? src[wd] : 0u;
-    }
+    if (used < words)
+        for (uint32_t r = warp; r < np; r += nwarps) {
+            uint32_t* o = reinterpret_cast<uint32_t*>(codes + (row0 + r) * kp);
+            for (uint32_t wd = used + lane; wd < words; wd += 32) o[wd] = 0u;
+        }
 }
 
 }  // namespace
@@ -912,15 +1062,17 @@ int launch_im2col_quantize_3x3_planar(uint8_t* codes, float* scales, float* pix_
                                       cudaStream_t st) {
     if (kp % 4 || kp < 9 * c) return set_error(DAV2CUDA_INVALID_ARGUMENT, "im2col 3x3: row width");
     const uint64_t pixels = (uint64_t)batch * h * w;
-    pixel_absmax_kernel<<<(unsigned)((pixels + 255) / 256), 256, 0, st>>>(pix_absmax, in, c, h * w, pixels);
+    pixel_absmax_kernel<<<(unsigned)((pixels + kAbsmaxPixels - 1) / kAbsmaxPixels), kAbsmaxPixels * kAbsmaxSplit, 0,
+                          st>>>(pix_absmax, in, c, h * w, pixels);
     if (c % 4) return set_error(DAV2CUDA_INVALID_ARGUMENT, "im2col 3x3: channels % 4");
-    const size_t smem = (size_t)kIm2colPixels * (kp + 4) + kIm2colPixels * 4;
-    if (smem > 200 * 1024) return set_error(DAV2CUDA_INVALID_ARGUMENT, "im2col 3x3: too many channels");
+    const uint64_t blocks = (uint64_t)batch * h * ((w + kIm2colPixels - 1) / kIm2colPixels);
+    if (blocks > 0x7fffffffull) return set_error(DAV2CUDA_INVALID_ARGUMENT, "im2col 3x3: grid too large");
+    const size_t smem = (3 * kIm2colHalo * kIm2colPixelWords + kIm2colPixels) * sizeof(float);
     if (cudaFuncSetAttribute(im2col_quantize_3x3_planar_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
         return set_error(DAV2CUDA_LAUNCH_FAILED, "im2col 3x3: cannot set shared memory size");
-    const uint64_t blocks = (uint64_t)batch * h * ((w + kIm2colPixels - 1) / kIm2colPixels);
-    im2col_quantize_3x3_planar_kernel<<<(unsigned)blocks, 256, smem, st>>>(codes, scales, in, pix_absmax, c, h, w, kp);
+    im2col_quantize_3x3_planar_kernel<<<(unsigned)blocks, 256, smem, st>>>(codes, scales, in, pix_absmax, c, h, w,
+                                                                           kp);
     return check_launch("im2col_quantize_3x3_planar");
 }
 
@@ -1032,13 +1184,23 @@ int launch_bilinear_align(TO* out, const TI* in, uint32_t iw, uint32_t ih, uint3
 template int launch_bilinear_align<float, float>(float*, const float*, uint32_t, uint32_t, uint32_t, uint32_t,
                                                  uint32_t, cudaStream_t);
 
+bool bilinear_nhwc_to_planar_supported(uint32_t iw, uint32_t c, uint32_t ow) {
+    return c && c % 32 == 0 && iw && ((uint64_t)2 * iw * kNhwcPixelWords + 2ull * ow) * sizeof(float) <= kNhwcMaxSmem;
+}
+
 int launch_bilinear_nhwc_to_planar(float* out, const float* in, uint32_t batch, uint32_t ih, uint32_t iw, uint32_t c,
                                    uint32_t oh, uint32_t ow, cudaStream_t st) {
-    if (c % 32 || iw > 65535 || !batch || !ih || !iw || !oh || !ow)
-        return set_error(DAV2CUDA_INVALID_ARGUMENT, "bilinear_nhwc_to_planar: channels % 32, width <= 65535");
-    const uint64_t blocks = (uint64_t)batch * oh * (c / 32);
+    if (!bilinear_nhwc_to_planar_supported(iw, c, ow) || !batch || !ih || !oh || !ow ||
+        reinterpret_cast<uintptr_t>(in) % 16)
+        return set_error(DAV2CUDA_INVALID_ARGUMENT,
+                         "bilinear_nhwc_to_planar: channels % 32, source width fitting shared memory, 16-byte source");
+    const uint64_t blocks = (uint64_t)batch * (ih > 1 ? ih - 1 : 1) * (c / 32);
     if (blocks > 0x7fffffffull) return set_error(DAV2CUDA_INVALID_ARGUMENT, "bilinear_nhwc_to_planar: grid too large");
-    bilinear_nhwc_to_planar_kernel<<<(unsigned)blocks, 256, 0, st>>>(out, in, ih, iw, c, oh, ow);
+    const size_t smem = ((size_t)2 * iw * kNhwcPixelWords + 2 * (size_t)ow) * sizeof(float);
+    if (cudaFuncSetAttribute(bilinear_nhwc_to_planar_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+        return set_error(DAV2CUDA_LAUNCH_FAILED, "bilinear_nhwc_to_planar: cannot set shared memory size");
+    bilinear_nhwc_to_planar_kernel<<<(unsigned)blocks, 256, smem, st>>>(out, in, ih, iw, c, oh, ow);
     return check_launch("bilinear_nhwc_to_planar");
 }
 

@@ -48,7 +48,9 @@ template <typename TI, typename TO>
 int launch_bilinear_align(TO* out, const TI* in, uint32_t iw, uint32_t ih, uint32_t ow, uint32_t oh,
                           uint32_t planes, cudaStream_t st);
 // Align-corners bilinear of channels-last f32 maps [B][ih][iw][C] (C % 32 == 0)
-// into planar f32 [B][C][oh][ow].
+// into planar f32 [B][C][oh][ow]; _supported() says whether two source rows of
+// iw pixels and the ow-column coordinate table fit the kernel's shared memory.
+bool bilinear_nhwc_to_planar_supported(uint32_t iw, uint32_t c, uint32_t ow);
 int launch_bilinear_nhwc_to_planar(float* out, const float* in, uint32_t batch, uint32_t ih, uint32_t iw, uint32_t c,
                                    uint32_t oh, uint32_t ow, cudaStream_t st);
 int launch_minmax(const float* in, float* range, uint64_t n, cudaStream_t st);

@@ -355,8 +355,14 @@ def test_conv_transpose_int8_bit_exact(cuda, dav2lib, c, h, w, k):
     assert np.array_equal(host(out), oracle.conv_transpose_s8(pk, pw, sc, sw, b, w, h, c, c, k))
 
 
-def test_conv3x3_int8_up2(cuda, dav2lib):
-    B, C, H, W, O = 2, 256, 20, 18, 256
+@pytest.mark.parametrize("B,C,H,W,O", [(2, 256, 20, 18, 256),
+                                       # ragged pixel tiles, a partial channel chunk, zero pad columns (kp > 9C)
+                                       (1, 36, 9, 70, 32),
+                                       # two channel chunks (128 + 4), planar conv output (O % 32 != 0)
+                                       (1, 132, 5, 33, 48),
+                                       # 1x1 maps: every tap but the centre is padding
+                                       (3, 8, 1, 1, 64)])
+def test_conv3x3_int8_up2(cuda, dav2lib, B, C, H, W, O):
     x = rng(7).standard_normal((B, C, H, W)).astype(np.float32)
     wt = rng(8).uniform(-127, 127, (O, C, 3, 3)).astype(np.float32)
     b = rng(9).standard_normal(O).astype(np.float32)

@@ -461,25 +461,26 @@ __global__ void __launch_bounds__(256, 4) bilinear_nhwc_to_planar_kernel(float* 
         const float ga = __fsub_rn(1.0f, fa), gb = __fsub_rn(1.0f, fb);
         const bool plain = ya0 == r0 && ya1 != r0 && yb0 == r0 && yb1 != r0;
         const bool ta = ya0 != r0, ba = ya1 != r0, tb = yb0 != r0, bb = yb1 != r0;
-#pragma unroll 1
-        for (uint32_t q = 0; q < 4; ++q) {
-            const uint32_t cw = warp + 8 * q;
-            float* oa = out + (b * c + 32u * g + cw) * plane + (uint64_t)yc * ow;
-            float* ob = oa + ow;
-            for (uint32_t x = lane; x < ow; x += 32) {
-                const uint32_t t = tab_x[x], x0 = t & 0xffffu, x1 = t >> 16;
-                const float fx = tab_f[x], gx = __fsub_rn(1.0f, fx);
+        // row pointers of the warp's four channels (warp + 8q)
+        float* oa[4];
+#pragma unroll
+        for (uint32_t q = 0; q < 4; ++q) oa[q] = out + (b * c + 32u * g + warp + 8 * q) * plane + (uint64_t)yc * ow;
+        const float* w0 = s0 + warp;
+        const float* w1 = s1 + warp;
+        for (uint32_t x = lane; x < ow; x += 32) {
+            const uint32_t t = tab_x[x], o0 = (t & 0xffffu) * kNhwcPixelWords, o1 = (t >> 16) * kNhwcPixelWords;
+            const float fx = tab_f[x], gx = __fsub_rn(1.0f, fx);
+#pragma unroll
+            for (uint32_t q = 0; q < 4; ++q) {
                 // the shader's order: a*(1-f) + b*f, each product and sum rounded
-                const float h0 = __fadd_rn(__fmul_rn(s0[x0 * kNhwcPixelWords + cw], gx),
-                                           __fmul_rn(s0[x1 * kNhwcPixelWords + cw], fx));
-                const float h1 = __fadd_rn(__fmul_rn(s1[x0 * kNhwcPixelWords + cw], gx),
-                                           __fmul_rn(s1[x1 * kNhwcPixelWords + cw], fx));
+                const float h0 = __fadd_rn(__fmul_rn(w0[o0 + 8 * q], gx), __fmul_rn(w0[o1 + 8 * q], fx));
+                const float h1 = __fadd_rn(__fmul_rn(w1[o0 + 8 * q], gx), __fmul_rn(w1[o1 + 8 * q], fx));
                 if (plain) {
-                    oa[x] = __fadd_rn(__fmul_rn(h0, ga), __fmul_rn(h1, fa));
-                    if (two) ob[x] = __fadd_rn(__fmul_rn(h0, gb), __fmul_rn(h1, fb));
+                    oa[q][x] = __fadd_rn(__fmul_rn(h0, ga), __fmul_rn(h1, fa));
+                    if (two) oa[q][x + ow] = __fadd_rn(__fmul_rn(h0, gb), __fmul_rn(h1, fb));
                 } else {
-                    oa[x] = __fadd_rn(__fmul_rn(ta ? h1 : h0, ga), __fmul_rn(ba ? h1 : h0, fa));
-                    if (two) ob[x] = __fadd_rn(__fmul_rn(tb ? h1 : h0, gb), __fmul_rn(bb ? h1 : h0, fb));
+                    oa[q][x] = __fadd_rn(__fmul_rn(ta ? h1 : h0, ga), __fmul_rn(ba ? h1 : h0, fa));
+                    if (two) oa[q][x + ow] = __fadd_rn(__fmul_rn(tb ? h1 : h0, gb), __fmul_rn(bb ? h1 : h0, fb));
                 }
             }
         }
@@ -938,18 +939,21 @@ __global__ void __launch_bounds__(kAbsmaxPixels * kAbsmaxSplit) pixel_absmax_ker
 // image row, kIm2colChunk channels at a time: the chunk's 3-row x
 // (kIm2colPixels+2)-pixel halo is staged channel-fastest in shared memory
 // (lanes walk the pixels, so every plane read is coalesced; one float4 store
-// per 4 channels), then a warp takes one pixel at a time, a lane 4 channels,
-// and walks the 9 taps: one float4 shared read, x*(1/scale) for each value,
-// one 4-code word, the warp's 32 words one 128-byte store into the pixel's
+// per 4 channels), then kIm2colChunk/4 lanes take a pixel (a lane 4
+// channels) and walk the 9 taps: one float4 shared read, x*(1/scale) for each
+// value, one 4-code word, the pixel's words one contiguous store into its
 // GEMM row at column tap*C + channel ((ky, kx, c) order). Columns [9C, kp)
-// are written zero.
+// are written zero. A small chunk keeps 5 blocks per SM in flight, so one
+// block's staging loads overlap the others' code phases.
 constexpr uint32_t kIm2colPixels = 32;
-constexpr uint32_t kIm2colChunk = 128;
+constexpr uint32_t kIm2colChunk = 64;  // 27.7 KB of halo
+constexpr uint32_t kIm2colLanesPerPixel = kIm2colChunk / 4;
+constexpr uint32_t kIm2colPixelsPerWarp = 32 / kIm2colLanesPerPixel;
 constexpr uint32_t kIm2colHalo = kIm2colPixels + 2;
 constexpr uint32_t kIm2colPixelWords = kIm2colChunk + 4;  // 16-byte rows; conflict-free float4 staging stores
 constexpr uint32_t kIm2colStageItems = 6;                  // (group, row) pairs in flight per warp while staging
 
-__global__ void __launch_bounds__(256) im2col_quantize_3x3_planar_kernel(
+__global__ void __launch_bounds__(256, 5) im2col_quantize_3x3_planar_kernel(
     uint8_t* __restrict__ codes, float* __restrict__ scales, const float* __restrict__ in,
     const float* __restrict__ pix_absmax, uint32_t c, uint32_t h, uint32_t w, uint32_t kp) {
     extern __shared__ float4 im2col_smem[];  // halo [3][kIm2colHalo][kIm2colPixelWords], then inv_s
@@ -1029,14 +1033,16 @@ __global__ void __launch_bounds__(256) im2col_quantize_3x3_planar_kernel(
             *reinterpret_cast<float4*>(halo + (r * kIm2colHalo + px) * kIm2colPixelWords + 4 * grp) = v;
         }
         __syncthreads();
-        // codes: a warp per pixel (p = warp, warp + 8, ...), a lane per 4
-        // channels, the 9 taps unrolled (constant shared offsets)
-        if (lane < groups) {
+        // codes: kIm2colLanesPerPixel lanes per pixel (a lane per 4 channels),
+        // kIm2colPixelsPerWarp pixels per warp step, the 9 taps unrolled
+        // (constant shared offsets)
+        const uint32_t gl = lane % kIm2colLanesPerPixel, sub = lane / kIm2colLanesPerPixel;
+        if (gl < groups) {
             const uint32_t tap_words = c / 4;
-            for (uint32_t p = warp; p < np; p += nwarps) {
+            for (uint32_t p = warp * kIm2colPixelsPerWarp + sub; p < np; p += nwarps * kIm2colPixelsPerWarp) {
                 const float inv = inv_s[p];
-                const float* hp = halo + p * kIm2colPixelWords + 4 * lane;
-                uint32_t* o = reinterpret_cast<uint32_t*>(codes + (row0 + p) * kp + ch0) + lane;
+                const float* hp = halo + p * kIm2colPixelWords + 4 * gl;
+                uint32_t* o = reinterpret_cast<uint32_t*>(codes + (row0 + p) * kp + ch0) + gl;
 #pragma unroll
                 for (uint32_t tap = 0; tap < 9; ++tap, o += tap_words) {
                     const float4 v = *reinterpret_cast<const float4*>(

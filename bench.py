@@ -652,14 +652,18 @@ def main():
         barrier()
         torch.cuda.synchronize()
         clocks.mark_start()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        for _ in range(args.steps):
+        # one event between consecutive steps: the first and last bracket the
+        # timed region, the others show the spread of single steps
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        marks[0].record(stream)
+        for i in range(args.steps):
             flush.zero_()
             device_step()
-        end.record(stream)
+            marks[i + 1].record(stream)
+        start, end = marks[0], marks[-1]
         torch.cuda.synchronize()
         clocks.mark_end()
+        step_ms = sorted(marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps))
         barrier()
         dev_ms = max_over_ranks(start.elapsed_time(end), dist)
         launches1 = ctypes.c_uint64()
@@ -777,6 +781,8 @@ def main():
             "cpu_baseline": cpu,
             "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
             "gpu_launches": int(launches1.value - launches0.value),
+            "step_ms": {"min": round(step_ms[0], 3), "median": round(step_ms[len(step_ms) // 2], 3),
+                        "max": round(step_ms[-1], 3)},
             "effective_tflops": round(value / world * GFLOP_PER_IMAGE / 1e3, 1),
         }
         print(json.dumps(line), flush=True)

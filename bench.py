@@ -423,8 +423,63 @@ def op_microbench(lib, torch, hbm_pk, ops=MICRO_OPS):
         _micro_softmax(lib, torch, gen(2), flush, check, rec)
     if "conv3x3_int8_up2" in ops:
         _micro_conv(lib, torch, gen(3), flush, check, rec)
+    del flush
     torch.cuda.empty_cache()
+    for name, cpu in op_cpu_baseline(torch, [o for o in ops if o in out]).items():
+        out[name].update(cpu)
+        out[name]["vs_cpu"] = round(cpu["cpu_ms"] / out[name]["ms"], 1)
     return out
+
+
+def op_cpu_baseline(torch, ops, reps=3):
+    """The reference's CPU executor for each configuration-2 operation: LibTorch-CPU
+    fp32 (here PyTorch CPU, all host threads), timed as the median of `reps` runs
+    after a warm-up. Where the full shape would take long, on a bounded sample
+    scaled to the full shape (linear in images)."""
+    import torch.nn.functional as F
+
+    threads = os.cpu_count() or 1
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    res = {}
+
+    def timed(fn):
+        fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append((time.perf_counter() - t0) * 1e3)
+        return statistics.median(ts)
+
+    with torch.inference_mode():
+        if "layer_norm" in ops:
+            x = torch.randn((10960, 1024), generator=g)
+            w, b = torch.randn(1024, generator=g), torch.randn(1024, generator=g)
+            res["layer_norm"] = {"cpu_ms": timed(lambda: F.layer_norm(x, (1024,), w, b, 1e-6)),
+                                 "cpu_sample": "full shape"}
+        if "gelu" in ops:
+            x = torch.randn((10960, 4096), generator=g)
+            res["gelu"] = {"cpu_ms": timed(lambda: F.gelu(x)), "cpu_sample": "full shape"}
+        if "softmax" in ops:
+            x = torch.randn((16, 1370, 1370), generator=g)
+            res["softmax"] = {"cpu_ms": 8 * timed(lambda: F.softmax(x * 0.125, dim=-1)),
+                              "cpu_sample": "1 of the 8 images [16,1370,1370], x8"}
+        if "conv3x3_int8_up2" in ops:
+            x = torch.randn((1, 256, 148, 148), generator=g)
+            w = torch.randn((256, 256, 3, 3), generator=g) * 0.02
+            b = torch.randn(256, generator=g)
+            res["conv3x3_int8_up2"] = {
+                "cpu_ms": 8 * timed(lambda: F.interpolate(F.conv2d(x, w, b, padding=1), scale_factor=2,
+                                                          mode="bilinear", align_corners=True)),
+                "cpu_sample": "1 of the 8 images, fp32 conv2d (the CPU executor has no int8 path) + 2x "
+                              "align-corners bilinear, x8"}
+    torch.set_num_threads(prev)
+    for v in res.values():
+        v["cpu_ms"] = round(v["cpu_ms"], 3)
+        v["cpu_threads"] = threads
+    return res
 
 
 def _micro_layer_norm(lib, torch, g, check, rec):

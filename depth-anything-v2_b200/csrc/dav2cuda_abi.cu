@@ -216,6 +216,20 @@ int dav2cuda_bilinear_align_true(float* output, const float* input, uint32_t iw,
     return launch_bilinear_align<float, float>(output, input, iw, ih, ow, oh, channels, as_stream(stream));
 }
 
+int dav2cuda_bilinear_align_nhwc_16(void* output, const void* input, uint32_t batch, uint32_t iw, uint32_t ih,
+                                    uint32_t ow, uint32_t oh, uint32_t channels, uint32_t bf16, void* stream) {
+    REQUIRE(batch && iw && ih && ow && oh && channels, "invalid bilinear dimensions");
+    REQUIRE(!null_any(output, input), "bilinear: null buffer");
+    REQUIRE(reinterpret_cast<uintptr_t>(output) % 16 == 0 && reinterpret_cast<uintptr_t>(input) % 16 == 0,
+            "bilinear: buffers must be 16-byte aligned");
+    if (bf16)
+        return launch_bilinear_nhwc<__nv_bfloat16>(static_cast<__nv_bfloat16*>(output),
+                                                   static_cast<const __nv_bfloat16*>(input), batch, ih, iw, oh, ow,
+                                                   channels, as_stream(stream));
+    return launch_bilinear_nhwc<__half>(static_cast<__half*>(output), static_cast<const __half*>(input), batch, ih,
+                                        iw, oh, ow, channels, as_stream(stream));
+}
+
 int dav2cuda_reduce_minmax(const float* input, float* range, uint64_t count, void* stream) {
     REQUIRE(count != 0, "empty depth reduction");
     REQUIRE(!null_any(input, range), "reduce_minmax: null buffer");

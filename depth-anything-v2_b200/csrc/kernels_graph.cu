@@ -106,7 +106,11 @@ __global__ void fill_tokens_kernel(float* __restrict__ x, const float* __restric
     }
 }
 
-// Align-corners bilinear on channels-last half maps: 8 channels per thread.
+// Align-corners bilinear on channels-last 16-bit maps, 8 channels per thread,
+// in the arithmetic of bilinear_align_true.glsl:27-63: source coordinate
+// (x*(in-1))/(out-1), a*(1-f) + b*f with every product and sum rounded
+// (horizontal first, then vertical), f32 math, the result rounded to the
+// 16-bit type.
 template <typename H>
 __global__ void __launch_bounds__(256) bilinear_nhwc_kernel(H* __restrict__ out, const H* __restrict__ in,
                                                             uint32_t ih, uint32_t iw, uint32_t oh, uint32_t ow,
@@ -124,20 +128,21 @@ __global__ void __launch_bounds__(256) bilinear_nhwc_kernel(H* __restrict__ out,
         const uint32_t x1 = min(x0 + 1, iw - 1);
         xtab[3 * x] = x0 * c;
         xtab[3 * x + 1] = x1 * c;
-        xtab[3 * x + 2] = __float_as_uint(sxf - (float)x0);
+        xtab[3 * x + 2] = __float_as_uint(__fsub_rn(sxf, (float)x0));
     }
     const float syf = oh > 1 ? __fdiv_rn(__fmul_rn((float)y, (float)(ih - 1)), (float)(oh - 1)) : 0.f;
     const uint32_t y0 = (uint32_t)floorf(syf), y1 = min(y0 + 1, ih - 1);
-    const float fy = syf - (float)y0;
+    const float fy = __fsub_rn(syf, (float)y0), gy = __fsub_rn(1.0f, fy);
     const H* r0 = in + ((uint64_t)b * ih + y0) * iw * c;
     const H* r1 = in + ((uint64_t)b * ih + y1) * iw * c;
     H* o = out + ((uint64_t)b * oh + y) * ow * c;
     const uint32_t cc = (threadIdx.x % cv) * 8;
     const uint32_t step = blockDim.x / cv;
     __syncthreads();
+#pragma unroll 2
     for (uint32_t x = threadIdx.x / cv; x < ow; x += step) {
         const uint32_t o0 = xtab[3 * x] + cc, o1 = xtab[3 * x + 1] + cc;
-        const float fx = __uint_as_float(xtab[3 * x + 2]);
+        const float fx = __uint_as_float(xtab[3 * x + 2]), gx = __fsub_rn(1.0f, fx);
         const uint4 a00 = *reinterpret_cast<const uint4*>(r0 + o0);
         const uint4 a01 = *reinterpret_cast<const uint4*>(r0 + o1);
         const uint4 a10 = *reinterpret_cast<const uint4*>(r1 + o0);
@@ -150,9 +155,9 @@ __global__ void __launch_bounds__(256) bilinear_nhwc_kernel(H* __restrict__ out,
         H* r = reinterpret_cast<H*>(&res);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const float top = tof(h00[j]) * (1.f - fx) + tof(h01[j]) * fx;
-            const float bot = tof(h10[j]) * (1.f - fx) + tof(h11[j]) * fx;
-            r[j] = cvt<H>(top * (1.f - fy) + bot * fy);
+            const float top = __fadd_rn(__fmul_rn(tof(h00[j]), gx), __fmul_rn(tof(h01[j]), fx));
+            const float bot = __fadd_rn(__fmul_rn(tof(h10[j]), gx), __fmul_rn(tof(h11[j]), fx));
+            r[j] = cvt<H>(__fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, fy)));
         }
         *reinterpret_cast<uint4*>(o + (uint64_t)x * c + cc) = res;
     }

@@ -36,6 +36,7 @@ DAV2CUDA = {
     "dav2cuda_add": (ctypes.c_int, [vp, vp, vp, u64, vp]),
     "dav2cuda_sigmoid_scale": (ctypes.c_int, [vp, vp, u64, f32, vp]),
     "dav2cuda_bilinear_align_true": (ctypes.c_int, [vp, vp, u32, u32, u32, u32, u32, vp]),
+    "dav2cuda_bilinear_align_nhwc_16": (ctypes.c_int, [vp, vp, u32, u32, u32, u32, u32, u32, u32, vp]),
     "dav2cuda_reduce_minmax": (ctypes.c_int, [vp, vp, u64, vp]),
     "dav2cuda_normalize_relative": (ctypes.c_int, [vp, vp, u64, vp]),
     "dav2cuda_normalize_metric": (ctypes.c_int, [vp, vp, u64, f32, vp]),

@@ -103,6 +103,16 @@ DAV2CUDA_API int dav2cuda_bilinear_align_true(float* output, const float* input,
                                               uint32_t output_width, uint32_t output_height,
                                               uint32_t channels, void* stream);
 
+/* The DPT head's resizes in this executor's layout (src/dpt.cpp:598-605,
+ * 813-820 run bilinear_align_true on planar maps): batch x [H][W][channels]
+ * channels-last 16-bit maps (f16, or bf16 when bf16 != 0), channels a
+ * multiple of 8 (8..2048), 16-byte aligned buffers; the reference's f32
+ * arithmetic, the result rounded to the 16-bit type. */
+DAV2CUDA_API int dav2cuda_bilinear_align_nhwc_16(void* output, const void* input, uint32_t batch,
+                                                 uint32_t input_width, uint32_t input_height,
+                                                 uint32_t output_width, uint32_t output_height,
+                                                 uint32_t channels, uint32_t bf16, void* stream);
+
 /* VulkanOperators::reduce_minmax (src/operators.cpp:2050-2058): writes
  * range[0]=min, range[1]=max over count floats. */
 DAV2CUDA_API int dav2cuda_reduce_minmax(const float* input, float* range, uint64_t count,

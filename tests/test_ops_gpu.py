@@ -118,6 +118,29 @@ def test_bilinear_align_true(cuda, dav2lib, c, ih, iw, oh, ow):
     assert np.array_equal(host(out), want)
 
 
+@pytest.mark.parametrize("bf16", [0, 1])
+@pytest.mark.parametrize("b,c,ih,iw,oh,ow", [(2, 256, 37, 37, 74, 74),   # fusion resize (ViT-L, 37 -> 74)
+                                             (1, 128, 74, 74, 148, 148),
+                                             (3, 64, 19, 21, 37, 45),
+                                             (1, 8, 1, 5, 3, 9),           # one source row
+                                             (1, 2048, 3, 3, 7, 5)])       # widest channel count
+def test_bilinear_nhwc_16_bit_exact(cuda, dav2lib, bf16, b, c, ih, iw, oh, ow):
+    """The graph's channels-last 16-bit resize against the oracle's f32
+    align-corners bilinear of the same 16-bit inputs, rounded to the 16-bit
+    type: bit-exact."""
+    torch = cuda
+    dt = torch.bfloat16 if bf16 else torch.float16
+    x = torch.from_numpy(rng(c + ih).standard_normal((b, ih, iw, c)).astype(np.float32)).to(dt)
+    xd, out = x.cuda(), torch.empty((b, oh, ow, c), dtype=dt, device="cuda")
+    call(dav2lib, "dav2cuda_bilinear_align_nhwc_16", out.data_ptr(), xd.data_ptr(), b, iw, ih, ow, oh, c, bf16, None)
+    finish(cuda, dav2lib)
+    xf = x.float().numpy()
+    for i in range(b):
+        want = oracle.bilinear_align_true(np.ascontiguousarray(xf[i].transpose(2, 0, 1)), ow, oh)
+        want16 = torch.from_numpy(np.ascontiguousarray(want.transpose(1, 2, 0))).to(dt)
+        assert torch.equal(out[i].cpu().view(torch.int16), want16.view(torch.int16))
+
+
 def test_minmax_normalize_kat(cuda, dav2lib):
     # tests/vulkan_smoke.cpp:121-142: {2,3,5,10} -> {0,.125,.375,1} +-1e-6
     d = dev(cuda, np.array([2, 3, 5, 10], np.float32))

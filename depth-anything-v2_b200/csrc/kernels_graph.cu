@@ -110,56 +110,108 @@ __global__ void fill_tokens_kernel(float* __restrict__ x, const float* __restric
 // in the arithmetic of bilinear_align_true.glsl:27-63: source coordinate
 // (x*(in-1))/(out-1), a*(1-f) + b*f with every product and sum rounded
 // (horizontal first, then vertical), f32 math, the result rounded to the
-// 16-bit type.
+// 16-bit type. A block per (image, source row pair k): it writes every output
+// row whose top source row is k (the last pair also the rows on the last
+// source row), so each horizontal lerp of the two source rows is computed
+// once and shared by those rows (about oh/ih of them); the x table (source
+// columns and weight) is computed once per block into shared memory; each
+// thread keeps one 8-channel chunk and strides over the pixels (blockDim is a
+// multiple of the chunk count).
+__device__ __forceinline__ float nhwc_coord(uint32_t o, uint32_t in, uint32_t out) {
+    return out > 1 ? __fdiv_rn(__fmul_rn((float)o, (float)(in - 1)), (float)(out - 1)) : 0.f;
+}
+
+// source row pair of output row y: its top source row, the last source row
+// folded into the last pair (monotone in y)
+__device__ __forceinline__ uint32_t nhwc_row_pair(uint32_t y, uint32_t ih, uint32_t oh, uint32_t pairs) {
+    return min((uint32_t)floorf(nhwc_coord(y, ih, oh)), pairs - 1);
+}
+
+constexpr uint32_t kNhwcRowsMax = 4;  // output rows per pass over a staged pair
+
 template <typename H>
 __global__ void __launch_bounds__(256) bilinear_nhwc_kernel(H* __restrict__ out, const H* __restrict__ in,
                                                             uint32_t ih, uint32_t iw, uint32_t oh, uint32_t ow,
                                                             uint32_t c) {
-    // one block per output row (image b, row y); the row's x table (source
-    // columns and weight) is computed once into shared memory; each thread
-    // keeps one 8-channel chunk and strides over the pixels (blockDim is a
-    // multiple of the chunk count), so the inner loop has no division
     extern __shared__ uint32_t xtab[];  // [ow][3]: x0*c, x1*c, fx bits
     const uint32_t cv = c / 8;
-    const uint32_t y = blockIdx.x % oh, b = blockIdx.x / oh;
+    const uint32_t pairs = ih > 1 ? ih - 1 : 1;
+    const uint32_t k = blockIdx.x % pairs, b = blockIdx.x / pairs;
     for (uint32_t x = threadIdx.x; x < ow; x += blockDim.x) {
-        const float sxf = ow > 1 ? __fdiv_rn(__fmul_rn((float)x, (float)(iw - 1)), (float)(ow - 1)) : 0.f;
+        const float sxf = nhwc_coord(x, iw, ow);
         const uint32_t x0 = (uint32_t)floorf(sxf);
         const uint32_t x1 = min(x0 + 1, iw - 1);
         xtab[3 * x] = x0 * c;
         xtab[3 * x + 1] = x1 * c;
         xtab[3 * x + 2] = __float_as_uint(__fsub_rn(sxf, (float)x0));
     }
-    const float syf = oh > 1 ? __fdiv_rn(__fmul_rn((float)y, (float)(ih - 1)), (float)(oh - 1)) : 0.f;
-    const uint32_t y0 = (uint32_t)floorf(syf), y1 = min(y0 + 1, ih - 1);
-    const float fy = __fsub_rn(syf, (float)y0), gy = __fsub_rn(1.0f, fy);
-    const H* r0 = in + ((uint64_t)b * ih + y0) * iw * c;
-    const H* r1 = in + ((uint64_t)b * ih + y1) * iw * c;
-    H* o = out + ((uint64_t)b * oh + y) * ow * c;
+    // output rows of this pair: [y_lo, y_hi)
+    const uint64_t y_est = (uint64_t)k * (oh - 1) / pairs;  // within a few rows of the first one
+    uint32_t y_lo = (uint32_t)(y_est < oh ? y_est : oh - 1);
+    while (y_lo > 0 && nhwc_row_pair(y_lo - 1, ih, oh, pairs) >= k) --y_lo;
+    while (y_lo < oh && nhwc_row_pair(y_lo, ih, oh, pairs) < k) ++y_lo;
+    uint32_t y_hi = y_lo;
+    while (y_hi < oh && nhwc_row_pair(y_hi, ih, oh, pairs) == k) ++y_hi;
+    const uint32_t r0 = k, r1 = min(k + 1, ih - 1);
+    const H* s0 = in + ((uint64_t)b * ih + r0) * iw * c;
+    const H* s1 = in + ((uint64_t)b * ih + r1) * iw * c;
     const uint32_t cc = (threadIdx.x % cv) * 8;
     const uint32_t step = blockDim.x / cv;
     __syncthreads();
-#pragma unroll 2
-    for (uint32_t x = threadIdx.x / cv; x < ow; x += step) {
-        const uint32_t o0 = xtab[3 * x] + cc, o1 = xtab[3 * x + 1] + cc;
-        const float fx = __uint_as_float(xtab[3 * x + 2]), gx = __fsub_rn(1.0f, fx);
-        const uint4 a00 = *reinterpret_cast<const uint4*>(r0 + o0);
-        const uint4 a01 = *reinterpret_cast<const uint4*>(r0 + o1);
-        const uint4 a10 = *reinterpret_cast<const uint4*>(r1 + o0);
-        const uint4 a11 = *reinterpret_cast<const uint4*>(r1 + o1);
-        const H* h00 = reinterpret_cast<const H*>(&a00);
-        const H* h01 = reinterpret_cast<const H*>(&a01);
-        const H* h10 = reinterpret_cast<const H*>(&a10);
-        const H* h11 = reinterpret_cast<const H*>(&a11);
-        uint4 res;
-        H* r = reinterpret_cast<H*>(&res);
+    for (uint32_t yc = y_lo; yc < y_hi; yc += kNhwcRowsMax) {
+        const uint32_t nr = min(kNhwcRowsMax, y_hi - yc);
+        float fy[kNhwcRowsMax], gy[kNhwcRowsMax];
+        bool top1[kNhwcRowsMax], bot1[kNhwcRowsMax];  // top / bottom source row is r1 (else r0)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float top = __fadd_rn(__fmul_rn(tof(h00[j]), gx), __fmul_rn(tof(h01[j]), fx));
-            const float bot = __fadd_rn(__fmul_rn(tof(h10[j]), gx), __fmul_rn(tof(h11[j]), fx));
-            r[j] = cvt<H>(__fadd_rn(__fmul_rn(top, gy), __fmul_rn(bot, fy)));
+        for (uint32_t j = 0; j < kNhwcRowsMax; ++j) {
+            const float syf = nhwc_coord(yc + j, ih, oh);
+            const uint32_t y0 = (uint32_t)floorf(syf), y1 = min(y0 + 1, ih - 1);
+            fy[j] = __fsub_rn(syf, (float)y0);
+            gy[j] = __fsub_rn(1.0f, fy[j]);
+            top1[j] = y0 != r0;
+            bot1[j] = y1 != r0;
         }
-        *reinterpret_cast<uint4*>(o + (uint64_t)x * c + cc) = res;
+        bool plain = true;  // every row of the pass: top r0, bottom r1
+#pragma unroll
+        for (uint32_t j = 0; j < kNhwcRowsMax; ++j) plain = plain && (j >= nr || (!top1[j] && bot1[j]));
+        H* o = out + ((uint64_t)b * oh + yc) * ow * c;
+        for (uint32_t x = threadIdx.x / cv; x < ow; x += step) {
+            const uint32_t o0 = xtab[3 * x] + cc, o1 = xtab[3 * x + 1] + cc;
+            const float fx = __uint_as_float(xtab[3 * x + 2]), gx = __fsub_rn(1.0f, fx);
+            const uint4 a00 = *reinterpret_cast<const uint4*>(s0 + o0);
+            const uint4 a01 = *reinterpret_cast<const uint4*>(s0 + o1);
+            const uint4 a10 = *reinterpret_cast<const uint4*>(s1 + o0);
+            const uint4 a11 = *reinterpret_cast<const uint4*>(s1 + o1);
+            const H* h00 = reinterpret_cast<const H*>(&a00);
+            const H* h01 = reinterpret_cast<const H*>(&a01);
+            const H* h10 = reinterpret_cast<const H*>(&a10);
+            const H* h11 = reinterpret_cast<const H*>(&a11);
+            float hz0[8], hz1[8];  // horizontal lerps of source rows r0 and r1
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                hz0[j] = __fadd_rn(__fmul_rn(tof(h00[j]), gx), __fmul_rn(tof(h01[j]), fx));
+                hz1[j] = __fadd_rn(__fmul_rn(tof(h10[j]), gx), __fmul_rn(tof(h11[j]), fx));
+            }
+#pragma unroll
+            for (uint32_t r = 0; r < kNhwcRowsMax; ++r) {
+                if (r < nr) {
+                    uint4 res;
+                    H* rr = reinterpret_cast<H*>(&res);
+                    if (plain) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            rr[j] = cvt<H>(__fadd_rn(__fmul_rn(hz0[j], gy[r]), __fmul_rn(hz1[j], fy[r])));
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float top = top1[r] ? hz1[j] : hz0[j], bot = bot1[r] ? hz1[j] : hz0[j];
+                            rr[j] = cvt<H>(__fadd_rn(__fmul_rn(top, gy[r]), __fmul_rn(bot, fy[r])));
+                        }
+                    }
+                    *reinterpret_cast<uint4*>(o + ((uint64_t)r * ow + x) * c + cc) = res;
+                }
+            }
+        }
     }
 }
 
@@ -380,7 +432,9 @@ int launch_bilinear_nhwc(H* out, const H* in, uint32_t batch, uint32_t ih, uint3
     if (cv == 0 || cv > 256) return set_error(DAV2CUDA_INVALID_ARGUMENT, "bilinear_nhwc: channels must be 8..2048");
     const size_t tab = (size_t)ow * 3 * sizeof(uint32_t);
     if (tab > 48 * 1024) return set_error(DAV2CUDA_INVALID_ARGUMENT, "bilinear_nhwc: output row too wide");
-    bilinear_nhwc_kernel<H><<<(unsigned)(batch * oh), (256 / cv) * cv, tab, st>>>(out, in, ih, iw, oh, ow, c);
+    const uint64_t blocks = (uint64_t)batch * (ih > 1 ? ih - 1 : 1);
+    if (blocks > 0x7fffffffull) return set_error(DAV2CUDA_INVALID_ARGUMENT, "bilinear_nhwc: grid too large");
+    bilinear_nhwc_kernel<H><<<(unsigned)blocks, (256 / cv) * cv, tab, st>>>(out, in, ih, iw, oh, ow, c);
     return check_launch("bilinear_nhwc");
 }
 

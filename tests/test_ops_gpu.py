@@ -402,6 +402,44 @@ def test_conv3x3_int8_up2(cuda, dav2lib, B, C, H, W, O):
         assert np.array_equal(got[i], oracle.bilinear_align_true(conv, 2 * W, 2 * H))
 
 
+def test_conv3x3_int8_up2_bench_shape(cuda, dav2lib):
+    """BASELINE configuration 2's full shape [8,256,148,148]: the last image's
+    codes and scales (read back from the workspace) bit-exact against the
+    oracle, and its upsampled output bit-exact against the oracle's order of
+    operations. The conv sums are an exact float64 BLAS product of the integer
+    codes (|acc| < 2^24), dequantized in f32 as (acc*s_in)*s_w + b."""
+    B, C, H, W, O = 8, 256, 148, 148, 256
+    x = rng(11).standard_normal((B, C, H, W)).astype(np.float32)
+    wt = rng(12).uniform(-127, 127, (O, C, 3, 3)).astype(np.float32)
+    b = rng(13).standard_normal(O).astype(np.float32)
+    pw, sw = oracle.pack_weight_s8(wt)
+    ws = dav2lib.dav2cuda_conv3x3_int8_up2_workspace_size(B, W, H, C, O)
+    out, wsb = empty(cuda, (B, O, 2 * H, 2 * W)), empty(cuda, (ws,), np.uint8)
+    call(dav2lib, "dav2cuda_conv3x3_int8_up2", ptr(out), ptr(dev(cuda, x)), ptr(dev(cuda, pw.view(np.int32))),
+         ptr(dev(cuda, sw)), ptr(dev(cuda, b)), B, W, H, C, O, ptr(wsb), ws, None)
+    finish(cuda, dav2lib)
+    i, hw, K = B - 1, H * W, 9 * C
+    kp = (K + 15) // 16 * 16
+    a256 = lambda n: (n + 255) // 256 * 256
+    codes_off = a256(B * hw * 4)
+    scales_off = codes_off + a256(B * hw * kp)
+    got_codes = wsb[codes_off + i * hw * kp: codes_off + (i + 1) * hw * kp].cpu().numpy().view(np.int8)
+    got_scales = wsb[scales_off + i * hw * 4: scales_off + (i + 1) * hw * 4].cpu().numpy().view(np.float32)
+    pk, sc = oracle.im2col_quantize_s8(x[i], 3, 1, 1)
+    codes = pk.view(np.int8).reshape(hw, -1)[:, :K]  # columns (c, ky, kx)
+    assert np.array_equal(got_scales, sc)
+    # the device rows hold the same codes in (ky, kx, c) column order
+    assert np.array_equal(got_codes.reshape(hw, kp)[:, :K].reshape(hw, 9, C),
+                          codes.reshape(hw, C, 9).transpose(0, 2, 1))
+    wc = pw.view(np.int8).reshape(O, -1)[:, :K].astype(np.float64)
+    conv = np.empty((hw, O), np.float32)
+    for r0 in range(0, hw, 4096):
+        acc = codes[r0:r0 + 4096].astype(np.float64) @ wc.T
+        conv[r0:r0 + 4096] = (acc.astype(np.float32) * sc[r0:r0 + 4096, None]) * sw[None, :] + b[None, :]
+    want = oracle.bilinear_align_true(np.ascontiguousarray(conv.T.reshape(O, H, W)), 2 * W, 2 * H)
+    assert np.array_equal(host(out[i]), want)
+
+
 # ------------------------------------------------------------- attention
 def test_attention_reference_kat(cuda, dav2lib):
     # tests/vulkan_smoke.cpp:540-628: 5 tokens, 2 heads; fp16 within 3e-4 of fp32

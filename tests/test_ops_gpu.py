@@ -23,9 +23,10 @@ def rng(seed=0):
 
 # ---------------------------------------------------------------- row ops
 @pytest.mark.parametrize("rows,cols", [(4, 17), (37, 384), (129, 768), (300, 1024), (5, 1000),
-                                       (8200, 1024), (9001, 768)])
+                                       (8200, 1024), (9001, 768), (10960, 1024)])
 def test_layer_norm(cuda, dav2lib, rows, cols):
-    """Row counts from a handful to above the ViT-S batch-6 token count."""
+    """Row counts from a handful to above the ViT-S batch-6 token count, and
+    BASELINE configuration 2's [10960, 1024]."""
     r = rng(rows)
     x = r.standard_normal((rows, cols)).astype(np.float32) * 3 + 0.5
     w = r.standard_normal(cols).astype(np.float32)
@@ -50,7 +51,7 @@ def test_layer_norm_reference_kat(cuda, dav2lib):
     assert np.abs(host(out) - (x - mean) / np.sqrt(var + 1e-6)).max() <= 1e-5
 
 
-@pytest.mark.parametrize("n", [1, 7, 4096, 10960 * 4])
+@pytest.mark.parametrize("n", [1, 7, 4096, 10960 * 4, 10960 * 4096])  # the last: configuration 2's shape
 def test_gelu(cuda, dav2lib, n):
     x = rng(n).standard_normal(n).astype(np.float32) * 4
     out = empty(cuda, (n,))
@@ -61,7 +62,8 @@ def test_gelu(cuda, dav2lib, n):
 
 
 @pytest.mark.parametrize("rows,cols,scale", [(16, 1370, 0.125), (8, 5, 1.0), (3, 3001, 1.0), (2, 4000, 0.125),
-                                              (5, 7, 0.5)])
+                                              (5, 7, 0.5),
+                                              (8 * 16 * 1370, 1370, 0.125)])  # configuration 2's [8,16,1370,1370]
 def test_softmax(cuda, dav2lib, rows, cols, scale):
     x = rng(cols).standard_normal((rows, cols)).astype(np.float32) * 4
     out = empty(cuda, (rows, cols))

@@ -53,6 +53,15 @@ int launch_bilinear_align(TO* out, const TI* in, uint32_t iw, uint32_t ih, uint3
 bool bilinear_nhwc_to_planar_supported(uint32_t iw, uint32_t c, uint32_t ow);
 int launch_bilinear_nhwc_to_planar(float* out, const float* in, uint32_t batch, uint32_t ih, uint32_t iw, uint32_t c,
                                    uint32_t oh, uint32_t ow, cudaStream_t st);
+// The DPT head's output_conv2 (3x3, cp -> 32, + bias, ReLU) and 1x1 32 -> 1
+// head (+ head_b, ReLU or sigmoid * head_max) as one halo-loading tcgen05
+// kernel over channels-last 16-bit maps [batch][h][w][cp] -> f32 [batch][h][w]
+// (destination read from out_slot when set); weight [32][9 * cp] 16-bit,
+// column (ky*3 + kx)*cp + c.
+bool conv_head_halo_supported(uint32_t cp, uint32_t cout);
+int launch_conv_head_halo(float* out, float* const* out_slot, const void* in, const void* weight, const float* bias,
+                          const float* head_w, float head_b, float head_max, bool metric, bool bf16, uint32_t batch,
+                          uint32_t h, uint32_t w, uint32_t cp, cudaStream_t st);
 int launch_minmax(const float* in, float* range, uint64_t n, cudaStream_t st);
 int launch_normalize(float* d, const float* range, uint64_t n, float maximum, cudaStream_t st);
 // Per-image forms over `batch` images of n values each: ranges [batch][2].

@@ -1058,7 +1058,13 @@ private:
             step(st, launch_gemm(g, st), "output_conv1");
         }
         step(st, bilinear16(p.full, p.oc1, B, h1, w1, p.H, p.W, cp_half_, st), "head resize");
-        {
+        if (conv_head_halo_supported(cp_half_, out_conv2_.n)) {
+            const float max_depth = model_.metric_max_depth();
+            step(st,
+                 launch_conv_head_halo(p.depth, p.depth_slot, p.full, out_conv2_.w, out_conv2_.b, head_w_, head_b_,
+                                       max_depth, max_depth > 0, bf16_, B, p.H, p.W, cp_half_, st),
+                 "output_conv2");
+        } else {
             GemmArgs g = conv3x3(out_conv2_, p.full, B, p.H, p.W, cp_half_);
             g.flags |= kEpiHeadDot | (model_.metric_max_depth() > 0 ? kEpiMetricHead : 0u);
             g.head_w = head_w_;

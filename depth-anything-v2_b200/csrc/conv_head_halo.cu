@@ -7,16 +7,16 @@
 // as an N=256 one but does an eighth of the work, so the implicit-GEMM kernel
 // that loads one shifted A tile per tap spends its time waiting on those
 // loads. This kernel loads each input pixel once per tile instead: a tile is
-// 128 consecutive output pixels of one image row, and per 32-channel chunk
-// TMA brings the 3 x 130-pixel halo of the tile into shared memory as four
-// 8-channel planes [row][pixel][8 channels] (16 bytes per pixel: the
-// no-swizzle K-major core-matrix layout). Tap (dy, dx) is then the same
-// planes seen from a base dy*130 + dx pixels further: an operand descriptor
-// with K-direction stride = plane size and M-direction stride = 8 pixels. The
-// weights, packed in the same layout once per CTA, stay in shared memory.
+// 128 consecutive output pixels of one image row, and per 64-channel chunk
+// one TMA box brings the 3 x 130-pixel halo of the tile into shared memory as
+// 128-byte pixel rows [row][pixel][64 channels] with the 128-byte swizzle
+// (the K-major layout the MMA reads). Tap (dy, dx) is then the same rows seen
+// from a base dy*130 + dx pixels further: an operand descriptor whose start is
+// that pixel's row. The weights, packed in the same layout once per CTA, stay
+// in shared memory.
 //
 // Roles (persistent, one CTA per SM): warp 0 TMA (halo planes into a ring of
-// kStages chunk stages), warp 1 the MMA issuer (18 MMAs per chunk, four chunks
+// kStages chunk stages), warp 1 the MMA issuer (36 MMAs per chunk, two chunks
 // per tile at Cp = 128, into one of two 32-column TMEM accumulators), warps
 // 2..5 the head (one TMEM lane quarter each: relu(acc + b) . w + head_b per
 // pixel, written to the depth map). Every wait is bounded; a timeout sets the
@@ -34,17 +34,17 @@ namespace {
 
 constexpr uint32_t kHaloPixels = 130;                    // 128 output pixels + left and right halo
 constexpr uint32_t kHaloRows = 3;
-constexpr uint32_t kPlaneBytes = 6272;                   // 3 x 130 x 16 B = 6240, rounded to 128 B
-constexpr uint32_t kChunkChannels = 32;                  // channels per stage (four 8-channel planes)
-constexpr uint32_t kStageBytes = 4 * kPlaneBytes;
-constexpr uint32_t kStages = 6;
+constexpr uint32_t kChunkChannels = 64;                  // channels per stage: one 128-byte row per pixel
+constexpr uint32_t kHaloBytes = kHaloRows * kHaloPixels * 128;  // 49920 per stage
+constexpr uint32_t kStageBytes = 50176;                  // rounded to 1 KB (the swizzle pattern's period)
+constexpr uint32_t kStages = 3;
 constexpr uint32_t kCout = 32;
 constexpr uint32_t kThreads = 6 * 32;
 constexpr uint32_t kMaxCp = 128;                         // weights resident: 9 x Cp x 32 x 2 B
 constexpr uint32_t kWeightBytes = 9 * kMaxCp * kCout * 2;  // 73728
 constexpr uint32_t kSmem = kWeightBytes + kStages * kStageBytes + 1024 + 1024;  // + barriers + alignment slack
 static_assert(kSmem <= 232448, "shared memory above the per-block limit");
-static_assert(kPlaneBytes % 128 == 0 && kPlaneBytes >= kHaloRows * kHaloPixels * 16, "plane size");
+static_assert(kStageBytes % 1024 == 0 && kStageBytes >= kHaloBytes, "stage size");
 
 struct HeadParams {
     uint32_t batch, h, w, cp;  // input / output maps [batch][h][w][cp] -> [batch][h][w]
@@ -59,12 +59,16 @@ struct HeadParams {
     int* err;
 };
 
-// Shared-memory operand descriptor, K-major, no swizzle: core matrices of
-// 8 rows x 16 bytes, lbo = byte stride between K-adjacent core matrices,
-// sbo = byte stride between 8-row groups (M or N direction).
-__device__ __forceinline__ uint64_t desc_noswizzle(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(lbo >> 4) << 16) |
-           (static_cast<uint64_t>(sbo >> 4) << 32) | (static_cast<uint64_t>(1) << 46);
+// Shared-memory operand descriptor, K-major, 128-byte rows with the 128-byte
+// swizzle (8-row groups 1 KB apart), for an operand that may start at any
+// row of a 1 KB-aligned swizzled region: the MMA undoes the swizzle from the
+// absolute address bits of each row, as TMA applied it, so the start needs no
+// phase correction (base-offset field 0; a start row's phase written there
+// was measured to misplace the rows).
+__device__ __forceinline__ uint64_t desc_sw128_at(uint32_t saddr) {
+    return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+           (static_cast<uint64_t>(2) << 61);
 }
 
 template <bool kBF16>
@@ -74,8 +78,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // 1 KB-aligned working area (the dynamic allocation carries 1 KB of slack)
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint8_t* sW = smem;                          // [tap][8-channel group][32 rows][16 B]
-    uint8_t* sA = smem + kWeightBytes;           // [stage][plane][3 x 130 pixels][16 B]
+    uint8_t* sW = smem;                          // [tap][chunk][32 rows][128 B, swizzled]
+    uint8_t* sA = smem + kWeightBytes;           // [stage][3 x 130 pixels][128 B, swizzled]
     uint64_t* bars = reinterpret_cast<uint64_t*>(sA + kStages * kStageBytes);
     uint64_t* full = bars;                       // [stage]
     uint64_t* empty = full + kStages;            // [stage]
@@ -84,7 +88,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* drain = tempty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    const uint32_t groups = p.cp / 8, chunks = p.cp / kChunkChannels;
+    const uint32_t chunks = p.cp / kChunkChannels;
 
     if (threadIdx.x == 0) {
         tma_prefetch_desc(&tm);
@@ -100,11 +104,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 0;
         fence_barrier_init();
     }
-    // weights into the core-matrix layout: unit (tap, group, row) = 8 channels
-    for (uint32_t u = threadIdx.x; u < 9 * groups * kCout; u += blockDim.x) {
-        const uint32_t row = u % kCout, tg = u / kCout, g = tg % groups, tap = tg / groups;
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.weight + (uint64_t)row * 9 * p.cp + tap * p.cp + g * 8));
-        *reinterpret_cast<uint4*>(sW + (size_t)u * 16) = v;
+    // weights into the swizzled K-major layout: a 4 KB tile per (tap, chunk),
+    // 16-byte unit j of row r at r*128 + ((j ^ (r & 7)) << 4)
+    for (uint32_t u = threadIdx.x; u < 9 * chunks * kCout * 8; u += blockDim.x) {
+        const uint32_t j = u & 7u, row = (u >> 3) % kCout, tc = (u >> 3) / kCout, c = tc % chunks, tap = tc / chunks;
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.weight + (uint64_t)row * 9 * p.cp + tap * p.cp +
+                                                             c * kChunkChannels + j * 8));
+        *reinterpret_cast<uint4*>(sW + (size_t)(tc * kCout + row) * 128 + ((j ^ (row & 7u)) << 4)) = v;
     }
     fence_async_smem();
     if (warp == 1) tmem_alloc(tmem_slot, 64);
@@ -127,11 +133,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[s], 4 * kHaloRows * kHaloPixels * 16);
-#pragma unroll
-                    for (uint32_t q = 0; q < 4; ++q)
-                        tma_load_4d(sA + s * kStageBytes + q * kPlaneBytes, &tm, &full[s],
-                                    (int)(c * kChunkChannels + 8 * q), (int)(xt * 128u) - 1, (int)y - 1, (int)img);
+                    mbar_arrive_expect_tx(&full[s], kHaloBytes);
+                    tma_load_4d(sA + s * kStageBytes, &tm, &full[s], (int)(c * kChunkChannels), (int)(xt * 128u) - 1,
+                                (int)y - 1, (int)img);
                 }
             }
         }
@@ -156,16 +160,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t stage = a0 + s * kStageBytes;
 #pragma unroll
                     for (uint32_t tap = 0; tap < 9; ++tap) {
-                        const uint32_t shift = ((tap / 3) * kHaloPixels + tap % 3) * 16u;
+                        // A: the tap's base pixel row of the stage; B: the (tap, chunk) weight tile
+                        const uint32_t arow = stage + ((tap / 3) * kHaloPixels + tap % 3) * 128u;
+                        const uint32_t brow = w0 + (tap * chunks + c) * (kCout * 128u);
 #pragma unroll
-                        for (uint32_t kk = 0; kk < 2; ++kk) {
-                            // A: planes 2kk, 2kk+1 of the stage, from the tap's base pixel;
-                            // B: groups 4c+2kk, 4c+2kk+1 of the tap's weights
-                            const uint64_t da = desc_noswizzle(stage + 2 * kk * kPlaneBytes + shift, kPlaneBytes, 128);
-                            const uint64_t db =
-                                desc_noswizzle(w0 + (tap * groups + c * 4 + 2 * kk) * (kCout * 16u), kCout * 16u, 128);
-                            umma<false>(tmem + buf * kCout, da, db, idesc, (c | tap | kk) ? 1u : 0u);
-                        }
+                        for (uint32_t kk = 0; kk < 4; ++kk)  // 16 channels per MMA
+                            umma<false>(tmem + buf * kCout, desc_sw128_at(arow + 32u * kk),
+                                        desc_sw128_at(brow + 32u * kk), idesc, (c | tap | kk) ? 1u : 0u);
                     }
                     umma_commit(&empty[s]);
                     mma_issued = true;
@@ -245,7 +246,7 @@ int launch_conv_head_halo(float* out, float* const* out_slot, const void* in, co
                           const float* head_w, float head_b, float head_max, bool metric, bool bf16, uint32_t batch,
                           uint32_t h, uint32_t w, uint32_t cp, cudaStream_t st) {
     if (!conv_head_halo_supported(cp, kCout) || !batch || !h || !w)
-        return set_error(DAV2CUDA_INVALID_ARGUMENT, "conv_head_halo: channels must be a multiple of 32 up to 128");
+        return set_error(DAV2CUDA_INVALID_ARGUMENT, "conv_head_halo: channels must be 64 or 128");
     if (reinterpret_cast<uintptr_t>(in) % 16 || reinterpret_cast<uintptr_t>(weight) % 16 ||
         reinterpret_cast<uintptr_t>(bias) % 16 || reinterpret_cast<uintptr_t>(head_w) % 16)
         return set_error(DAV2CUDA_INVALID_ARGUMENT, "conv_head_halo: buffers must be 16-byte aligned");
@@ -257,16 +258,16 @@ int launch_conv_head_halo(float* out, float* const* out_slot, const void* in, co
             g_head_enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     });
     if (!g_head_enc) return set_error(DAV2CUDA_INTERNAL_ERROR, "cuTensorMapEncodeTiled unavailable");
-    // [batch][h][w][cp] 16-bit, box = 8 channels x 130 pixels x 3 rows x 1 image,
-    // no swizzle: the box lands as [row][pixel][8 channels]
+    // [batch][h][w][cp] 16-bit, box = 64 channels x 130 pixels x 3 rows x 1 image,
+    // 128-byte swizzle: the box lands as [row][pixel][64 channels]
     CUtensorMap tm;
     const cuuint64_t dims[4] = {cp, w, h, batch};
     const cuuint64_t strides[3] = {(cuuint64_t)cp * 2, (cuuint64_t)w * cp * 2, (cuuint64_t)h * w * cp * 2};
-    const cuuint32_t box[4] = {8, kHaloPixels, kHaloRows, 1};
+    const cuuint32_t box[4] = {kChunkChannels, kHaloPixels, kHaloRows, 1};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     if (g_head_enc(&tm, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
                    const_cast<void*>(in), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return set_error(DAV2CUDA_INVALID_ARGUMENT, "conv_head_halo: tensor map encoding failed");
     auto kernel = bf16 ? conv_head_halo_kernel<true> : conv_head_halo_kernel<false>;

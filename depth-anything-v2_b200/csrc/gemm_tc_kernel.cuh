@@ -560,6 +560,24 @@ __device__ __forceinline__ void dequant4(const uint32_t* acc, float si, const fl
     }
 }
 
+// dequant4 with the column parameters already in registers (loaded ahead of
+// the accumulator wait).
+template <bool kInt8, bool BIAS, bool GELU>
+__device__ __forceinline__ void dequant4_pre(const uint32_t* acc, float si, float4 w, float4 b, float* v) {
+    const float ws[4] = {w.x, w.y, w.z, w.w}, bs[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float t = kInt8 ? (float)(int32_t)acc[k] : __uint_as_float(acc[k]);
+        if (kInt8) t = __fmul_rn(__fmul_rn(t, si), ws[k]);
+        if (BIAS) t = __fadd_rn(t, bs[k]);
+        v[k] = t;
+    }
+    if (GELU) {
+        gelu_erf_as2(v[0], v[1]);
+        gelu_erf_as2(v[2], v[3]);
+    }
+}
+
 // One chunk (64 bytes of output per row: 16 f32 or 32 f16 columns):
 // registers -> 64-byte-swizzled staging boxes. Row `lane` is at lane*64; its
 // 16-byte unit u sits at unit u ^ ((lane >> 1) & 3), conflict-free for
@@ -568,7 +586,8 @@ __device__ __forceinline__ void dequant4(const uint32_t* acc, float si, const fl
 // the ReLU copy (RC) on exit.
 template <bool kInt8, bool F32, bool BIAS, bool GELU, bool LS, bool RELU, bool R1, bool R2, bool RC>
 __device__ __forceinline__ void tma_chunk_compute(const GemmParamsDev& p, const uint32_t* acc, float si,
-                                                  uint32_t col0, uint8_t* box, uint8_t* box2, uint32_t lane) {
+                                                  uint32_t col0, uint8_t* box, uint8_t* box2, uint32_t lane,
+                                                  const float4* pre_w = nullptr, const float4* pre_b = nullptr) {
     const bool hb = p.out_bf16 != 0;
     const uint32_t sw = (lane >> 1) & 3u;
 #pragma unroll
@@ -578,7 +597,8 @@ __device__ __forceinline__ void tma_chunk_compute(const GemmParamsDev& p, const 
         if (F32) {
             const uint32_t c = col0 + 4u * u;
             float v[4];
-            dequant4<kInt8, BIAS, GELU>(acc + 4 * u, si, p.s_w, p.bias, c, v);
+            if (pre_w) dequant4_pre<kInt8, BIAS, GELU>(acc + 4 * u, si, pre_w[u], pre_b[u], v);
+            else dequant4<kInt8, BIAS, GELU>(acc + 4 * u, si, p.s_w, p.bias, c, v);
             if (LS) {
                 const float4 gm = ldg4(p.gamma + c);
                 const float4 r = *reinterpret_cast<const float4*>(q);
@@ -702,8 +722,8 @@ __device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const Epi
     uint32_t local = 0;
     for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
         const uint32_t buf = local & 1u;
-        if (!mbar_wait(&tfull[buf], (local >> 1) & 1u, abort_flag, p.err)) break;
-        tc_fence_after();
+        // the row scale is loaded before the accumulator wait (its latency
+        // overlaps the wait)
         const uint32_t m_blk = tile / p.num_n_tiles;
         float si = 0.f;
         if (kInt8) {
@@ -721,10 +741,26 @@ __device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const Epi
             }
             if (valid) si = __ldg(p.s_in + r);
         }
+        if (!mbar_wait(&tfull[buf], (local >> 1) & 1u, abort_flag, p.err)) break;
+        tc_fence_after();
         const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + buf * (uint32_t)BN;
         bool ok = true;
 #pragma unroll 1
         for (uint32_t c = first_c; c < (uint32_t)BN; c += kStride) {
+            // f32 outputs without LayerScale (fc1): this chunk's 16 column scales
+            // and biases are loaded before the TMEM read, so their latency
+            // overlaps it (measured 3% on fc1; the LayerScale programs, which
+            // also hold residuals, keep their loads in place)
+            constexpr bool kPre = F32 && !LS;
+            float4 pre_w[4], pre_b[4];
+            if constexpr (kPre) {
+                const uint32_t col = origin(tile, c).c;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    pre_w[u] = kInt8 ? ldg4(p.s_w + col + 4u * u) : make_float4(1.f, 1.f, 1.f, 1.f);
+                    pre_b[u] = BIAS ? ldg4(p.bias + col + 4u * u) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
             uint32_t acc[CW];
             if constexpr (CW == 32) {
                 tmem_ld_32x32b_x32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(acc));
@@ -783,8 +819,8 @@ __device__ __noinline__ void epilogue_tma_loop(const GemmParamsDev& p, const Epi
                 if (lane == 0) bulk_wait_group_read<1>();
                 __syncwarp();
             }
-            tma_chunk_compute<kInt8, F32, BIAS, GELU, LS, RELU, R1, R2, RC>(p, acc, si, (uint32_t)at.c, box, box2,
-                                                                            lane);
+            tma_chunk_compute<kInt8, F32, BIAS, GELU, LS, RELU, R1, R2, RC>(
+                p, acc, si, (uint32_t)at.c, box, box2, lane, kPre ? pre_w : nullptr, kPre ? pre_b : nullptr);
             fence_async_smem();
             __syncwarp();
             if (lane == 0) {

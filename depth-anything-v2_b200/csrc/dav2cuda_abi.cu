@@ -803,6 +803,16 @@ int dav2cuda_conv3x3_int8_up2(float* output, const float* input, const uint32_t*
     return launch_bilinear_align<float, float>(output, conv, w, h, 2 * w, 2 * h, batch * oc, st);
 }
 
+int dav2cuda_conv3x3_head_16(float* depth, const void* input, const void* weight, const float* bias,
+                             const float* head_weight, float head_bias, float max_depth, uint32_t batch,
+                             uint32_t width, uint32_t height, uint32_t channels, uint32_t bf16, void* stream) {
+    REQUIRE(batch && width && height && channels, "invalid head dimensions");
+    REQUIRE(!null_any(depth, input, weight, bias, head_weight), "conv3x3_head: null buffer");
+    REQUIRE(conv_head_halo_supported(channels, 32), "conv3x3_head: channels must be 64 or 128");
+    return launch_conv_head_halo(depth, nullptr, input, weight, bias, head_weight, head_bias, max_depth,
+                                 max_depth > 0.0f, bf16 != 0, batch, height, width, channels, as_stream(stream));
+}
+
 uint64_t dav2cuda_attention_head64_workspace_size(uint32_t batch, uint32_t tokens, uint32_t heads) {
     const uint64_t e = (uint64_t)heads * 64;
     return align256((uint64_t)batch * tokens * 3 * e * 2) + align256((uint64_t)batch * tokens * e * 2) + 256;

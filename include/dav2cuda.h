@@ -276,6 +276,20 @@ DAV2CUDA_API int dav2cuda_conv3x3_int8_up2(float* output, const float* input,
                                            uint32_t output_channels, void* workspace,
                                            uint64_t workspace_bytes, void* stream);
 
+/* The DPT output head's last layers (src/dpt.cpp:830-854): output_conv2.0
+ * (3x3, pad 1, channels -> 32, + bias), ReLU, output_conv2.2 (1x1, 32 -> 1,
+ * + head_bias), then ReLU (max_depth <= 0: relative depth) or
+ * sigmoid * max_depth (metric), as the executor runs them: channels-last
+ * 16-bit input [batch][H][W][channels] (f16, or bf16 when bf16 != 0),
+ * channels 64 or 128, weight [32][9 * channels] 16-bit with column
+ * (ky*3 + kx)*channels + c, bias and head_weight 32 floats, output depth
+ * [batch][H][W]; 16-byte aligned buffers. */
+DAV2CUDA_API int dav2cuda_conv3x3_head_16(float* depth, const void* input, const void* weight,
+                                          const float* bias, const float* head_weight,
+                                          float head_bias, float max_depth, uint32_t batch,
+                                          uint32_t width, uint32_t height, uint32_t channels,
+                                          uint32_t bf16, void* stream);
+
 /* ------------------------------------------------------------ token ops */
 
 /* VulkanOperators::prepare_tokens (src/operators.h:127-141,

@@ -442,6 +442,41 @@ def test_conv3x3_int8_up2_bench_shape(cuda, dav2lib):
     assert np.array_equal(host(out[i]), want)
 
 
+@pytest.mark.parametrize("bf16,b,c,h,w,max_depth", [(0, 2, 128, 20, 150, 0.0),   # ViT-L head width, ragged tile
+                                                   (1, 2, 128, 9, 300, 0.0),
+                                                   (0, 1, 64, 1, 37, 0.0),      # one row: halo rows are padding
+                                                   (1, 1, 64, 3, 518, 0.0),
+                                                   (0, 1, 128, 5, 128, 20.0)])  # metric head
+def test_conv3x3_head_16(cuda, dav2lib, bf16, b, c, h, w, max_depth):
+    """The output head kernel (3x3 conv to 32 channels, ReLU, 1x1 to one
+    channel, ReLU or sigmoid * max_depth) against a float64 evaluation of the
+    same 16-bit inputs; the kernel accumulates in f32, bound 2e-4 of the
+    largest |depth|."""
+    torch = cuda
+    dt = torch.bfloat16 if bf16 else torch.float16
+    r = rng(c + h + w)
+    x = torch.from_numpy(r.standard_normal((b, h, w, c)).astype(np.float32)).to(dt)
+    wt = torch.from_numpy((r.standard_normal((32, 9 * c)) * 0.03).astype(np.float32)).to(dt)
+    bias = (r.standard_normal(32) * 0.1).astype(np.float32)
+    hw = (r.standard_normal(32) * 0.2).astype(np.float32)
+    hb = 0.05
+    xd, wd = x.cuda(), wt.cuda()
+    out = empty(cuda, (b, h, w))
+    call(dav2lib, "dav2cuda_conv3x3_head_16", ptr(out), xd.data_ptr(), wd.data_ptr(), ptr(dev(cuda, bias)),
+         ptr(dev(cuda, hw)), hb, max_depth, b, w, h, c, bf16, None)
+    finish(cuda, dav2lib)
+    xf = np.pad(x.float().numpy().astype(np.float64), ((0, 0), (1, 1), (1, 1), (0, 0)))
+    wf = wt.float().numpy().astype(np.float64)
+    acc = np.zeros((b, h, w, 32))
+    for t in range(9):
+        ky, kx = divmod(t, 3)
+        acc += xf[:, ky:ky + h, kx:kx + w, :] @ wf[:, t * c:(t + 1) * c].T
+    d = np.maximum(acc + bias, 0.0) @ hw.astype(np.float64) + hb
+    want = max_depth / (1.0 + np.exp(-d)) if max_depth > 0 else np.maximum(d, 0.0)
+    got = host(out)
+    assert np.abs(got - want).max() <= 2e-4 * max(np.abs(want).max(), 1e-6)
+
+
 # ------------------------------------------------------------- attention
 def test_attention_reference_kat(cuda, dav2lib):
     # tests/vulkan_smoke.cpp:540-628: 5 tokens, 2 heads; fp16 within 3e-4 of fp32

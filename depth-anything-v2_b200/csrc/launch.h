@@ -58,6 +58,12 @@ int launch_bilinear_nhwc_to_planar(float* out, const float* in, uint32_t batch, 
 // kernel over channels-last 16-bit maps [batch][h][w][cp] -> f32 [batch][h][w]
 // (destination read from out_slot when set); weight [32][9 * cp] 16-bit,
 // column (ky*3 + kx)*cp + c.
+// 3x3 convolution (pad 1) + bias to 128 channels on channels-last 16-bit maps
+// [batch][h][w][cin] -> [batch][h][w][128] (cin a multiple of 64), as one
+// halo-loading tcgen05 kernel; weight [128][9 * cin], column (ky*3 + kx)*cin + c.
+bool conv3x3_halo_supported(uint32_t cin, uint32_t cout, uint32_t ldo);
+int launch_conv3x3_halo(void* out, const void* in, const void* weight, const float* bias, bool bf16, uint32_t batch,
+                        uint32_t h, uint32_t w, uint32_t cin, cudaStream_t st);
 bool conv_head_halo_supported(uint32_t cp, uint32_t cout);
 int launch_conv_head_halo(float* out, float* const* out_slot, const void* in, const void* weight, const float* bias,
                           const float* head_w, float head_b, float head_max, bool metric, bool bf16, uint32_t batch,

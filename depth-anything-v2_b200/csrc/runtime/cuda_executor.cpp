@@ -1050,7 +1050,10 @@ private:
         }
         // ---- output head (src/dpt.cpp:813-854)
         const uint32_t h1 = 2 * p.lh[0], w1 = 2 * p.lw[0];
-        {
+        if (conv3x3_halo_supported(F, out_conv1_.n, cp_half_)) {
+            step(st, launch_conv3x3_halo(p.oc1, path, out_conv1_.w, out_conv1_.b, bf16_, B, h1, w1, F, st),
+                 "output_conv1");
+        } else {
             GemmArgs g = conv3x3(out_conv1_, path, B, h1, w1, F);
             g.out = p.oc1;
             g.out_kind = kOutHalfRows;

@@ -803,6 +803,15 @@ int dav2cuda_conv3x3_int8_up2(float* output, const float* input, const uint32_t*
     return launch_bilinear_align<float, float>(output, conv, w, h, 2 * w, 2 * h, batch * oc, st);
 }
 
+int dav2cuda_conv3x3_c128_16(void* output, const void* input, const void* weight, const float* bias, uint32_t batch,
+                             uint32_t width, uint32_t height, uint32_t input_channels, uint32_t bf16, void* stream) {
+    REQUIRE(batch && width && height && input_channels, "invalid convolution dimensions");
+    REQUIRE(!null_any(output, input, weight, bias), "conv3x3_c128: null buffer");
+    REQUIRE(conv3x3_halo_supported(input_channels, 128, 128), "conv3x3_c128: input channels must be a multiple of 64");
+    return launch_conv3x3_halo(output, input, weight, bias, bf16 != 0, batch, height, width, input_channels,
+                               as_stream(stream));
+}
+
 int dav2cuda_conv3x3_head_16(float* depth, const void* input, const void* weight, const float* bias,
                              const float* head_weight, float head_bias, float max_depth, uint32_t batch,
                              uint32_t width, uint32_t height, uint32_t channels, uint32_t bf16, void* stream) {

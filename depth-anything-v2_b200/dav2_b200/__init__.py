@@ -58,6 +58,7 @@ DAV2CUDA = {
     "dav2cuda_conv3x3_int8_up2_workspace_size": (u64, [u32, u32, u32, u32, u32]),
     "dav2cuda_conv3x3_int8_up2": (ctypes.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, u64, vp]),
     "dav2cuda_conv3x3_head_16": (ctypes.c_int, [vp, vp, vp, vp, vp, f32, f32, u32, u32, u32, u32, u32, vp]),
+    "dav2cuda_conv3x3_c128_16": (ctypes.c_int, [vp, vp, vp, vp, u32, u32, u32, u32, u32, vp]),
     "dav2cuda_prepare_tokens_workspace_size": (u64, [u32, u32, u32]),
     "dav2cuda_prepare_tokens_half": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, vp, u64, vp]),
     "dav2cuda_prepare_tokens_int8": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, vp, u64, vp]),

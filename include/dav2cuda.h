@@ -276,6 +276,17 @@ DAV2CUDA_API int dav2cuda_conv3x3_int8_up2(float* output, const float* input,
                                            uint32_t output_channels, void* workspace,
                                            uint64_t workspace_bytes, void* stream);
 
+/* VulkanOperators::conv2d (src/operators.cpp:1528-1675) for the DPT head's
+ * output_conv1 shape, as the executor runs it: 3x3, pad 1, + bias, from a
+ * channels-last 16-bit map [batch][H][W][input_channels] (f16, or bf16 when
+ * bf16 != 0; input_channels a multiple of 64) to [batch][H][W][128] 16-bit;
+ * weight [128][9 * input_channels] 16-bit with column (ky*3 + kx)*C + c, bias
+ * 128 floats; 16-byte aligned buffers. */
+DAV2CUDA_API int dav2cuda_conv3x3_c128_16(void* output, const void* input, const void* weight,
+                                          const float* bias, uint32_t batch, uint32_t width,
+                                          uint32_t height, uint32_t input_channels, uint32_t bf16,
+                                          void* stream);
+
 /* The DPT output head's last layers (src/dpt.cpp:830-854): output_conv2.0
  * (3x3, pad 1, channels -> 32, + bias), ReLU, output_conv2.2 (1x1, 32 -> 1,
  * + head_bias), then ReLU (max_depth <= 0: relative depth) or

@@ -477,6 +477,37 @@ def test_conv3x3_head_16(cuda, dav2lib, bf16, b, c, h, w, max_depth):
     assert np.abs(got - want).max() <= 2e-4 * max(np.abs(want).max(), 1e-6)
 
 
+@pytest.mark.parametrize("bf16,b,c,h,w", [(0, 2, 256, 7, 150),    # odd height: the last tile's second row is padding
+                                          (1, 1, 256, 4, 296),
+                                          (0, 1, 64, 1, 37),      # one row
+                                          (1, 2, 128, 6, 128)])
+def test_conv3x3_c128_16(cuda, dav2lib, bf16, b, c, h, w):
+    """output_conv1's kernel (3x3 to 128 channels + bias, 16-bit channels-last)
+    against a float64 evaluation of the same 16-bit inputs, compared after
+    rounding the reference to the 16-bit type: within one 16-bit step plus the
+    f32 accumulation error (bound 8e-3 of the largest |output|)."""
+    torch = cuda
+    dt = torch.bfloat16 if bf16 else torch.float16
+    r = rng(c + h + w + 1)
+    x = torch.from_numpy(r.standard_normal((b, h, w, c)).astype(np.float32)).to(dt)
+    wt = torch.from_numpy((r.standard_normal((128, 9 * c)) * 0.03).astype(np.float32)).to(dt)
+    bias = (r.standard_normal(128) * 0.1).astype(np.float32)
+    xd, wd = x.cuda(), wt.cuda()
+    out = torch.empty((b, h, w, 128), dtype=dt, device="cuda")
+    call(dav2lib, "dav2cuda_conv3x3_c128_16", out.data_ptr(), xd.data_ptr(), wd.data_ptr(), ptr(dev(cuda, bias)),
+         b, w, h, c, bf16, None)
+    finish(cuda, dav2lib)
+    xf = np.pad(x.float().numpy().astype(np.float64), ((0, 0), (1, 1), (1, 1), (0, 0)))
+    wf = wt.float().numpy().astype(np.float64)
+    acc = np.zeros((b, h, w, 128))
+    for t in range(9):
+        ky, kx = divmod(t, 3)
+        acc += xf[:, ky:ky + h, kx:kx + w, :] @ wf[:, t * c:(t + 1) * c].T
+    want = acc + bias
+    got = out.float().cpu().numpy().astype(np.float64)
+    assert np.abs(got - want).max() <= 8e-3 * np.abs(want).max()
+
+
 # ------------------------------------------------------------- attention
 def test_attention_reference_kat(cuda, dav2lib):
     # tests/vulkan_smoke.cpp:540-628: 5 tokens, 2 heads; fp16 within 3e-4 of fp32

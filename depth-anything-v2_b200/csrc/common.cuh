@@ -340,24 +340,45 @@ __device__ __forceinline__ float gelu_erf_as(float v) {
     return 0.5f * v * (1.0f + copysignf(e, v));
 }
 
-// gelu_erf_as on a pair, its fp32 multiply-adds issued as f32x2 (the same
-// operations and roundings per value, about half the instructions).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// The same A&S 7.1.26 GELU on a pair, rearranged for fewer instructions:
+// gelu(v) = max(v, 0) - |v|/2 * erfc(|v|/sqrt2), and with t = 1/(1 + p|v|/sqrt2),
+// erfc = t(a1 + ... + t^4 a5) e^{-v^2/2}; the -1/2 goes into the coefficients
+// (b_i = -a_i/2, exact) and e^{-v^2/2} = 2^{c v^2}, c = -log2(e)/2, so
+//   gelu(v) = |v| * t(b1 + t(b2 + t(b3 + t(b4 + t b5)))) * 2^{c v^2} + max(v, 0).
+// The negative branch has no cancellation (the result is the product term
+// alone). Multiply-adds are issued as f32x2; reciprocal and exponential are
+// the hardware approximations (relative error near 2^-22).
 __device__ __forceinline__ void gelu_erf_as2(float& v0, float& v1) {
-    float z0, z1, d0, d1, p0, p1, q0, q1, e0, e1, h0, h1;
-    f2_mul(z0, z1, fabsf(v0), fabsf(v1), 0.70710678118654752f, 0.70710678118654752f);
-    f2_fma(d0, d1, 0.3275911f, 0.3275911f, z0, z1, 1.0f, 1.0f);
-    const float t0 = __fdividef(1.0f, d0), t1 = __fdividef(1.0f, d1);
-    f2_fma(p0, p1, t0, t1, 1.061405429f, 1.061405429f, -1.453152027f, -1.453152027f);
-    f2_fma(p0, p1, t0, t1, p0, p1, 1.421413741f, 1.421413741f);
-    f2_fma(p0, p1, t0, t1, p0, p1, -0.284496736f, -0.284496736f);
-    f2_fma(p0, p1, t0, t1, p0, p1, 0.254829592f, 0.254829592f);
-    f2_mul(p0, p1, t0, t1, p0, p1);
-    f2_mul(q0, q1, -z0, -z1, z0, z1);
-    const float x0 = __expf(q0), x1 = __expf(q1);
-    f2_fma(e0, e1, -p0, -p1, x0, x1, 1.0f, 1.0f);
-    f2_add(e0, e1, 1.0f, 1.0f, copysignf(e0, v0), copysignf(e1, v1));
-    f2_mul(h0, h1, 0.5f, 0.5f, v0, v1);
-    f2_mul(v0, v1, h0, h1, e0, e1);
+    constexpr float kP = 0.3275911f * 0.70710678118654752f;
+    constexpr float kC = -0.72134752044448170f;
+    constexpr float b1 = -0.5f * 0.254829592f, b2 = -0.5f * -0.284496736f, b3 = -0.5f * 1.421413741f,
+                    b4 = -0.5f * -1.453152027f, b5 = -0.5f * 1.061405429f;
+    const float a0 = fabsf(v0), a1 = fabsf(v1);
+    float d0, d1, q0, q1, w0, w1;
+    f2_fma(d0, d1, a0, a1, kP, kP, 1.0f, 1.0f);
+    const float t0 = rcp_approx(d0), t1 = rcp_approx(d1);
+    f2_mul(w0, w1, v0, v1, kC, kC);
+    f2_fma(q0, q1, t0, t1, b5, b5, b4, b4);
+    f2_mul(w0, w1, w0, w1, v0, v1);
+    f2_fma(q0, q1, t0, t1, q0, q1, b3, b3);
+    f2_fma(q0, q1, t0, t1, q0, q1, b2, b2);
+    const float e0 = ex2_approx(w0), e1 = ex2_approx(w1);
+    f2_fma(q0, q1, t0, t1, q0, q1, b1, b1);
+    f2_mul(q0, q1, t0, t1, q0, q1);
+    f2_mul(q0, q1, q0, q1, e0, e1);
+    f2_fma(v0, v1, q0, q1, a0, a1, fmaxf(v0, 0.0f), fmaxf(v1, 0.0f));
 }
 
 // Four bytes q8(x[k] / scale) (IEEE quotient) packed little-endian, for a

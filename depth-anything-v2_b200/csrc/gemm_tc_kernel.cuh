@@ -538,13 +538,25 @@ constexpr uint32_t kStageBufBytes = 2048;  // one 32-row box of 64-byte rows (32
 
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 
+// Four accumulator columns to values, the column parameters already in
+// registers (loaded ahead of the accumulator wait).
 template <bool kInt8, bool BIAS, bool GELU>
-__device__ __forceinline__ void dequant4(const uint32_t* acc, float si, const float* s_w, const float* bias,
-                                         uint32_t c, float* v) {
-    float4 w = make_float4(1.f, 1.f, 1.f, 1.f), b = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (kInt8) w = ldg4(s_w + c);
-    if (BIAS) b = ldg4(bias + c);
+__device__ __forceinline__ void dequant4_pre(const uint32_t* acc, float si, float4 w, float4 b, float* v) {
     const float ws[4] = {w.x, w.y, w.z, w.w}, bs[4] = {b.x, b.y, b.z, b.w};
+    if (kInt8 && GELU) {
+        // followed by GELU, whose result is an approximation anyway: one fused
+        // multiply-add acc * (s_in * s_w) + b per value, issued as f32x2
+        float s[4];
+        f2_mul(s[0], s[1], si, si, ws[0], ws[1]);
+        f2_mul(s[2], s[3], si, si, ws[2], ws[3]);
+#pragma unroll
+        for (int k = 0; k < 4; k += 2)
+            f2_fma(v[k], v[k + 1], (float)(int32_t)acc[k], (float)(int32_t)acc[k + 1], s[k], s[k + 1],
+                   BIAS ? bs[k] : 0.0f, BIAS ? bs[k + 1] : 0.0f);
+        gelu_erf_as2(v[0], v[1]);
+        gelu_erf_as2(v[2], v[3]);
+        return;
+    }
     // (acc * s_in) * s_w + b with the reference's separate roundings (scalar:
     // bit-exact with the oracle), then GELU on pairs of columns
 #pragma unroll
@@ -560,22 +572,14 @@ __device__ __forceinline__ void dequant4(const uint32_t* acc, float si, const fl
     }
 }
 
-// dequant4 with the column parameters already in registers (loaded ahead of
-// the accumulator wait).
+// dequant4_pre with the column parameters loaded here.
 template <bool kInt8, bool BIAS, bool GELU>
-__device__ __forceinline__ void dequant4_pre(const uint32_t* acc, float si, float4 w, float4 b, float* v) {
-    const float ws[4] = {w.x, w.y, w.z, w.w}, bs[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        float t = kInt8 ? (float)(int32_t)acc[k] : __uint_as_float(acc[k]);
-        if (kInt8) t = __fmul_rn(__fmul_rn(t, si), ws[k]);
-        if (BIAS) t = __fadd_rn(t, bs[k]);
-        v[k] = t;
-    }
-    if (GELU) {
-        gelu_erf_as2(v[0], v[1]);
-        gelu_erf_as2(v[2], v[3]);
-    }
+__device__ __forceinline__ void dequant4(const uint32_t* acc, float si, const float* s_w, const float* bias,
+                                         uint32_t c, float* v) {
+    float4 w = make_float4(1.f, 1.f, 1.f, 1.f), b = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (kInt8) w = ldg4(s_w + c);
+    if (BIAS) b = ldg4(bias + c);
+    dequant4_pre<kInt8, BIAS, GELU>(acc, si, w, b, v);
 }
 
 // One chunk (64 bytes of output per row: 16 f32 or 32 f16 columns):

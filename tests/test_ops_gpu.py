@@ -23,10 +23,11 @@ def rng(seed=0):
 
 # ---------------------------------------------------------------- row ops
 @pytest.mark.parametrize("rows,cols", [(4, 17), (37, 384), (129, 768), (300, 1024), (5, 1000),
-                                       (8200, 1024), (9001, 768), (10960, 1024)])
+                                       (8200, 1024), (9001, 768), (10960, 1024), (1, 1024), (7, 1024),
+                                       (301, 1024)])
 def test_layer_norm(cuda, dav2lib, rows, cols):
     """Row counts from a handful to above the ViT-S batch-6 token count, and
-    BASELINE configuration 2's [10960, 1024]."""
+    BASELINE configuration 2's [10960, 1024]; odd row counts at ViT-L's width."""
     r = rng(rows)
     x = r.standard_normal((rows, cols)).astype(np.float32) * 3 + 0.5
     w = r.standard_normal(cols).astype(np.float32)

@@ -19,6 +19,7 @@ Contents:
 from __future__ import annotations
 
 import ctypes
+import os
 import subprocess
 import sys
 from pathlib import Path
@@ -76,4 +77,8 @@ def main(reference: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    # the reference checkout: the first argument, else DAV2_REFERENCE_DIR
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DAV2_REFERENCE_DIR", "")
+    if not ref:
+        sys.exit(f"usage: python {Path(__file__).name} <reference checkout> (or set DAV2_REFERENCE_DIR)")
+    main(ref)

@@ -394,6 +394,55 @@ int dav2cuda_linear_int8(float* output, const float* input, const uint32_t* int8
     return launch_gemm(g, st);
 }
 
+// The encoder's int8 residual update in the form the executor runs it for
+// proj and fc2: rows quantized into the workspace, then one GEMM whose
+// epilogue reads each residual row, adds (dequant + bias) * layer_scale in the
+// reference's order and writes the row back in place.
+int dav2cuda_linear_int8_residual(float* residual, const float* input, const uint32_t* int8_weight,
+                                  const float* weight_scales, const float* bias, const float* layer_scale,
+                                  uint32_t rows, uint32_t input_columns, uint32_t output_columns, void* workspace,
+                                  uint64_t workspace_bytes, void* stream) {
+    REQUIRE(rows && input_columns && output_columns && input_columns % 4 == 0, "invalid INT8 residual dimensions");
+    REQUIRE(input_columns <= 0xFFFFFFF0u, "INT8 residual: input_columns too large");
+    REQUIRE(!null_any(residual, input, int8_weight, weight_scales, bias, layer_scale, workspace),
+            "INT8 residual: null buffer");
+    REQUIRE(workspace_bytes >= dav2cuda_linear_int8_workspace_size(rows, input_columns, output_columns),
+            "INT8 residual: workspace is too small");
+    cudaStream_t st = as_stream(stream);
+    const uint32_t kp = round_up(input_columns, 16);
+    Carve ws(workspace, workspace_bytes);
+    uint32_t* codes = ws.take<uint32_t>((uint64_t)rows * kp);
+    float* scales = ws.take<float>((uint64_t)rows * 4);
+    const uint32_t* w = int8_weight;
+    if (kp != input_columns) {
+        uint8_t* wp = ws.take<uint8_t>((uint64_t)output_columns * kp);
+        if (int rc = pad_byte_rows(wp, int8_weight, output_columns, input_columns, kp, st)) return rc;
+        w = reinterpret_cast<const uint32_t*>(wp);
+    }
+    if (int rc = launch_quantize_rows<float>(codes, scales, input, rows, input_columns, 0, rows,
+                                             (uint64_t)rows * input_columns, input_columns, kp / 4, st))
+        return rc;
+    GemmArgs g;
+    g.elem = kElemS8;
+    g.a = codes;
+    g.lda = kp;
+    g.b = w;
+    g.ldb = kp;
+    g.m = rows;
+    g.n = output_columns;
+    g.k = kp;
+    g.flags = kEpiDequant | kEpiBias | kEpiLayerScale;
+    g.s_in = scales;
+    g.s_w = weight_scales;
+    g.bias = bias;
+    g.gamma = layer_scale;
+    g.res1 = residual;
+    g.out = residual;
+    g.out_kind = kOutF32Rows;
+    g.ldo = output_columns;
+    return launch_gemm(g, st);
+}
+
 uint64_t dav2cuda_conv2d_int8_workspace_size(uint32_t iw, uint32_t ih, uint32_t ic, uint32_t oc, uint32_t k,
                                              uint32_t s, uint32_t p) {
     if (!iw || !ih || !k || !s || iw + 2 * p < k || ih + 2 * p < k) return 0;

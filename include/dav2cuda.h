@@ -221,6 +221,21 @@ DAV2CUDA_API int dav2cuda_linear_int8(float* output, const float* input, const u
                                       uint32_t input_columns, uint32_t output_columns, uint32_t gelu,
                                       void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* The encoder block's int8 residual update, src/encoder.cpp:478-489 (proj,
+ * ls1) and 561-572 (fc2, ls2): VulkanOperators::linear_int8
+ * (src/operators.cpp:770-845, reached through DinoEncoder::linear at
+ * src/encoder.cpp:292 in int8 mode) into a temporary, then add_scaled
+ * (src/operators.cpp:1072-1096) into the residual stream, done here as one
+ * GEMM whose epilogue updates the stream in place:
+ *   residual[r][c] = residual[r][c] + ((acc * s_in[r]) * s_w[c] + bias[c]) * layer_scale[c]
+ * with the reference's separate roundings. Workspace: the size
+ * dav2cuda_linear_int8_workspace_size() returns for the same shape. */
+DAV2CUDA_API int dav2cuda_linear_int8_residual(float* residual, const float* input, const uint32_t* int8_weight,
+                                               const float* weight_scales, const float* bias,
+                                               const float* layer_scale, uint32_t rows, uint32_t input_columns,
+                                               uint32_t output_columns, void* workspace, uint64_t workspace_bytes,
+                                               void* stream);
+
 /* dav2cuda_linear_int8 for callers that may not allocate device memory —
  * host applications that own the device heap (video pipelines, game
  * engines, inference servers that reserve memory at start-up and treat a

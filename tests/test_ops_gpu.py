@@ -311,6 +311,28 @@ def test_linear_int8(cuda, dav2lib, rows, k, n, gelu):
         assert np.array_equal(host(out), want)
 
 
+@pytest.mark.parametrize("rows,k,n", [(1370, 1024, 1024), (300, 4096, 1024), (129, 384, 384), (64, 20, 9),
+                                      (77, 128, 48)])
+def test_linear_int8_residual_bit_exact(cuda, dav2lib, rows, k, n):
+    """The encoder's fused int8 residual update (proj: K = D; fc2: K = 4D, which
+    runs the 8-warp epilogue; narrow and unaligned outputs take the generic row
+    program; K = 20 pads the weight rows) against the oracle's linear_s8 then
+    add_scaled, bit for bit."""
+    x, _, b, px, sx, pw, sw = _s8_problem(rows * 7 + k, rows, k, n)
+    r = rng(rows + n)
+    res = r.standard_normal((rows, n)).astype(np.float32)
+    gamma = (r.standard_normal(n) * 0.1).astype(np.float32)
+    ws = dav2lib.dav2cuda_linear_int8_workspace_size(rows, k, n)
+    wsb = empty(cuda, (ws,), np.uint8)
+    dres = dev(cuda, res)
+    call(dav2lib, "dav2cuda_linear_int8_residual", ptr(dres), ptr(dev(cuda, x)), ptr(dev(cuda, pw.view(np.int32))),
+         ptr(dev(cuda, sw)), ptr(dev(cuda, b)), ptr(dev(cuda, gamma)), rows, k, n, ptr(wsb), ws, None)
+    finish(cuda, dav2lib)
+    lin = oracle.linear_s8(px, pw, sx, sw, b, rows, k, n).reshape(rows, n)
+    want = oracle.add_scaled(res, lin, gamma)
+    assert np.array_equal(host(dres), want)
+
+
 def test_conv2d_int8_reference_kat(cuda, dav2lib):
     # tests/vulkan_smoke.cpp:143-186: int8 conv 3x3 pad 1 within 0.006 of fp32 conv
     W, H, C, O, K = 5, 4, 4, 5, 3

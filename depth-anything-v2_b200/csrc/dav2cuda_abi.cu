@@ -443,6 +443,24 @@ int dav2cuda_linear_int8_residual(float* residual, const float* input, const uin
     return launch_gemm(g, st);
 }
 
+// The graph's channels-last im2col-quantize (f32 maps): one block per output
+// pixel, columns in (ky, kx, c) order, row_bytes apart, zero past k*k*c.
+int dav2cuda_im2col_quantize_nhwc(uint8_t* codes, float* scales, const float* input, uint32_t batch,
+                                  uint32_t height, uint32_t width, uint32_t channels, uint32_t kernel,
+                                  uint32_t stride, uint32_t padding, uint32_t row_bytes, void* stream) {
+    REQUIRE(batch && height && width && channels && kernel && stride && (uint64_t)height + 2ull * padding >= kernel &&
+                (uint64_t)width + 2ull * padding >= kernel,
+            "invalid channels-last im2col dimensions");
+    const uint64_t cols = (uint64_t)kernel * kernel * channels;
+    REQUIRE(cols < 0x80000000ull, "channels-last im2col: kernel*kernel*channels too large");
+    REQUIRE(row_bytes >= cols, "channels-last im2col: row_bytes below kernel*kernel*channels");
+    REQUIRE(!null_any(codes, scales, input), "channels-last im2col: null buffer");
+    const uint32_t oh = (height + 2 * padding - kernel) / stride + 1, ow = (width + 2 * padding - kernel) / stride + 1;
+    REQUIRE((uint64_t)batch * oh * ow <= 0x7FFFFFFFull, "channels-last im2col: too many output pixels");
+    return launch_im2col_quantize_nhwc<float>(codes, scales, input, batch, height, width, channels, channels, kernel,
+                                              stride, padding, oh, ow, row_bytes, as_stream(stream));
+}
+
 uint64_t dav2cuda_conv2d_int8_workspace_size(uint32_t iw, uint32_t ih, uint32_t ic, uint32_t oc, uint32_t k,
                                              uint32_t s, uint32_t p) {
     if (!iw || !ih || !k || !s || iw + 2 * p < k || ih + 2 * p < k) return 0;

@@ -52,6 +52,7 @@ DAV2CUDA = {
     "dav2cuda_conv_transpose_int8_workspace_size": (u64, [u32, u32, u32, u32, u32]),
     "dav2cuda_linear_int8": (ctypes.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, vp, u64, vp]),
     "dav2cuda_linear_int8_residual": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, u32, u32, u32, vp, u64, vp]),
+    "dav2cuda_im2col_quantize_nhwc": (ctypes.c_int, [vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, u32, vp]),
     "dav2cuda_linear_int8_noalloc_scratch_limit": (u64, []),
     "dav2cuda_linear_int8_noalloc": (ctypes.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, vp]),
     "dav2cuda_conv2d_int8": (ctypes.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, u32, vp, u64, vp]),

@@ -176,6 +176,18 @@ DAV2CUDA_API int dav2cuda_pack_weight_s8(uint8_t* codes, float* scales, const fl
                                          uint32_t output_channels, uint32_t kernel, uint32_t input_channels,
                                          void* stream);
 
+/* The same im2col-quantize (im2col_quantize_int8.glsl, src/operators.cpp:
+ * 1787-1801) on a channels-last f32 map [batch][H][W][C], as the executor
+ * runs it for the resize-3 convolution and the conv-transpose inputs: one
+ * row of row_bytes bytes per output pixel, columns in (ky, kx, c) order —
+ * the reference's (c, ky, kx) order permuted, with the weight columns
+ * permuted alike, which leaves every row scale and code unchanged — and zero
+ * bytes past kernel*kernel*C. Row scale = max(absmax/127, 1e-8). */
+DAV2CUDA_API int dav2cuda_im2col_quantize_nhwc(uint8_t* codes, float* scales, const float* input, uint32_t batch,
+                                               uint32_t height, uint32_t width, uint32_t channels,
+                                               uint32_t kernel, uint32_t stride, uint32_t padding,
+                                               uint32_t row_bytes, void* stream);
+
 /* im2col_quantize_int8.glsl dispatch (src/operators.cpp:1787-1801) on a
  * planar [C,H,W] input: rows = output pixels, padded to ceil(C*k*k/4) words
  * (the reference layout). */

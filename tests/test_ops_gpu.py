@@ -255,6 +255,34 @@ def test_im2col_quantize_bit_exact(cuda, dav2lib, c, h, w, k, s, p):
     assert np.array_equal(host(pk, np.uint32), want_pk)
 
 
+@pytest.mark.parametrize("b,c,h,w,k,s,p", [(2, 64, 9, 7, 3, 2, 1), (1, 1024, 37, 37, 3, 2, 1), (2, 12, 5, 6, 3, 1, 1),
+                                           (3, 256, 37, 37, 1, 1, 0), (1, 8, 1, 1, 3, 1, 1)])
+def test_im2col_quantize_nhwc_bit_exact(cuda, dav2lib, b, c, h, w, k, s, p):
+    """The graph's channels-last im2col-quantize (ViT-L's resize-3 convolution:
+    1024 channels 3x3 stride 2 on 37x37; the conv-transpose inputs: 1x1 rows;
+    a channel count off the 8-channel vector path; a one-pixel map) against the
+    oracle's planar im2col of each image: equal row scales, and equal codes once
+    the reference's (c, ky, kx) columns are put in (ky, kx, c) order; the row
+    padding is zero."""
+    x = rng(b * c + h).standard_normal((b, c, h, w)).astype(np.float32)
+    ow, oh = (w + 2 * p - k) // s + 1, (h + 2 * p - k) // s + 1
+    cols = c * k * k
+    row_bytes = (cols + 15) // 16 * 16
+    codes, sc = empty(cuda, (b * oh * ow, row_bytes), np.uint8), empty(cuda, (b * oh * ow,))
+    nhwc = np.ascontiguousarray(x.transpose(0, 2, 3, 1))
+    call(dav2lib, "dav2cuda_im2col_quantize_nhwc", ptr(codes), ptr(sc), ptr(dev(cuda, nhwc)), b, h, w, c, k, s, p,
+         row_bytes, None)
+    finish(cuda, dav2lib)
+    got = host(codes, np.uint8).reshape(b, oh * ow, row_bytes)
+    got_sc = host(sc).reshape(b, oh * ow)
+    for i in range(b):
+        want_pk, want_sc = oracle.im2col_quantize_s8(x[i], k, s, p)
+        want = want_pk.view(np.uint8)[:, :cols].reshape(oh * ow, c, k, k).transpose(0, 2, 3, 1).reshape(oh * ow, cols)
+        assert np.array_equal(got_sc[i], want_sc)
+        assert np.array_equal(got[i, :, :cols], want)
+        assert not got[i, :, cols:].any()
+
+
 def _s8_problem(seed, rows, k, n):
     r = rng(seed)
     x = r.standard_normal((rows, k)).astype(np.float32)

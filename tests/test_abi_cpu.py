@@ -39,6 +39,28 @@ def test_validation_without_gpu(dav2lib):
     assert dav2lib.dav2cuda_attention_head64_workspace_size(1, 1370, 16) >= 1370 * 1024 * 2 * 4
 
 
+def test_validation_of_graph_form_entries(dav2lib):
+    # the operator forms of the executor's fused kernels reject bad shapes and
+    # buffers before any launch (null pointers only: nothing can be touched)
+    f = dav2lib.dav2cuda_linear_int8_residual
+    assert f(None, None, None, None, None, None, 0, 1024, 1024, None, 0, None) == 1
+    assert b"invalid INT8 residual dimensions" in dav2lib.dav2cuda_last_error()
+    assert f(None, None, None, None, None, None, 4, 0xFFFFFFF4, 8, None, 0, None) == 1
+    assert b"too large" in dav2lib.dav2cuda_last_error()
+    assert f(None, None, None, None, None, None, 4, 1024, 1024, None, 1 << 20, None) == 1
+    assert b"null buffer" in dav2lib.dav2cuda_last_error()
+    g = dav2lib.dav2cuda_im2col_quantize_nhwc
+    assert g(None, None, None, 1, 4, 4, 8, 0, 1, 0, 16, None) == 1
+    assert b"invalid channels-last im2col dimensions" in dav2lib.dav2cuda_last_error()
+    assert g(None, None, None, 1, 2, 2, 8, 5, 1, 1, 256, None) == 1  # 5x5 kernel on a 2x2 map, pad 1
+    assert g(None, None, None, 1, 4, 4, 8, 3, 1, 1, 71, None) == 1  # 72 columns need 72 bytes
+    assert b"row_bytes below" in dav2lib.dav2cuda_last_error()
+    assert g(None, None, None, 1, 64, 64, 1 << 28, 3, 1, 1, 0xFFFFFFFF, None) == 1
+    assert b"too large" in dav2lib.dav2cuda_last_error()
+    assert g(None, None, None, 1, 4, 4, 8, 3, 1, 1, 80, None) == 1
+    assert b"null buffer" in dav2lib.dav2cuda_last_error()
+
+
 def test_oracle_library_builds():
     import oracle
 
